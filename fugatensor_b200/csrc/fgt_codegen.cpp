@@ -1,0 +1,1094 @@
+// fgt_codegen.cpp — specialising the kernel templates for one partition.
+//
+// Each kernel family (ELEM / ROW / COLFIN / FULLFIN, see fgt_plan.h) is a
+// fixed loop skeleton written here; per partition only the element functor
+// (straight-line code for one element), the index arithmetic and the
+// reduction set are generated. Values are placed in the outermost scope
+// where they are computable: kernel constants once per CTA, row statistics
+// once per row, column operands (gamma, beta) once per CTA in registers,
+// element values per lane. Streamed operands are loaded with 128-bit vector
+// loads once per row and stay in registers across the row's phases.
+//
+// Arithmetic follows the reference's owned kernels: IEEE f32 with no FMA
+// contraction (src/fugatensor/_ask/gpu.py:189), f16/bf16 computed in f32 and
+// rounded once per operation, exp/log/tanh/erf through CUDA's f32 math
+// library (the reference links libdevice, src/fugatensor/_ask/cuda.py:215-229).
+#include <cstring>
+#include <sstream>
+
+#include "fgt_plan.h"
+
+namespace fgt {
+
+namespace {
+
+std::string st_t(int dt) {
+  switch (dt) {
+    case FGT_BOOL: return "fgt_u8";
+    case FGT_I32: return "int";
+    case FGT_I64: return "fgt_i64";
+    case FGT_F32: return "float";
+    default: return "fgt_u16";
+  }
+}
+std::string vt_t(int dt) {
+  switch (dt) {
+    case FGT_BOOL: return "bool";
+    case FGT_I32: return "int";
+    case FGT_I64: return "fgt_i64";
+    default: return "float";
+  }
+}
+std::string ut_t(int dt) { return dt == FGT_I64 ? "fgt_u64" : "fgt_u32"; }
+std::string min_lit(int dt) { return dt == FGT_I64 ? "(-9223372036854775807LL-1LL)" : "(-2147483647-1)"; }
+std::string max_lit(int dt) { return dt == FGT_I64 ? "9223372036854775807LL" : "2147483647"; }
+int bits_of(int dt) { return dt == FGT_I64 ? 64 : 32; }
+
+std::string ld_conv(int dt, const std::string& x) {
+  switch (dt) {
+    case FGT_F16: return "fgt_f16_to_f32(" + x + ")";
+    case FGT_BF16: return "fgt_bf16_to_f32(" + x + ")";
+    case FGT_BOOL: return "((" + x + ")!=0)";
+    default: return x;
+  }
+}
+std::string st_conv(int dt, const std::string& x) {
+  switch (dt) {
+    case FGT_F16: return "fgt_f32_to_f16(" + x + ")";
+    case FGT_BF16: return "fgt_f32_to_bf16(" + x + ")";
+    case FGT_BOOL: return "(fgt_u8)(" + x + ")";
+    default: return x;
+  }
+}
+std::string rnd(int dt, const std::string& x) {
+  if (dt == FGT_F16) return "fgt_rnd_f16(" + x + ")";
+  if (dt == FGT_BF16) return "fgt_rnd_bf16(" + x + ")";
+  return x;
+}
+
+float half_bits_to_float(uint16_t h) {
+  uint32_t s = (h >> 15) & 1, e = (h >> 10) & 0x1f, f = h & 0x3ff;
+  uint32_t out;
+  if (e == 0x1f) out = (s << 31) | 0x7f800000u | (f ? 0x400000u : 0);
+  else if (e == 0) {
+    if (!f) out = s << 31;
+    else {
+      int ex = -14;
+      while (!(f & 0x400)) {
+        f <<= 1;
+        --ex;
+      }
+      f &= 0x3ff;
+      out = (s << 31) | ((uint32_t)(ex + 127) << 23) | (f << 13);
+    }
+  } else out = (s << 31) | ((e - 15 + 127) << 23) | (f << 13);
+  float r;
+  std::memcpy(&r, &out, 4);
+  return r;
+}
+
+std::string hex32(uint32_t v) {
+  char b[32];
+  std::snprintf(b, sizeof b, "0x%08xu", v);
+  return b;
+}
+
+std::string literal(int dt, uint64_t bits) {
+  switch (dt) {
+    case FGT_BOOL: return (bits & 0xff) ? "true" : "false";
+    case FGT_I32: return "((int)" + hex32((uint32_t)bits) + ")";
+    case FGT_I64: {
+      char b[48];
+      std::snprintf(b, sizeof b, "((fgt_i64)0x%016llxULL)", (unsigned long long)bits);
+      return b;
+    }
+    case FGT_F32: return "__uint_as_float(" + hex32((uint32_t)bits) + ")";
+    case FGT_F16: {
+      float f = half_bits_to_float((uint16_t)bits);
+      uint32_t u;
+      std::memcpy(&u, &f, 4);
+      return "__uint_as_float(" + hex32(u) + ")";
+    }
+    case FGT_BF16: return "__uint_as_float(" + hex32(((uint32_t)(bits & 0xffff)) << 16) + ")";
+  }
+  return "0";
+}
+
+std::string cast_expr(int from, int to, const std::string& a) {
+  if (from == to) return a;
+  if (to == FGT_BOOL) return "((" + a + ")!=0)";
+  if (from == FGT_BOOL) {
+    if (is_float(to)) return "((" + a + ")?1.0f:0.0f)";
+    return "((" + vt_t(to) + ")((" + a + ")?1:0))";
+  }
+  if (is_int(from) && is_int(to)) return "((" + vt_t(to) + ")(" + a + "))";
+  if (is_int(from)) {
+    if (to == FGT_F32) return "((float)(" + a + "))";
+    if (to == FGT_F16) return "fgt_i64_to_f16v((fgt_i64)(" + a + "))";
+    return "fgt_i64_to_bf16v((fgt_i64)(" + a + "))";
+  }
+  // from floating
+  if (to == FGT_I32) return "fgt_f32_to_i32(" + a + ")";
+  if (to == FGT_I64) return "fgt_f32_to_i64(" + a + ")";
+  return rnd(to, a);  // f32/f16/bf16 -> narrower or equal: one rounding
+}
+
+const char* cmp_op(int p) {
+  switch (p) {
+    case FGT_CMP_EQ: return "==";
+    case FGT_CMP_NE: return "!=";
+    case FGT_CMP_LT: return "<";
+    case FGT_CMP_LE: return "<=";
+    case FGT_CMP_GT: return ">";
+    default: return ">=";
+  }
+}
+
+std::string binary_expr(int op, int dt, const std::string& a, const std::string& b) {
+  const std::string T = vt_t(dt), U = ut_t(dt);
+  const bool f = is_float(dt);
+  switch (op) {
+    case FGT_OP_ADD: return f ? rnd(dt, "__fadd_rn(" + a + "," + b + ")") : "fgt_wrap_add<" + T + "," + U + ">(" + a + "," + b + ")";
+    case FGT_OP_MUL: return f ? rnd(dt, "__fmul_rn(" + a + "," + b + ")") : "fgt_wrap_mul<" + T + "," + U + ">(" + a + "," + b + ")";
+    case FGT_OP_DIV: return rnd(dt, "__fdiv_rn(" + a + "," + b + ")");
+    case FGT_OP_MAXIMUM:
+      if (f) return "fgt_fmax(" + a + "," + b + ")";
+      if (dt == FGT_BOOL) return "(" + a + "||" + b + ")";
+      return "fgt_imax<" + T + ">(" + a + "," + b + ")";
+    case FGT_OP_MINIMUM:
+      if (f) return "fgt_fmin(" + a + "," + b + ")";
+      if (dt == FGT_BOOL) return "(" + a + "&&" + b + ")";
+      return "fgt_imin<" + T + ">(" + a + "," + b + ")";
+    case FGT_OP_POW: return f ? rnd(dt, "powf(" + a + "," + b + ")") : "fgt_ipow<" + T + "," + U + ">(" + a + "," + b + ")";
+    case FGT_OP_FLOORDIV:
+      return f ? rnd(dt, "fgt_ffloordiv(" + a + "," + b + ")") : "fgt_ifloordiv<" + T + ">(" + a + "," + b + "," + min_lit(dt) + ")";
+    case FGT_OP_MOD: return f ? rnd(dt, "fgt_fmod_py(" + a + "," + b + ")") : "fgt_imod<" + T + ">(" + a + "," + b + "," + min_lit(dt) + ")";
+    case FGT_OP_BITWISE_AND: return dt == FGT_BOOL ? "(" + a + "&&" + b + ")" : "(" + a + "&" + b + ")";
+    case FGT_OP_BITWISE_OR: return dt == FGT_BOOL ? "(" + a + "||" + b + ")" : "(" + a + "|" + b + ")";
+    case FGT_OP_BITWISE_XOR: return dt == FGT_BOOL ? "(" + a + "!=" + b + ")" : "(" + a + "^" + b + ")";
+    case FGT_OP_SHIFT_LEFT: return "fgt_ishl<" + T + "," + U + "," + std::to_string(bits_of(dt)) + ">(" + a + "," + b + ")";
+    case FGT_OP_SHIFT_RIGHT: return "fgt_ishr<" + T + "," + std::to_string(bits_of(dt)) + ">(" + a + "," + b + ")";
+  }
+  fail(FGT_ERR_UNSUPPORTED, "binary opcode not supported by the generator");
+}
+
+std::string unary_expr(int op, int dt, const std::string& a) {
+  switch (op) {
+    case FGT_OP_EXP: return rnd(dt, "expf(" + a + ")");
+    case FGT_OP_LOG: return rnd(dt, "logf(" + a + ")");
+    case FGT_OP_SQRT: return rnd(dt, "__fsqrt_rn(" + a + ")");
+    case FGT_OP_SIN: return rnd(dt, "sinf(" + a + ")");
+    case FGT_OP_COS: return rnd(dt, "cosf(" + a + ")");
+    case FGT_OP_TANH: return rnd(dt, "tanhf(" + a + ")");
+    case FGT_OP_ERF: return rnd(dt, "erff(" + a + ")");
+    case FGT_OP_FLOOR: return "floorf(" + a + ")";
+    case FGT_OP_CEIL: return "ceilf(" + a + ")";
+    case FGT_OP_ROUND: return "rintf(" + a + ")";
+    case FGT_OP_ABS:
+      if (is_float(dt)) return "fabsf(" + a + ")";
+      return "((" + a + ")<0?(" + vt_t(dt) + ")((" + ut_t(dt) + ")0-(" + ut_t(dt) + ")(" + a + ")):(" + a + "))";
+    case FGT_OP_BITWISE_NOT: return dt == FGT_BOOL ? "(!" + a + ")" : "(~" + a + ")";
+  }
+  fail(FGT_ERR_UNSUPPORTED, "unary opcode not supported by the generator");
+}
+
+bool expensive(int op) {
+  switch (op) {
+    case FGT_OP_EXP:
+    case FGT_OP_LOG:
+    case FGT_OP_SQRT:
+    case FGT_OP_SIN:
+    case FGT_OP_COS:
+    case FGT_OP_TANH:
+    case FGT_OP_ERF:
+    case FGT_OP_POW:
+    case FGT_OP_DIV:
+      return true;
+  }
+  return false;
+}
+
+// ----------------------------------------------------- reduction algebra ---
+enum Ctx { CTX_ROW, CTX_COL, CTX_FULL, CTX_FIN };
+
+struct RedText {
+  bool arg = false, is_max = false, fl = false;
+  std::string acc_t, part_t, fin_t, ident, identi;
+  int op = 0, dt = 0, odt = 0;  // reduction op, result dtype, operand dtype
+  bool storage = false;
+};
+
+RedText red_text(const Graph& g, int node, int policy, Ctx ctx) {
+  const Node& n = g.nodes[node];
+  const Node& x = g.nodes[n.args[0]];
+  RedText t;
+  t.op = n.op;
+  t.dt = n.dt;
+  t.odt = x.dt;
+  t.fl = is_float(x.dt);
+  t.storage = policy == FGT_ACCUM_STORAGE;
+  if (is_argreduce(n.op)) {
+    t.arg = true;
+    t.is_max = n.op == FGT_OP_ARGMAX;
+    t.acc_t = t.part_t = t.fin_t = vt_t(x.dt);
+    if (t.fl) t.ident = t.is_max ? "__int_as_float(0xff800000)" : "__int_as_float(0x7f800000)";
+    else t.ident = t.is_max ? min_lit(x.dt) : max_lit(x.dt);
+    t.identi = "9223372036854775807LL";
+    return t;
+  }
+  switch (n.op) {
+    case FGT_OP_REDUCE_SUM:
+    case FGT_OP_REDUCE_PROD: {
+      std::string one = n.op == FGT_OP_REDUCE_SUM ? "0" : "1";
+      if (t.fl && !t.storage) {
+        // f32 within a thread's bounded span (a row, or a CTA's rows of one
+        // column), f64 across unbounded spans (grid-stride loops, partials).
+        t.acc_t = (ctx == CTX_FULL || ctx == CTX_FIN) ? "double" : "float";
+        t.part_t = ctx == CTX_COL ? "float" : "double";
+        t.fin_t = "double";
+        t.ident = (ctx == CTX_FULL || ctx == CTX_FIN) ? one + ".0" : one + ".0f";
+      } else if (t.fl) {
+        t.acc_t = t.part_t = t.fin_t = "float";
+        t.ident = one + ".0f";
+      } else {
+        t.acc_t = t.part_t = t.fin_t = vt_t(x.dt);
+        t.ident = "((" + vt_t(x.dt) + ")" + one + ")";
+      }
+      break;
+    }
+    case FGT_OP_REDUCE_MAX:
+    case FGT_OP_REDUCE_MIN: {
+      bool mx = n.op == FGT_OP_REDUCE_MAX;
+      t.acc_t = t.part_t = t.fin_t = vt_t(x.dt);
+      if (t.fl) t.ident = mx ? "__int_as_float(0xff800000)" : "__int_as_float(0x7f800000)";
+      else t.ident = mx ? min_lit(x.dt) : max_lit(x.dt);
+      break;
+    }
+    case FGT_OP_REDUCE_ANY:
+    case FGT_OP_REDUCE_ALL:
+      t.acc_t = t.fin_t = "bool";
+      t.part_t = "fgt_u8";
+      t.ident = n.op == FGT_OP_REDUCE_ANY ? "false" : "true";
+      break;
+  }
+  return t;
+}
+
+// a = a (+) b for a value reduction, as a statement.
+std::string comb_stmt(const RedText& t, const std::string& a, const std::string& b) {
+  const std::string T = vt_t(t.odt), U = ut_t(t.odt);
+  switch (t.op) {
+    case FGT_OP_REDUCE_SUM:
+      if (t.fl) return a + " = " + (t.storage ? rnd(t.odt, "__fadd_rn(" + a + "," + b + ")") : a + " + " + b) + ";";
+      return a + " = fgt_wrap_add<" + T + "," + U + ">(" + a + "," + b + ");";
+    case FGT_OP_REDUCE_PROD:
+      if (t.fl) return a + " = " + (t.storage ? rnd(t.odt, "__fmul_rn(" + a + "," + b + ")") : a + " * " + b) + ";";
+      return a + " = fgt_wrap_mul<" + T + "," + U + ">(" + a + "," + b + ");";
+    case FGT_OP_REDUCE_MAX:
+      return a + " = " + (t.fl ? "fgt_fmax(" : "fgt_imax<" + T + ">(") + a + "," + b + ");";
+    case FGT_OP_REDUCE_MIN:
+      return a + " = " + (t.fl ? "fgt_fmin(" : "fgt_imin<" + T + ">(") + a + "," + b + ");";
+    case FGT_OP_REDUCE_ANY: return a + " = " + a + " || " + b + ";";
+    case FGT_OP_REDUCE_ALL: return a + " = " + a + " && " + b + ";";
+  }
+  return "";
+}
+std::string arg_stmt(const RedText& t, const std::string& a, const std::string& ai, const std::string& b,
+                     const std::string& bi) {
+  std::string fn = t.fl ? std::string("fgt_arg_better_f<") + (t.is_max ? "true" : "false") + ">"
+                        : std::string("fgt_arg_better_i<") + (t.is_max ? "true" : "false") + "," + vt_t(t.odt) + ">";
+  return "if (" + fn + "(" + b + "," + bi + "," + a + "," + ai + ")) { " + a + " = " + b + "; " + ai + " = " + bi + "; }";
+}
+// Round a finished accumulator to the reduction's result dtype (once).
+std::string finalize(const RedText& t, const std::string& acc, const std::string& acc_t) {
+  if (!t.fl || t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN) return acc;
+  if (acc_t == "double") {
+    if (t.dt == FGT_F32) return "__double2float_rn(" + acc + ")";
+    if (t.dt == FGT_F16) return "fgt_rnd_f16(fgt_f64_to_f32_odd(" + acc + "))";
+    return "fgt_rnd_bf16(fgt_f64_to_f32_odd(" + acc + "))";
+  }
+  return rnd(t.dt, acc);
+}
+
+// ------------------------------------------------------------------ emitter -
+enum ScKind { SC_PRO, SC_PROLANE, SC_ROW, SC_LANE, SC_CACHE };
+struct Sc {
+  ScKind k;
+  int p;
+};
+
+struct Emitter {
+  const Plan& P;
+  const Graph& g;
+  const KernelDef& K;
+  const Domain& d;
+  std::set<int64_t>* temps_loaded;
+  std::vector<RedDef> fin_reds;
+  Analyzer an;
+  bool row = false, elem = false, fin = false, cached = false;
+  int nphase = 1;
+  int U = 1;
+
+  std::vector<std::string> kdecl, prosites, prolane, rowdecl, rowsites, rowend, kend;
+  std::vector<std::vector<std::string>> rowsc, lane, chunkpre, chunkpost, post;
+  std::vector<std::string> eload;  // ELEM: site loads (per u)
+  std::map<std::string, std::string> memo;
+  std::map<int, std::string> red_var;  // node -> variable holding its value
+  int uid = 0;
+
+  Emitter(const Plan& P_, const KernelDef& K_, std::set<int64_t>* tl)
+      : P(P_), g(P_.g), K(K_), d(K_.dom), temps_loaded(tl), an(P_.g, P_.loc, K_.kind, K_.dom) {
+    row = K.kind == KKind::ROW;
+    elem = K.kind == KKind::ELEM;
+    fin = K.kind == KKind::COLFIN || K.kind == KKind::FULLFIN;
+    cached = row && !K.streaming;
+    U = elem ? K.unroll : 1;
+    fin_reds = K.reds;
+    for (auto& rd : fin_reds) an.group[rd.node] = &rd;
+  }
+
+  std::string fresh(const char* p) { return std::string(p) + std::to_string(uid++); }
+
+  void add(Sc s, const std::string& st) {
+    switch (s.k) {
+      case SC_PRO: kdecl.push_back(st); break;
+      case SC_PROLANE: prolane.push_back(st); break;
+      case SC_ROW: rowsc[s.p].push_back(st); break;
+      default: lane[s.p].push_back(st); break;
+    }
+  }
+
+  // Integer index text in the given scope. Digits collapse to r / e when the
+  // coefficients follow the mixed radix (the common, vectorisable case).
+  std::string itext(const Idx& a, const char* evar = "e") {
+    if (!a.aff) return "(" + a.code + ")";
+    std::ostringstream s;
+    s << "(" << a.k << "LL";
+    bool prop = d.no() > 0;
+    int64_t alpha = 0;
+    for (int k = 0; k < d.no(); ++k) {
+      if (k == d.no() - 1) alpha = a.c[k];
+    }
+    for (int k = 0; k < d.no() && prop; ++k)
+      if (a.c[k] != alpha * d.ow[k]) prop = false;
+    if (prop) {
+      if (alpha) s << "+" << alpha << "LL*r";
+    } else {
+      for (int k = 0; k < d.no(); ++k)
+        if (a.c[k]) s << "+" << a.c[k] << "LL*o" << k;
+    }
+    const int ni = (int)d.id.size();
+    bool propi = ni > 0;
+    int64_t beta = ni ? a.c[d.no() + ni - 1] : 0;
+    for (int k = 0; k < ni && propi; ++k)
+      if (a.c[d.no() + k] != beta * d.iw[k]) propi = false;
+    if (propi) {
+      if (beta) s << "+" << beta << "LL*" << evar;
+    } else {
+      for (int k = 0; k < ni; ++k) {
+        if (!a.c[d.no() + k]) continue;
+        if (std::string(evar) == "e") s << "+" << a.c[d.no() + k] << "LL*i" << k;
+        else s << "+" << a.c[d.no() + k] << "LL*((" << evar << "/" << d.iw[k] << "LL)%" << d.id[k] << "LL)";
+      }
+    }
+    s << ")";
+    return s.str();
+  }
+
+  // Is the affine address exactly base(o) + e with base aligned to the vector?
+  bool contiguous(const Idx& a, std::string* base) {
+    if (!a.aff || d.id.empty()) return false;
+    for (int k = 0; k < (int)d.id.size(); ++k)
+      if (a.c[d.no() + k] != d.iw[k]) return false;
+    if (d.NI % K.vec) return false;
+    if (a.k % K.vec) return false;
+    for (int k = 0; k < d.no(); ++k)
+      if (a.c[k] % K.vec) return false;
+    Idx b = a;
+    for (int k = 0; k < (int)d.id.size(); ++k) b.c[d.no() + k] = 0;
+    *base = itext(b);
+    return true;
+  }
+  bool uniform(const Idx& a) {
+    if (!a.aff || d.id.empty()) return false;
+    if (a.c[d.nd() - 1] != 0) return false;
+    return d.id.back() % K.vec == 0;
+  }
+
+  std::string ptr_of(int node, bool for_store = false, int port = -1, int64_t temp = -1) {
+    const Node& n = g.nodes[node];
+    const std::string T = st_t(n.dt);
+    if (for_store) {
+      if (port >= 0) return "((" + T + "*)p.out[" + std::to_string(port) + "])";
+      return "((" + T + "*)(p.ws+" + std::to_string(temp) + "LL))";
+    }
+    const Loc& L = P.loc[node];
+    if (L.kind == Loc::INPUT) return "((const " + T + "*)p.in[" + std::to_string(L.index) + "])";
+    if (L.kind == Loc::OUTPUT) return "((const " + T + "*)p.out[" + std::to_string(L.index) + "])";
+    if (temps_loaded) temps_loaded->insert(L.offset);
+    return "((const " + T + "*)(p.ws+" + std::to_string(L.offset) + "LL))";
+  }
+
+  std::string load(int id, const Map& m, Sc D) {
+    const Node& n = g.nodes[id];
+    Idx A = to_linear(m, n.shape, d);
+    const std::string ptr = ptr_of(id);
+    const std::string VT = vt_t(n.dt), ST = st_t(n.dt);
+    if (D.k == SC_PRO) {
+      std::string v = fresh("g");
+      add(D, "const " + VT + " " + v + " = " + ld_conv(n.dt, ptr + "[" + itext(A) + "]") + ";");
+      return v;
+    }
+    if (D.k == SC_ROW) {
+      std::string v = fresh("w");
+      add(D, "const " + VT + " " + v + " = rv ? " + ld_conv(n.dt, ptr + "[" + itext(A) + "]") + " : (" + VT + ")0;");
+      return v;
+    }
+    std::string base;
+    const bool prol = D.k == SC_PROLANE;
+    std::string ctx = prol ? "P" : cached ? "R" : elem ? "E" : ("S" + std::to_string(D.p));
+    if (contiguous(A, &base)) {
+      std::string key = "site" + ctx + "|" + std::to_string(id) + "|" + base;
+      auto it = memo.find(key);
+      std::string s;
+      if (it != memo.end()) s = it->second;
+      else {
+        s = fresh("s");
+        memo[key] = s;
+        const std::string vec = std::to_string(K.vec);
+        if (prol) {
+          prosites.push_back(ST + " " + s + "[" + vec + "]; fgt_vload_keep(" + s + ", " + ptr + " + " + base + " + e0);");
+        } else if (cached) {
+          rowdecl.push_back(ST + " " + s + "[" + std::to_string(K.nch) + "][" + vec + "];");
+          rowsites.push_back("fgt_vload(" + s + "[c], " + ptr + " + " + base + " + e0);");
+        } else if (elem) {
+          eload.push_back("fgt_vload(" + s + "[u], " + ptr + " + " + base + " + e0);");
+          rowdecl.push_back(ST + " " + s + "[" + std::to_string(U) + "][" + vec + "];");
+        } else {
+          chunkpre[D.p].push_back(ST + " " + s + "[" + vec + "]; fgt_vload(" + s + ", " + ptr + " + " + base + " + e0);");
+        }
+      }
+      if (prol) return ld_conv(n.dt, s + "[v]");
+      if (cached) return ld_conv(n.dt, s + "[c][v]");
+      if (elem) return ld_conv(n.dt, s + "[u][v]");
+      return ld_conv(n.dt, s + "[v]");
+    }
+    if (uniform(A)) {
+      std::string at = itext(A, "e0");
+      std::string key = "uni" + ctx + "|" + std::to_string(id) + "|" + at;
+      auto it = memo.find(key);
+      std::string s;
+      if (it != memo.end()) s = it->second;
+      else {
+        s = fresh("u");
+        memo[key] = s;
+        if (prol) prosites.push_back("const " + ST + " " + s + " = " + ptr + "[" + at + "];");
+        else if (cached) {
+          rowdecl.push_back(ST + " " + s + "[" + std::to_string(K.nch) + "];");
+          rowsites.push_back(s + "[c] = " + ptr + "[" + at + "];");
+        } else if (elem) {
+          rowdecl.push_back(ST + " " + s + "[" + std::to_string(U) + "];");
+          eload.push_back(s + "[u] = " + ptr + "[" + at + "];");
+        } else {
+          chunkpre[D.p].push_back("const " + ST + " " + s + " = " + ptr + "[" + at + "];");
+        }
+      }
+      if (prol) return ld_conv(n.dt, s);
+      if (cached) return ld_conv(n.dt, s + "[c]");
+      if (elem) return ld_conv(n.dt, s + "[u]");
+      return ld_conv(n.dt, s);
+    }
+    std::string v = fresh("x");
+    add(D, "const " + VT + " " + v + " = " + ld_conv(n.dt, "__ldg(" + ptr + " + " + itext(A) + ")") + ";");
+    return v;
+  }
+
+  // Value of node `id` read at map m, usable from scope s.
+  std::string val(int id, const Map& m, Sc s) {
+    Level L = an.run(id, m);
+    Sc D{SC_PRO, 0};
+    if (L.kind == 0) D = {SC_PRO, 0};
+    else if (L.kind == 1) D = {SC_ROW, L.phase};
+    else if (L.kind == 2) D = cached ? Sc{SC_PROLANE, 0} : Sc{SC_LANE, s.k == SC_LANE ? s.p : 0};
+    else {
+      require(s.k == SC_LANE, "internal: element value requested outside an element loop", FGT_ERR_UNSUPPORTED);
+      D = {SC_LANE, s.p};
+      if (cached && s.p > L.phase && expensive(g.nodes[id].op)) D = {SC_CACHE, L.phase};
+    }
+    if (s.k == SC_PROLANE && D.k == SC_LANE) D = s;
+    std::string key = std::to_string(id) + "@" + m.key() + "#" + std::to_string((int)D.k) + ":" + std::to_string(D.p);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+    std::string r;
+    const Node& n = g.nodes[id];
+    if (D.k == SC_CACHE) {
+      std::string v = val(id, m, Sc{SC_LANE, D.p});
+      std::string cname = fresh("c");
+      rowdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
+      lane[D.p].push_back(cname + "[c][v] = " + v + ";");
+      r = cname + "[c][v]";
+    } else if (D.k == SC_PROLANE && s.k != SC_PROLANE) {
+      std::string v = val(id, m, Sc{SC_PROLANE, 0});
+      std::string cname = fresh("cv");
+      kdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
+      prolane.push_back(cname + "[c][v] = " + v + ";");
+      r = cname + "[c][v]";
+      memo[key] = r;
+      return r;
+    } else {
+      r = define(id, m, D);
+    }
+    memo[key] = r;
+    return r;
+  }
+
+  std::string define(int id, const Map& m, Sc D) {
+    const Node& n = g.nodes[id];
+    auto rv = red_var.find(id);
+    if (rv != red_var.end() && an.group.count(id)) return rv->second;
+    if (P.loc[id].kind != Loc::NONE && !an.group.count(id)) return load(id, m, D);
+    switch (n.op) {
+      case FGT_OP_CONSTANT:
+        return literal(n.dt, n.cbits);
+      case FGT_OP_IOTA: {
+        auto C = to_coords(m, n.shape, d);
+        std::string t = itext(C[n.attrs[0]]);
+        auto io = P.iota_offsets.find(id);
+        if (io != P.iota_offsets.end()) t = "(" + t + "+" + std::to_string(io->second) + "LL)";
+        return cast_expr(FGT_I64, n.dt, t);
+      }
+      case FGT_OP_SPLAT:
+      case FGT_OP_RESHAPE:
+      case FGT_OP_BROADCAST_IN_DIM:
+      case FGT_OP_TRANSPOSE:
+      case FGT_OP_STOP_GRADIENT: {
+        auto ms = operand_maps(g, id, m, d);
+        return val(n.args[0], ms[0], D);
+      }
+      default:
+        break;
+    }
+    auto ms = operand_maps(g, id, m, d);
+    std::vector<std::string> a;
+    for (size_t k = 0; k < n.args.size(); ++k) a.push_back(val(n.args[k], ms[k], D));
+    std::string expr;
+    const int odt = g.nodes[n.args[0]].dt;
+    if (n.op == FGT_OP_CAST) expr = cast_expr(odt, n.dt, a[0]);
+    else if (n.op == FGT_OP_COMPARE) expr = "(" + a[0] + cmp_op(n.pred) + a[1] + ")";
+    else if (n.op == FGT_OP_SELECT) expr = "(" + a[0] + "?" + a[1] + ":" + a[2] + ")";
+    else if (is_binary(n.op)) expr = binary_expr(n.op, n.dt, a[0], a[1]);
+    else if (is_unary(n.op)) expr = unary_expr(n.op, n.dt, a[0]);
+    else fail(FGT_ERR_UNSUPPORTED, std::string("generator cannot place ") + opcode_name(n.op));
+    std::string v = fresh("t");
+    add(D, "const " + vt_t(n.dt) + " " + v + " = " + expr + ";");
+    return v;
+  }
+
+  // ---------------------------------------------------------------------
+  Map store_map(const OutStore& st) {
+    const Node& n = g.nodes[st.node];
+    Map m;
+    if (st.level == 3) {
+      m.co.assign(n.rank(), idx_const(d.nd(), 0));
+      return m;
+    }
+    if (st.level == 2 || st.level == 1) {
+      // row level: the row digits; column level: the FIN kernel's digits
+      int k = 0;
+      for (int64_t s : n.shape) m.co.push_back(s == 1 ? idx_const(d.nd(), 0) : idx_digit(d.nd(), k++));
+      return m;
+    }
+    // element level
+    if (elem) {
+      m.lin = true;
+      m.l = idx_const(d.nd(), 0);
+      for (int j = 0; j < d.nd(); ++j) m.l.c[j] = d.iw[j];
+      return m;
+    }
+    // same non-unit extents as the seed reduction's operand
+    const RedDef& seed = K.reds.front();
+    const Node& x = g.nodes[g.nodes[seed.node].args[0]];
+    std::vector<Idx> nu;
+    for (size_t j = 0; j < x.shape.size(); ++j)
+      if (x.shape[j] != 1) nu.push_back(seed.opmap.co[j]);
+    size_t t = 0;
+    for (int64_t s : n.shape) m.co.push_back(s == 1 ? idx_const(d.nd(), 0) : nu[t++]);
+    return m;
+  }
+
+  std::string store_stmt_elem(const OutStore& st, int phase, const std::string& v) {
+    const Node& n = g.nodes[st.node];
+    Map m = store_map(st);
+    Idx A = to_linear(m, n.shape, d);
+    std::string ptr = ptr_of(st.node, true, st.port, st.temp_offset);
+    std::string base;
+    if (contiguous(A, &base)) {
+      std::string ob = fresh("ob");
+      chunkpre[phase].push_back(st_t(n.dt) + " " + ob + "[" + std::to_string(K.vec) + "];");
+      chunkpost[phase].push_back("fgt_vstore(" + ptr + " + " + base + " + e0, " + ob + ");");
+      return ob + "[v] = " + st_conv(n.dt, v) + ";";
+    }
+    return ptr + "[" + itext(A) + "] = " + st_conv(n.dt, v) + ";";
+  }
+
+  // Butterfly within TW lanes then (if the group spans warps) a sequential
+  // combine of the warp partials in warp order, so every lane ends with the
+  // same deterministic value.
+  void group_reduce(std::vector<std::string>& out, const std::vector<std::pair<RedText, std::string>>& accs,
+                    int TW, bool cross_warp, int NW, const std::string& tag) {
+    if (accs.empty()) return;
+    out.push_back("#pragma unroll");
+    out.push_back("for (int m_ = 1; m_ < " + std::to_string(TW) + "; m_ <<= 1) {");
+    for (auto& [t, a] : accs) {
+      if (t.arg) {
+        out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); const fgt_i64 oi = fgt_shfl_xor(" + a +
+                      "i, m_); " + arg_stmt(t, a, a + "i", "ov", "oi") + " }");
+      } else {
+        out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); " + comb_stmt(t, a, "ov") + " }");
+      }
+    }
+    out.push_back("}");
+    if (!cross_warp) return;
+    for (auto& [t, a] : accs) {
+      kdecl.push_back("__shared__ " + t.acc_t + " sm_" + a + tag + "[" + std::to_string(NW) + "];");
+      if (t.arg) kdecl.push_back("__shared__ fgt_i64 smi_" + a + tag + "[" + std::to_string(NW) + "];");
+    }
+    out.push_back("if ((tid & 31) == 0) {");
+    for (auto& [t, a] : accs) {
+      out.push_back("  sm_" + a + tag + "[tid >> 5] = " + a + ";");
+      if (t.arg) out.push_back("  smi_" + a + tag + "[tid >> 5] = " + a + "i;");
+    }
+    out.push_back("}");
+    out.push_back("__syncthreads();");
+    for (auto& [t, a] : accs) {
+      out.push_back(a + " = sm_" + a + tag + "[0];");
+      if (t.arg) out.push_back(a + "i = smi_" + a + tag + "[0];");
+      out.push_back("for (int w_ = 1; w_ < " + std::to_string(NW) + "; ++w_) {");
+      if (t.arg)
+        out.push_back("  { const " + t.acc_t + " ov = sm_" + a + tag + "[w_]; const fgt_i64 oi = smi_" + a + tag + "[w_]; " +
+                      arg_stmt(t, a, a + "i", "ov", "oi") + " }");
+      else out.push_back("  { const " + t.acc_t + " ov = sm_" + a + tag + "[w_]; " + comb_stmt(t, a, "ov") + " }");
+      out.push_back("}");
+    }
+    out.push_back("__syncthreads();");
+  }
+
+  std::string arg_index(const RedDef& rd) {
+    const Node& n = g.nodes[rd.node];
+    const Node& x = g.nodes[n.args[0]];
+    auto C = to_coords(rd.opmap, x.shape, d);
+    std::string t = itext(C[n.attrs[0]]);
+    return t;
+  }
+
+  // ------------------------------------------------------------ kernels --
+  std::string args_struct() {
+    const int nin = std::max<int>(1, (int)g.input_nodes.size());
+    const int nout = std::max<int>(1, (int)g.outputs.size());
+    return "struct FgtArgs { const void* in[" + std::to_string(nin) + "]; void* out[" + std::to_string(nout) +
+           "]; unsigned char* ws; long long nparts; long long pad_; };\n";
+  }
+
+  static void put(std::ostringstream& o, const std::vector<std::string>& v, const std::string& ind) {
+    for (auto& s : v)
+      if (!s.empty()) o << ind << s << "\n";
+  }
+
+  std::string digits_o() {
+    std::string s;
+    for (int k = 0; k < d.no(); ++k)
+      s += "const fgt_i64 o" + std::to_string(k) + " = (r / " + std::to_string(d.ow[k]) + "LL) % " + std::to_string(d.od[k]) + "LL; ";
+    return s;
+  }
+  std::string digits_i() {
+    std::string s;
+    for (int k = 0; k < (int)d.id.size(); ++k)
+      s += "const fgt_i64 i" + std::to_string(k) + " = (e / " + std::to_string(d.iw[k]) + "LL) % " + std::to_string(d.id[k]) + "LL; ";
+    return s;
+  }
+
+  std::string build_row() {
+    // Phases: one element loop per dependency level of the row reductions.
+    std::vector<const RedDef*> rows, cols;
+    for (auto& rd : K.reds) (rd.role == ROLE_ROW ? rows : cols).push_back(&rd);
+    int maxp = 0;
+    std::map<int, int> rphase;
+    for (auto* rd : rows) {
+      an.run(rd->node, [&] {
+        Map m;
+        const Node& n = g.nodes[rd->node];
+        int k = 0;
+        for (int64_t s : n.shape) m.co.push_back(s == 1 ? idx_const(d.nd(), 0) : idx_digit(d.nd(), k++));
+        return m;
+      }());
+      rphase[rd->node] = an.red_phase[rd->node];
+      maxp = std::max(maxp, rphase[rd->node]);
+    }
+    std::map<const RedDef*, int> cphase;
+    for (auto* rd : cols) {
+      int p = an.run(g.nodes[rd->node].args[0], rd->opmap).phase;
+      cphase[rd] = p;
+      maxp = std::max(maxp, p);
+    }
+    std::vector<std::pair<const OutStore*, int>> estores;
+    for (auto& st : K.stores)
+      if (st.level == 0) {
+        int p = an.run(st.node, store_map(st)).phase;
+        estores.push_back({&st, p});
+        maxp = std::max(maxp, p);
+      }
+    nphase = maxp + 1;
+    rowsc.assign(nphase + 1, {});
+    lane.assign(nphase, {});
+    chunkpre.assign(nphase, {});
+    chunkpost.assign(nphase, {});
+    post.assign(nphase, {});
+    const int TW = std::min(K.tpr, 32);
+    const bool xw = K.tpr > 32;
+    const int NW = K.nt / 32;
+    // row reductions
+    std::map<int, std::vector<std::pair<RedText, std::string>>> phase_accs;
+    std::map<int, std::string> acc_of;
+    for (auto* rd : rows) {
+      RedText t = red_text(g, rd->node, P.opt.accumulation, CTX_ROW);
+      int p = rphase[rd->node];
+      std::string a = fresh("acc");
+      rowsc[p].push_back(t.acc_t + " " + a + " = " + t.ident + ";");
+      if (t.arg) rowsc[p].push_back("fgt_i64 " + a + "i = " + t.identi + ";");
+      std::string v = val(g.nodes[rd->node].args[0], rd->opmap, Sc{SC_LANE, p});
+      if (t.arg) lane[p].push_back("{ const fgt_i64 ix = " + arg_index(*rd) + "; " + arg_stmt(t, a, a + "i", v, "ix") + " }");
+      else lane[p].push_back(comb_stmt(t, a, v));
+      phase_accs[p].push_back({t, a});
+      acc_of[rd->node] = a;
+      std::string rv = fresh("red");
+      red_var[rd->node] = rv;
+    }
+    for (auto& [p, accs] : phase_accs) {
+      group_reduce(post[p], accs, TW, xw, NW, "_p" + std::to_string(p));
+    }
+    for (auto* rd : rows) {
+      int p = rphase[rd->node];
+      RedText t = red_text(g, rd->node, P.opt.accumulation, CTX_ROW);
+      const std::string& a = acc_of[rd->node];
+      if (t.arg) {
+        std::string ix = a + "i";
+        if (rd->index_offset) ix = "(" + ix + "+" + std::to_string(rd->index_offset) + "LL)";
+        post[p].push_back("const fgt_i64 " + red_var[rd->node] + " = " + ix + ";");
+      } else {
+        post[p].push_back("const " + vt_t(t.dt) + " " + red_var[rd->node] + " = " + finalize(t, a, t.acc_t) + ";");
+      }
+    }
+    // column reductions: per-thread accumulators across the CTA's rows
+    std::vector<std::string> colfin;
+    for (auto* rd : cols) {
+      RedText t = red_text(g, rd->node, P.opt.accumulation, CTX_COL);
+      int p = cphase[rd];
+      std::string a = fresh("cacc");
+      std::string dims = "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "]";
+      kdecl.push_back(t.acc_t + " " + a + dims + ";");
+      if (t.arg) kdecl.push_back("fgt_i64 " + a + "i" + dims + ";");
+      std::string init = "for (int c = 0; c < " + std::to_string(K.nch) + "; ++c) for (int v = 0; v < " + std::to_string(K.vec) +
+                         "; ++v) { " + a + "[c][v] = " + t.ident + ";" + (t.arg ? " " + a + "i[c][v] = " + t.identi + ";" : std::string()) + " }";
+      kdecl.push_back(init);
+      std::string v = val(g.nodes[rd->node].args[0], rd->opmap, Sc{SC_LANE, p});
+      if (t.arg) {
+        std::string ix = arg_index(*rd);
+        if (rd->index_offset) ix = "(" + ix + "+" + std::to_string(rd->index_offset) + "LL)";
+        lane[p].push_back("{ const fgt_i64 ix = " + ix + "; " + arg_stmt(t, a + "[c][v]", a + "i[c][v]", v, "ix") + " }");
+      } else {
+        lane[p].push_back(comb_stmt(t, a + "[c][v]", v));
+      }
+      std::string slot = "((fgt_i64)blockIdx.x * " + std::to_string(K.rows_per_cta) + " + grp)";
+      std::string pv = "((" + t.part_t + "*)(p.ws+" + std::to_string(rd->part_val) + "LL))";
+      std::string body = pv + "[" + slot + "*" + std::to_string(d.NI) + "LL + e] = (" + t.part_t + ")" + a + "[c][v];";
+      if (t.arg) body += " ((fgt_i64*)(p.ws+" + std::to_string(rd->part_idx) + "LL))[" + slot + "*" + std::to_string(d.NI) +
+                         "LL + e] = " + a + "i[c][v];";
+      colfin.push_back(body);
+    }
+    // element stores
+    for (auto& [st, p] : estores) {
+      std::string v = val(st->node, store_map(*st), Sc{SC_LANE, p});
+      lane[p].push_back(store_stmt_elem(*st, p, v));
+    }
+    // row-level stores (after the last phase)
+    for (auto& st : K.stores) {
+      if (st.level != 1) continue;
+      Map m = store_map(st);
+      std::string v = val(st.node, m, Sc{SC_ROW, nphase});
+      const Node& n = g.nodes[st.node];
+      Idx A = to_linear(m, n.shape, d);
+      rowend.push_back("if (rv && lane == 0) " + ptr_of(st.node, true, st.port, st.temp_offset) + "[" + itext(A) + "] = " +
+                       st_conv(n.dt, v) + ";");
+    }
+    // ---- assemble
+    std::ostringstream o;
+    const std::string NT = std::to_string(K.nt), TPR = std::to_string(K.tpr), VEC = std::to_string(K.vec),
+                      NCH = std::to_string(K.nch), RPC = std::to_string(K.rows_per_cta);
+    o << args_struct();
+    o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
+    o << "  const int tid = threadIdx.x; const int lane = tid % " << TPR << "; const int grp = tid / " << TPR << ";\n";
+    o << "  (void)lane; (void)grp;\n";
+    o << "  const fgt_i64 NR = " << d.NR << "LL, NI = " << d.NI << "LL; (void)NI;\n";
+    put(o, kdecl, "  ");
+    if (cached && !prolane.empty()) {
+      o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
+      o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << "    if (e0 < NI) {\n";
+      put(o, prosites, "      ");
+      o << "      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+      put(o, prolane, "        ");
+      o << "      }\n    }\n  }\n";
+    }
+    o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += (fgt_i64)gridDim.x * " << RPC << ") {\n";
+    o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
+    put(o, rowdecl, "    ");
+    if (cached && !rowsites.empty()) {
+      o << "    if (rv) {\n      #pragma unroll\n      for (int c = 0; c < " << NCH << "; ++c) {\n";
+      o << "        const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << "        if (e0 < NI) {\n";
+      put(o, rowsites, "          ");
+      o << "        }\n      }\n    }\n";
+    }
+    for (int p = 0; p < nphase; ++p) {
+      put(o, rowsc[p], "    ");
+      o << "    if (rv) {\n";
+      if (cached) o << "      #pragma unroll\n";
+      else o << "      #pragma unroll 1\n";
+      o << "      for (int c = 0; c < " << NCH << "; ++c) {\n";
+      o << "        const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << "        if (e0 < NI) {\n";
+      put(o, chunkpre[p], "          ");
+      o << "          #pragma unroll\n          for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << "            const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+      put(o, lane[p], "            ");
+      o << "          }\n";
+      put(o, chunkpost[p], "          ");
+      o << "        }\n      }\n    }\n";
+      put(o, post[p], "    ");
+    }
+    put(o, rowsc[nphase], "    ");
+    put(o, rowend, "    ");
+    o << "  }\n";
+    if (!colfin.empty()) {
+      o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
+      o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << "    if (e0 < NI) {\n      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << "        const fgt_i64 e = e0 + v;\n";
+      put(o, colfin, "        ");
+      o << "      }\n    }\n  }\n";
+    }
+    o << "}\n";
+    return o.str();
+  }
+
+  std::string build_elem() {
+    nphase = 1;
+    rowsc.assign(2, {});
+    lane.assign(1, {});
+    chunkpre.assign(1, {});
+    chunkpost.assign(1, {});
+    post.assign(1, {});
+    std::vector<std::pair<RedText, std::string>> accs;
+    std::vector<std::string> partial_store;
+    for (auto& rd : K.reds) {
+      RedText t = red_text(g, rd.node, P.opt.accumulation, CTX_FULL);
+      std::string a = fresh("acc");
+      kdecl.push_back(t.acc_t + " " + a + " = " + t.ident + ";");
+      if (t.arg) kdecl.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
+      std::string v = val(g.nodes[rd.node].args[0], rd.opmap, Sc{SC_LANE, 0});
+      if (t.arg) {
+        std::string ix = arg_index(rd);
+        if (rd.index_offset) ix = "(" + ix + "+" + std::to_string(rd.index_offset) + "LL)";
+        lane[0].push_back("{ const fgt_i64 ix = " + ix + "; " + arg_stmt(t, a, a + "i", v, "ix") + " }");
+      } else if (t.acc_t == "double") {
+        lane[0].push_back(comb_stmt(t, a, "(double)(" + v + ")"));
+      } else {
+        lane[0].push_back(comb_stmt(t, a, v));
+      }
+      accs.push_back({t, a});
+      std::string ps = "((" + t.part_t + "*)(p.ws+" + std::to_string(rd.part_val) + "LL))[blockIdx.x] = (" + t.part_t + ")" + a + ";";
+      if (t.arg) ps += " ((fgt_i64*)(p.ws+" + std::to_string(rd.part_idx) + "LL))[blockIdx.x] = " + a + "i;";
+      partial_store.push_back(ps);
+    }
+    for (auto& st : K.stores) {
+      std::string v = val(st.node, store_map(st), Sc{SC_LANE, 0});
+      lane[0].push_back(store_stmt_elem(st, 0, v));
+    }
+    std::vector<std::string> red_code;
+    group_reduce(red_code, accs, 32, true, K.nt / 32, "_f");
+    std::ostringstream o;
+    const std::string NT = std::to_string(K.nt), VEC = std::to_string(K.vec), UU = std::to_string(U);
+    o << args_struct();
+    o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
+    o << "  const int tid = threadIdx.x; const fgt_i64 r = 0; const bool rv = true; (void)r; (void)rv;\n";
+    o << "  const fgt_i64 NI = " << d.NI << "LL; const fgt_i64 NCK = NI / " << VEC << ";\n";
+    put(o, kdecl, "  ");
+    o << "  const fgt_i64 stride = (fgt_i64)gridDim.x * " << NT << ";\n";
+    o << "  for (fgt_i64 base = (fgt_i64)blockIdx.x * " << NT << " + tid; base < NCK; base += stride * " << UU << ") {\n";
+    put(o, rowdecl, "    ");
+    if (!eload.empty()) {
+      o << "    #pragma unroll\n    for (int u = 0; u < " << UU << "; ++u) {\n";
+      o << "      const fgt_i64 ch = base + u * stride;\n      if (ch < NCK) {\n        const fgt_i64 e0 = ch * " << VEC << ";\n";
+      put(o, eload, "        ");
+      o << "      }\n    }\n";
+    }
+    o << "    #pragma unroll\n    for (int u = 0; u < " << UU << "; ++u) {\n";
+    o << "      const fgt_i64 ch = base + u * stride;\n      if (ch < NCK) {\n        const fgt_i64 e0 = ch * " << VEC << ";\n";
+    put(o, chunkpre[0], "        ");
+    o << "        #pragma unroll\n        for (int v = 0; v < " << VEC << "; ++v) {\n";
+    o << "          const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+    put(o, lane[0], "          ");
+    o << "        }\n";
+    put(o, chunkpost[0], "        ");
+    o << "      }\n    }\n  }\n";
+    if (!accs.empty()) {
+      put(o, red_code, "  ");
+      o << "  if (tid == 0) {\n";
+      put(o, partial_store, "    ");
+      o << "  }\n";
+    }
+    o << "}\n";
+    return o.str();
+  }
+
+  // Combine partials for reduction rd into `a` (+ `a`i), per element e.
+  std::string fin_combine(const RedDef& rd, const RedText& t, const std::string& src_t, const std::string& a,
+                          const std::string& e, const std::string& count, int stage, int64_t rec_off) {
+    std::ostringstream s;
+    const std::string M = std::to_string(rd.M);
+    if (stage == 2) {
+      std::string recb = "(p.ws+" + std::to_string(K.recv_offset) + "LL)";
+      std::string pv = "((const " + t.part_t + "*)(" + recb + "+(fgt_i64)w_*" + std::to_string(K.record_bytes) + "LL+" +
+                       std::to_string(rec_off) + "LL))";
+      std::string pi = "((const fgt_i64*)(" + recb + "+(fgt_i64)w_*" + std::to_string(K.record_bytes) + "LL+" +
+                       std::to_string(rec_off + rd.M * 8) + "LL))";
+      std::string lo = rd.combine_ranks ? "0" : std::to_string(P.opt.rank);
+      std::string hi = rd.combine_ranks ? std::to_string(P.opt.world) : std::to_string(P.opt.rank + 1);
+      s << "for (int w_ = " << lo << "; w_ < " << hi << "; ++w_) { ";
+      if (t.arg) s << "{ const " << t.part_t << " ov = " << pv << "[" << e << "]; const fgt_i64 oi = " << pi << "[" << e << "]; "
+                   << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
+      else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << pv << "[" << e << "]; " << comb_stmt(t, a, "ov") << " }";
+      s << " }";
+      return s.str();
+    }
+    std::string pv = "((const " + src_t + "*)(p.ws+" + std::to_string(rd.part_val) + "LL))";
+    std::string pi = "((const fgt_i64*)(p.ws+" + std::to_string(rd.part_idx) + "LL))";
+    s << "for (fgt_i64 q_ = " << (K.kind == KKind::FULLFIN ? "tid" : "0") << "; q_ < " << count << "; q_ += "
+      << (K.kind == KKind::FULLFIN ? std::to_string(K.nt) : "1") << ") { ";
+    if (t.arg) s << "{ const " << src_t << " ov = " << pv << "[q_*" << M << "LL+" << e << "]; const fgt_i64 oi = " << pi << "[q_*"
+                 << M << "LL+" << e << "]; " << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
+    else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << pv << "[q_*" << M << "LL+" << e << "]; " << comb_stmt(t, a, "ov") << " }";
+    s << " }";
+    return s.str();
+  }
+
+  std::string build_fin() {
+    nphase = 1;
+    rowsc.assign(2, {});
+    lane.assign(1, {});
+    chunkpre.assign(1, {});
+    chunkpost.assign(1, {});
+    post.assign(1, {});
+    const bool col = K.kind == KKind::COLFIN;
+    const int stage = K.fin_stage;
+    std::vector<std::string> comb, rec_write;
+    std::vector<std::pair<RedText, std::string>> accs;
+    std::vector<std::string> finals;
+    int64_t rec_off = 0;
+    for (auto& rd : K.reds) {
+      RedText t = red_text(g, rd.node, P.opt.accumulation, CTX_FIN);
+      // partials are stored in the producer's partial type
+      const std::string src_t = red_text(g, rd.node, P.opt.accumulation, col ? CTX_COL : CTX_FULL).part_t;
+      std::string a = fresh("fa");
+      comb.push_back(t.fin_t + " " + a + " = " + t.ident + ";");
+      if (t.arg) comb.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
+      comb.push_back(fin_combine(rd, t, src_t, a, col ? "e" : "0", "p.nparts", stage, rec_off));
+      accs.push_back({t, a});
+      if (stage == 1) {
+        std::string recb = "(p.ws+" + std::to_string(K.send_offset) + "LL+" + std::to_string(rec_off) + "LL)";
+        rec_write.push_back("((" + t.part_t + "*)" + recb + ")[" + (col ? "e" : "0") + "] = (" + t.part_t + ")" + a + ";");
+        if (t.arg)
+          rec_write.push_back("((fgt_i64*)(" + recb + "+" + std::to_string(rd.M * 8) + "LL))[" + (col ? "e" : "0") + "] = " + a + "i;");
+      }
+      rec_off += rd.M * 8 * (t.arg ? 2 : 1);
+      std::string fv = fresh("fin");
+      red_var[rd.node] = fv;
+      if (t.arg) finals.push_back("const fgt_i64 " + fv + " = " + a + "i;");
+      else finals.push_back("const " + vt_t(t.dt) + " " + fv + " = " + finalize(t, a, t.fin_t) + ";");
+    }
+    if (stage != 1) {
+      for (auto& st : K.stores) {
+        Map m = store_map(st);
+        std::string v = val(st.node, m, Sc{SC_LANE, 0});
+        const Node& n = g.nodes[st.node];
+        Idx A = to_linear(m, n.shape, d);
+        lane[0].push_back(ptr_of(st.node, true, st.port, st.temp_offset) + "[" + itext(A) + "] = " + st_conv(n.dt, v) + ";");
+      }
+    }
+    // FULLFIN: one CTA; strided partial combine, then a block combine.
+    std::vector<std::string> red_code;
+    if (!col && stage != 2) group_reduce(red_code, accs, 32, true, K.nt / 32, "_fin");
+    std::ostringstream o;
+    const std::string NT = std::to_string(K.nt);
+    o << args_struct();
+    o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
+    o << "  const int tid = threadIdx.x; const fgt_i64 r = 0; const bool rv = true; (void)r; (void)rv;\n";
+    put(o, kdecl, "  ");
+    if (col) {
+      o << "  const fgt_i64 NI = " << d.NI << "LL;\n";
+      o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
+      o << "    " << digits_i() << "\n";
+      put(o, comb, "    ");
+      if (stage == 1) {
+        put(o, rec_write, "    ");
+      } else {
+        put(o, finals, "    ");
+        put(o, lane[0], "    ");
+      }
+      o << "  }\n}\n";
+      return o.str();
+    }
+    o << "  const fgt_i64 e = 0; (void)e;\n";
+    if (stage == 2) {
+      o << "  if (tid != 0) return;\n";
+      put(o, comb, "  ");
+    } else {
+      put(o, comb, "  ");
+      put(o, red_code, "  ");
+      o << "  if (tid != 0) return;\n";
+    }
+    if (stage == 1) {
+      put(o, rec_write, "  ");
+    } else {
+      put(o, finals, "  ");
+      put(o, lane[0], "  ");
+    }
+    o << "}\n";
+    return o.str();
+  }
+
+  std::string build() {
+    if (row) return build_row();
+    if (elem) return build_elem();
+    return build_fin();
+  }
+};
+
+}  // namespace
+
+void generate_sources(Plan& plan) {
+  // Later kernels first: a temp that no later kernel reads is not stored.
+  std::set<int64_t> loaded;
+  for (int i = (int)plan.kernels.size() - 1; i >= 0; --i) {
+    KernelDef& k = plan.kernels[i];
+    std::vector<OutStore> keep;
+    for (auto& s : k.stores)
+      if (s.port >= 0 || loaded.count(s.temp_offset)) keep.push_back(s);
+    k.stores = keep;
+    Emitter em(plan, k, &loaded);
+    k.source = em.build();
+  }
+}
+
+}  // namespace fgt

@@ -1,0 +1,198 @@
+// fgt_device.cuh — hand-written sm_100a device library shared by every
+// specialised partition kernel.
+//
+// The kernel generator (fgt_codegen.cpp) emits one kernel per fused kernel of
+// a partition; each includes this file verbatim (NVRTC, no other headers) and
+// uses only what is defined here:
+//   - storage codecs for f16/bf16 (RNE through cvt.rn.*) and the reference's
+//     cast rules (saturating float->int with NaN -> 0, int -> narrow float
+//     rounded once, tests/backend/support/pointwise.py:239-253);
+//   - IEEE maximum/minimum (NaN wins, +0 beats -0 for max; reference
+//     tests/support/reduction_max.py:64-70) and first-occurrence, NaN-first
+//     argmax/argmin ordering (tests/test_stage2_ops.py:148-157);
+//   - 128-bit vectorised global loads/stores with an L2 evict-first hint for
+//     streamed data;
+//   - lane-group (xor butterfly) and block reductions.
+// Floating arithmetic is IEEE with no FMA contraction: kernels are compiled
+// with -fmad=false (reference: fp_contract off, src/fugatensor/_ask/gpu.py:189).
+#pragma once
+
+typedef unsigned char fgt_u8;
+typedef unsigned short fgt_u16;
+typedef unsigned int fgt_u32;
+typedef unsigned long long fgt_u64;
+typedef long long fgt_i64;
+
+#define FGT_DEV static __device__ __forceinline__
+
+// ---------------------------------------------------------------- codecs ---
+FGT_DEV float fgt_f16_to_f32(fgt_u16 h) {
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+  return f;
+}
+FGT_DEV fgt_u16 fgt_f32_to_f16(float f) {
+  fgt_u16 h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+FGT_DEV float fgt_bf16_to_f32(fgt_u16 h) { return __uint_as_float(((fgt_u32)h) << 16); }
+FGT_DEV fgt_u16 fgt_f32_to_bf16(float f) {
+  fgt_u16 h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+// Values of f16/bf16 type are carried in f32 registers, always exactly
+// representable in the narrow format: every operation rounds once.
+FGT_DEV float fgt_rnd_f16(float f) { return fgt_f16_to_f32(fgt_f32_to_f16(f)); }
+FGT_DEV float fgt_rnd_bf16(float f) { return fgt_bf16_to_f32(fgt_f32_to_bf16(f)); }
+
+// Round-to-odd f32 image of an integer: narrow rounding of it afterwards is a
+// single correct rounding (the narrow formats keep <= 11 significand bits).
+FGT_DEV float fgt_i64_to_f32_odd(fgt_i64 x) {
+  float t;
+  asm("cvt.rz.f32.s64 %0, %1;" : "=f"(t) : "l"(x));
+  fgt_i64 back;
+  asm("cvt.rzi.s64.f32 %0, %1;" : "=l"(back) : "f"(t));
+  if (back != x) t = __uint_as_float(__float_as_uint(t) | 1u);
+  return t;
+}
+FGT_DEV float fgt_i64_to_f16v(fgt_i64 x) { return fgt_rnd_f16(fgt_i64_to_f32_odd(x)); }
+FGT_DEV float fgt_i64_to_bf16v(fgt_i64 x) { return fgt_rnd_bf16(fgt_i64_to_f32_odd(x)); }
+
+// Round-to-odd f32 image of a double (same single-rounding argument).
+FGT_DEV float fgt_f64_to_f32_odd(double d) {
+  float t = __double2float_rz(d);
+  if ((double)t != d && t == t) t = __uint_as_float(__float_as_uint(t) | 1u);
+  return t;
+}
+
+FGT_DEV int fgt_f32_to_i32(float f) {
+  int r;
+  asm("cvt.rzi.sat.s32.f32 %0, %1;" : "=r"(r) : "f"(f));
+  return r;
+}
+FGT_DEV fgt_i64 fgt_f32_to_i64(float f) {
+  fgt_i64 r;
+  asm("cvt.rzi.sat.s64.f32 %0, %1;" : "=l"(r) : "f"(f));
+  return r;
+}
+
+// ------------------------------------------------------- IEEE extrema ------
+FGT_DEV float fgt_fmax(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return (__float_as_uint(a) & 0x80000000u) ? b : a;
+  return a > b ? a : b;
+}
+FGT_DEV float fgt_fmin(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return (__float_as_uint(a) & 0x80000000u) ? a : b;
+  return a < b ? a : b;
+}
+template <class T> FGT_DEV T fgt_imax(T a, T b) { return a > b ? a : b; }
+template <class T> FGT_DEV T fgt_imin(T a, T b) { return a < b ? a : b; }
+
+// Is (a, ia) strictly preferred over (b, ib) for argmax (MAX=true) / argmin?
+// NaN counts as the extremum; ties keep the lowest index.
+template <bool MAX> FGT_DEV bool fgt_arg_better_f(float a, fgt_i64 ia, float b, fgt_i64 ib) {
+  const bool an = a != a, bn = b != b;
+  if (an || bn) return (an && bn) ? ia < ib : an;
+  if (MAX ? a > b : a < b) return true;
+  if (MAX ? a < b : a > b) return false;
+  return ia < ib;
+}
+template <bool MAX, class T> FGT_DEV bool fgt_arg_better_i(T a, fgt_i64 ia, T b, fgt_i64 ib) {
+  if (MAX ? a > b : a < b) return true;
+  if (MAX ? a < b : a > b) return false;
+  return ia < ib;
+}
+
+// --------------------------------------------------- integer semantics ----
+// Wrapping arithmetic and the reference's floordiv/mod/shift definitions
+// (tests/support/stage2.py:36-67): division by zero gives 0; MIN // -1 = MIN.
+template <class T, class U> FGT_DEV T fgt_wrap_add(T a, T b) { return (T)((U)a + (U)b); }
+template <class T, class U> FGT_DEV T fgt_wrap_mul(T a, T b) { return (T)((U)a * (U)b); }
+template <class T> FGT_DEV T fgt_ifloordiv(T a, T b, T minv) {
+  if (b == 0) return 0;
+  if (a == minv && b == (T)-1) return minv;
+  T q = a / b;
+  if ((a % b != 0) && ((a < 0) != (b < 0))) q -= 1;
+  return q;
+}
+template <class T> FGT_DEV T fgt_imod(T a, T b, T minv) {
+  if (b == 0) return 0;
+  if (a == minv && b == (T)-1) return 0;
+  T r = a % b;
+  if (r != 0 && ((r < 0) != (b < 0))) r += b;
+  return r;
+}
+template <class T, class U, int BITS> FGT_DEV T fgt_ishl(T a, T b) {
+  if (b < 0 || b >= BITS) return 0;
+  return (T)((U)a << b);
+}
+template <class T, int BITS> FGT_DEV T fgt_ishr(T a, T b) {
+  if (b < 0) return 0;
+  if (b >= BITS) return a < 0 ? (T)-1 : (T)0;
+  return a >> b;
+}
+template <class T, class U> FGT_DEV T fgt_ipow(T base, T e) {
+  if (e < 0) {
+    if (base == 1) return 1;
+    if (base == (T)-1) return (e & 1) ? (T)-1 : (T)1;
+    return 0;
+  }
+  U result = 1, b = (U)base;
+  while (e) {
+    if (e & 1) result *= b;
+    b *= b;
+    e >>= 1;
+  }
+  return (T)result;
+}
+FGT_DEV float fgt_ffloordiv(float a, float b) { return floorf(__fdiv_rn(a, b)); }
+FGT_DEV float fgt_fmod_py(float a, float b) {
+  float r = fmodf(a, b);
+  if (r != 0.0f && ((r < 0.0f) != (b < 0.0f))) r = __fadd_rn(r, b);
+  return r;
+}
+
+// ------------------------------------------------------ vector memory -----
+// 16-byte vector accesses. Streamed inputs are read once: evict-first keeps
+// them from displacing reused data (broadcast operands, partials) in L2.
+template <int BYTES> struct fgt_vec_t;
+template <> struct fgt_vec_t<16> { typedef uint4 type; };
+template <> struct fgt_vec_t<8> { typedef uint2 type; };
+template <> struct fgt_vec_t<4> { typedef unsigned int type; };
+template <> struct fgt_vec_t<2> { typedef unsigned short type; };
+template <> struct fgt_vec_t<1> { typedef unsigned char type; };
+
+template <class T, int N> FGT_DEV void fgt_vload(T (&dst)[N], const T* __restrict__ src) {
+  typedef typename fgt_vec_t<sizeof(T) * N>::type V;
+  union { V v; T e[N]; } u;
+  u.v = __ldcs(reinterpret_cast<const V*>(src));
+#pragma unroll
+  for (int k = 0; k < N; ++k) dst[k] = u.e[k];
+}
+template <class T, int N> FGT_DEV void fgt_vload_keep(T (&dst)[N], const T* __restrict__ src) {
+  typedef typename fgt_vec_t<sizeof(T) * N>::type V;
+  union { V v; T e[N]; } u;
+  u.v = __ldg(reinterpret_cast<const V*>(src));
+#pragma unroll
+  for (int k = 0; k < N; ++k) dst[k] = u.e[k];
+}
+template <class T, int N> FGT_DEV void fgt_vstore(T* __restrict__ dst, const T (&src)[N]) {
+  typedef typename fgt_vec_t<sizeof(T) * N>::type V;
+  union { V v; T e[N]; } u;
+#pragma unroll
+  for (int k = 0; k < N; ++k) u.e[k] = src[k];
+  __stcs(reinterpret_cast<V*>(dst), u.v);
+}
+
+// ------------------------------------------------------- shuffles ---------
+FGT_DEV float fgt_shfl_xor(float v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+FGT_DEV double fgt_shfl_xor(double v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+FGT_DEV int fgt_shfl_xor(int v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+FGT_DEV fgt_i64 fgt_shfl_xor(fgt_i64 v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+FGT_DEV bool fgt_shfl_xor(bool v, int m) { return __shfl_xor_sync(0xffffffffu, (int)v, m) != 0; }

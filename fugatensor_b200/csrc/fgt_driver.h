@@ -1,0 +1,70 @@
+// fgt_driver.h — the CUDA driver entry points the runtime uses, opened with
+// dlopen on first use. The library therefore loads (and plans / compiles
+// partitions with NVRTC) on machines without a GPU driver; only launching
+// needs libcuda. Same approach as the reference's driver shim
+// (cpp/cuda_driver_api.h:35-98).
+#pragma once
+
+#include <cuda.h>
+#include <dlfcn.h>
+
+#include <mutex>
+#include <string>
+
+namespace fgt {
+
+struct Driver {
+  bool ok = false;
+  std::string err;
+  CUresult (*Init)(unsigned int) = nullptr;
+  CUresult (*GetErrorName)(CUresult, const char**) = nullptr;
+  CUresult (*GetErrorString)(CUresult, const char**) = nullptr;
+  CUresult (*CtxGetCurrent)(CUcontext*) = nullptr;
+  CUresult (*CtxSetCurrent)(CUcontext) = nullptr;
+  CUresult (*CtxGetDevice)(CUdevice*) = nullptr;
+  CUresult (*DeviceGet)(CUdevice*, int) = nullptr;
+  CUresult (*DeviceGetAttribute)(int*, CUdevice_attribute, CUdevice) = nullptr;
+  CUresult (*DevicePrimaryCtxRetain)(CUcontext*, CUdevice) = nullptr;
+  CUresult (*ModuleLoadData)(CUmodule*, const void*) = nullptr;
+  CUresult (*ModuleUnload)(CUmodule) = nullptr;
+  CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
+  CUresult (*OccupancyMaxActiveBlocksPerMultiprocessor)(int*, CUfunction, int, size_t) = nullptr;
+  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
+                           void**, void**) = nullptr;
+};
+
+inline Driver& drv() {
+  static Driver d;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      d.err = std::string("CUDA driver not available (libcuda.so.1): ") + dlerror();
+      return;
+    }
+    bool all = true;
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      all = all && fn != nullptr;
+    };
+    sym(d.Init, "cuInit");
+    sym(d.GetErrorName, "cuGetErrorName");
+    sym(d.GetErrorString, "cuGetErrorString");
+    sym(d.CtxGetCurrent, "cuCtxGetCurrent");
+    sym(d.CtxSetCurrent, "cuCtxSetCurrent");
+    sym(d.CtxGetDevice, "cuCtxGetDevice");
+    sym(d.DeviceGet, "cuDeviceGet");
+    sym(d.DeviceGetAttribute, "cuDeviceGetAttribute");
+    sym(d.DevicePrimaryCtxRetain, "cuDevicePrimaryCtxRetain");
+    sym(d.ModuleLoadData, "cuModuleLoadData");
+    sym(d.ModuleUnload, "cuModuleUnload");
+    sym(d.ModuleGetFunction, "cuModuleGetFunction");
+    sym(d.OccupancyMaxActiveBlocksPerMultiprocessor, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    sym(d.LaunchKernel, "cuLaunchKernel");
+    d.ok = all;
+    if (!all) d.err = "libcuda.so.1 lacks a required driver entry point";
+  });
+  return d;
+}
+
+}  // namespace fgt

@@ -1,0 +1,515 @@
+// fgt_runtime.cpp — the C ABI: spec creation (plan + specialise + compile),
+// launch on a caller stream, and leading-dimension sharded launches.
+//
+// Replaces, for the fused elementwise / reduction partitions, the reference's
+//   - owned-step build: ASK emit_cuda_llvm -> llc -> ptxas
+//     (src/fugatensor/_ask/gpu.py:160-216, src/fugatensor/_ask/cuda.py:185-313)
+//     here: template specialisation -> NVRTC (sm_100a, -fmad=false) -> cubin,
+//     cached on disk by content hash like the reference's IR/cubin caches
+//     (src/fugatensor/_ask/cache.py);
+//   - PreparedProgram::run / ProgramPorts::runFastCore
+//     (cpp/ask_runtime.cpp:412-463): stream-ordered cuLaunchKernel of the
+//     plan's kernels with caller-owned buffers and workspace.
+#include <nvrtc.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include "fgt_driver.h"
+#include "fgt_plan.h"
+
+extern const char* const fgt_device_library_source;  // fgt_device.cuh, embedded at build time
+
+namespace fgt {
+namespace {
+
+thread_local std::string g_last_error = "";
+
+fgt_status set_error(fgt_status s, const std::string& m) {
+  g_last_error = m;
+  return s;
+}
+
+void cu_check(CUresult r, const char* what) {
+  if (r != CUDA_SUCCESS) {
+    const char* name = nullptr;
+    const char* msg = nullptr;
+    drv().GetErrorName(r, &name);
+    drv().GetErrorString(r, &msg);
+    fail(FGT_ERR_CUDA, std::string(what) + ": " + (name ? name : "?") + " (" + (msg ? msg : "") + ")");
+  }
+}
+
+uint64_t fnv1a(const std::string& s, uint64_t h = 1469598103934665603ULL) {
+  for (unsigned char c : s) {
+    h ^= c;
+    h *= 1099511628211ULL;
+  }
+  return h;
+}
+
+std::string cache_root(const char* opt_dir) {
+  if (opt_dir && *opt_dir) return opt_dir;
+  const char* env = std::getenv("FGT_CACHE_DIR");
+  if (env && *env) return env;
+  const char* home = std::getenv("HOME");
+  return std::string(home ? home : "/tmp") + "/.cache/fgt_b200";
+}
+
+void mkdirs(const std::string& path) {
+  std::string cur;
+  for (size_t i = 0; i < path.size(); ++i) {
+    cur += path[i];
+    if (path[i] == '/' && i > 0) mkdir(cur.c_str(), 0755);
+  }
+  mkdir(path.c_str(), 0755);
+}
+
+const char* kNvrtcOptions[] = {"-arch=sm_100a", "-fmad=false", "-std=c++17", "-default-device", "-lineinfo",
+                               "-prec-div=true", "-prec-sqrt=true", "-ftz=false"};
+
+std::string compile_cubin(const std::string& name, const std::string& src, const std::string& cache_dir) {
+  int maj = 0, min = 0;
+  nvrtcVersion(&maj, &min);
+  std::string opts;
+  for (const char* o : kNvrtcOptions) opts += o, opts += ' ';
+  const std::string key = std::to_string(maj) + "." + std::to_string(min) + "|" + opts + "|" + src;
+  char hex[32];
+  std::snprintf(hex, sizeof hex, "%016llx", (unsigned long long)fnv1a(key));
+  const std::string path = cache_dir + "/" + name + "-" + hex + ".cubin";
+  {
+    std::ifstream f(path, std::ios::binary);
+    if (f) {
+      std::stringstream ss;
+      ss << f.rdbuf();
+      std::string data = ss.str();
+      if (!data.empty()) return data;
+    }
+  }
+  nvrtcProgram prog;
+  if (nvrtcCreateProgram(&prog, src.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) != NVRTC_SUCCESS)
+    fail(FGT_ERR_COMPILE, "nvrtcCreateProgram failed for " + name);
+  nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof kNvrtcOptions / sizeof kNvrtcOptions[0]), kNvrtcOptions);
+  size_t log_size = 0;
+  nvrtcGetProgramLogSize(prog, &log_size);
+  std::string log(log_size, '\0');
+  if (log_size) nvrtcGetProgramLog(prog, &log[0]);
+  if (r != NVRTC_SUCCESS) {
+    nvrtcDestroyProgram(&prog);
+    fail(FGT_ERR_COMPILE, "kernel " + name + " failed to compile: " + log);
+  }
+  size_t n = 0;
+  nvrtcGetCUBINSize(prog, &n);
+  std::string cubin(n, '\0');
+  nvrtcGetCUBIN(prog, &cubin[0]);
+  nvrtcDestroyProgram(&prog);
+  // Atomic publish: write a private file, then rename.
+  mkdirs(cache_dir);
+  const std::string tmp = path + ".tmp." + std::to_string(getpid());
+  {
+    std::ofstream f(tmp, std::ios::binary);
+    f.write(cubin.data(), (std::streamsize)cubin.size());
+  }
+  std::rename(tmp.c_str(), path.c_str());
+  return cubin;
+}
+
+// ---------------------------------------------------------------- NCCL ----
+// NCCL is opened at run time so that the process keeps whichever libnccl the
+// host framework already loaded (torch bundles its own).
+typedef int nccl_result;
+typedef void* nccl_comm;
+struct NcclApi {
+  bool ok = false;
+  std::string err;
+  nccl_result (*GetUniqueId)(void*) = nullptr;
+  nccl_result (*CommInitRank)(nccl_comm*, int, const void* /*ncclUniqueId by value*/, int) = nullptr;
+  nccl_result (*CommDestroy)(nccl_comm) = nullptr;
+  nccl_result (*AllGather)(const void*, void*, size_t, int, nccl_comm, void*) = nullptr;
+  const char* (*GetErrorString)(nccl_result) = nullptr;
+};
+
+struct UniqueId {
+  char internal[128];
+};
+typedef nccl_result (*InitRankFn)(nccl_comm*, int, UniqueId, int);
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      api.err = std::string("cannot load libnccl.so.2: ") + dlerror();
+      return;
+    }
+    api.GetUniqueId = (nccl_result(*)(void*))dlsym(h, "ncclGetUniqueId");
+    api.CommInitRank = (nccl_result(*)(nccl_comm*, int, const void*, int))dlsym(h, "ncclCommInitRank");
+    api.CommDestroy = (nccl_result(*)(nccl_comm))dlsym(h, "ncclCommDestroy");
+    api.AllGather = (nccl_result(*)(const void*, void*, size_t, int, nccl_comm, void*))dlsym(h, "ncclAllGather");
+    api.GetErrorString = (const char* (*)(nccl_result))dlsym(h, "ncclGetErrorString");
+    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.GetErrorString;
+    if (!api.ok) api.err = "libnccl.so.2 lacks a required symbol";
+  });
+  return api;
+}
+
+void nccl_check(nccl_result r, const char* what) {
+  if (r != 0) fail(FGT_ERR_NCCL, std::string(what) + ": " + nccl().GetErrorString(r));
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ spec ---
+struct LoadedModule {
+  std::vector<CUmodule> mods;
+  std::vector<CUfunction> fn;
+  std::vector<int> occupancy;  // resident CTAs per SM
+  int sms = 0;
+};
+
+}  // namespace fgt
+
+struct fgt_spec {
+  fgt::Plan plan;
+  std::vector<std::string> cubins;
+  std::mutex mu;
+  std::map<CUcontext, fgt::LoadedModule> modules;
+  std::string json;
+};
+
+struct fgt_comm {
+  fgt::nccl_comm comm = nullptr;
+  int world = 1, rank = 0;
+};
+
+namespace fgt {
+namespace {
+
+int current_sm_count() {
+  if (!drv().ok) return 0;
+  CUcontext ctx = nullptr;
+  if (drv().CtxGetCurrent(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  CUdevice dev;
+  if (drv().CtxGetDevice(&dev) != CUDA_SUCCESS) return 0;
+  int sms = 0;
+  drv().DeviceGetAttribute(&sms, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, dev);
+  return sms;
+}
+
+CUcontext ensure_context() {
+  require(drv().ok, drv().err, FGT_ERR_CUDA);
+  CUcontext ctx = nullptr;
+  CUresult r = drv().CtxGetCurrent(&ctx);
+  if (r == CUDA_ERROR_NOT_INITIALIZED) {
+    cu_check(drv().Init(0), "cuInit");
+    r = drv().CtxGetCurrent(&ctx);
+  }
+  cu_check(r, "cuCtxGetCurrent");
+  if (!ctx) {
+    CUdevice dev;
+    cu_check(drv().DeviceGet(&dev, 0), "cuDeviceGet");
+    cu_check(drv().DevicePrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain");
+    cu_check(drv().CtxSetCurrent(ctx), "cuCtxSetCurrent");
+  }
+  return ctx;
+}
+
+LoadedModule& module_for(fgt_spec* s) {
+  CUcontext ctx = ensure_context();
+  std::lock_guard<std::mutex> lock(s->mu);
+  auto it = s->modules.find(ctx);
+  if (it != s->modules.end()) return it->second;
+  LoadedModule lm;
+  CUdevice dev;
+  cu_check(drv().CtxGetDevice(&dev), "cuCtxGetDevice");
+  cu_check(drv().DeviceGetAttribute(&lm.sms, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, dev), "cuDeviceGetAttribute");
+  int major = 0;
+  cu_check(drv().DeviceGetAttribute(&major, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MAJOR, dev), "cuDeviceGetAttribute");
+  if (major != 10) fail(FGT_ERR_CUDA, "fgt kernels are built for sm_100a (B200); the current device is sm_" + std::to_string(major) + "x");
+  // One module per kernel keeps each cubin independent of the others.
+  for (size_t i = 0; i < s->plan.kernels.size(); ++i) {
+    CUmodule m;
+    cu_check(drv().ModuleLoadData(&m, s->cubins[i].data()), "cuModuleLoadData");
+    CUfunction f;
+    cu_check(drv().ModuleGetFunction(&f, m, s->plan.kernels[i].name.c_str()), "cuModuleGetFunction");
+    int occ = 1;
+    cu_check(drv().OccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, s->plan.kernels[i].nt, 0), "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    lm.mods.push_back(m);
+    lm.fn.push_back(f);
+    lm.occupancy.push_back(std::max(1, occ));
+  }
+  return s->modules.emplace(ctx, std::move(lm)).first->second;
+}
+
+struct ArgBlock {
+  std::vector<unsigned char> bytes;
+};
+
+ArgBlock make_args(const Plan& p, const void* const* inputs, void* const* outputs, void* ws, long long nparts) {
+  const int nin = std::max<int>(1, (int)p.g.input_nodes.size());
+  const int nout = std::max<int>(1, (int)p.g.outputs.size());
+  ArgBlock a;
+  a.bytes.assign((size_t)(nin + nout + 3) * 8, 0);
+  unsigned char* b = a.bytes.data();
+  for (size_t i = 0; i < p.g.input_nodes.size(); ++i) std::memcpy(b + 8 * i, &inputs[i], 8);
+  for (size_t i = 0; i < p.g.outputs.size(); ++i) std::memcpy(b + 8 * (nin + i), &outputs[i], 8);
+  std::memcpy(b + 8 * (nin + nout), &ws, 8);
+  std::memcpy(b + 8 * (nin + nout + 1), &nparts, 8);
+  return a;
+}
+
+int64_t grid_for(const KernelDef& k, const LoadedModule& lm, size_t idx) {
+  const int64_t resident = (int64_t)lm.sms * lm.occupancy[idx];
+  switch (k.kind) {
+    case KKind::ROW: {
+      int64_t groups = (k.dom.NR + k.rows_per_cta - 1) / k.rows_per_cta;
+      int64_t g = std::min(groups, resident);
+      if (k.max_ctas > 0) g = std::min(g, k.max_ctas);
+      return g;
+    }
+    case KKind::ELEM: {
+      int64_t chunks = k.dom.NI / std::max(1, k.vec);
+      int64_t need = (chunks + k.nt - 1) / k.nt;
+      int64_t g = std::min(need, resident);
+      if (k.max_ctas > 0) g = std::min(g, k.max_ctas);
+      return g;
+    }
+    case KKind::COLFIN:
+      return std::max<int64_t>(1, std::min<int64_t>((k.dom.NI + k.nt - 1) / k.nt, (int64_t)lm.sms * 4));
+    case KKind::FULLFIN:
+      return 1;
+  }
+  return 1;
+}
+
+bool empty_kernel(const KernelDef& k) {
+  if (k.kind == KKind::ELEM) return k.dom.NI == 0;
+  if (k.kind == KKind::ROW) return k.dom.NR == 0;
+  if (k.kind == KKind::COLFIN) return k.dom.NI == 0;
+  return false;
+}
+
+void check_ptr(const void* p, int64_t bytes, const std::string& what) {
+  if (bytes == 0) return;
+  require(p != nullptr, what + " is NULL");
+  require(((uintptr_t)p % 16) == 0, what + " must be 16-byte aligned");
+}
+
+void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* const* outputs, void* ws, size_t ws_bytes,
+                void* stream) {
+  const Plan& p = s->plan;
+  require((int64_t)ws_bytes >= p.workspace_bytes, "workspace of " + std::to_string(ws_bytes) + " bytes is smaller than the " +
+                                                      std::to_string(p.workspace_bytes) + " bytes the partition needs",
+          FGT_ERR_WORKSPACE);
+  if (p.workspace_bytes > 0) require(ws != nullptr && ((uintptr_t)ws % 256) == 0, "workspace must be a 256-byte aligned device buffer", FGT_ERR_WORKSPACE);
+  for (size_t i = 0; i < p.g.input_nodes.size(); ++i) {
+    const Node& n = p.g.nodes[p.g.input_nodes[i]];
+    check_ptr(inputs ? inputs[i] : nullptr, n.n() * dtype_size(n.dt), "input " + std::to_string(i));
+  }
+  for (size_t i = 0; i < p.g.outputs.size(); ++i) {
+    const Node& n = p.g.nodes[p.g.outputs[i]];
+    check_ptr(outputs ? outputs[i] : nullptr, n.n() * dtype_size(n.dt), "output " + std::to_string(i));
+  }
+  if (!p.collectives.empty()) {
+    require(comm != nullptr, "this spec reduces over the sharded dimension: launch it with fgt_spec_launch_sharded");
+    require(comm->world == p.opt.world && comm->rank == p.opt.rank, "communicator rank/world differ from the spec's shard options");
+  }
+  LoadedModule& lm = module_for(s);
+  CUstream st = (CUstream)stream;
+  std::vector<int64_t> parts(p.kernels.size(), 0);
+  for (size_t i = 0; i < p.kernels.size(); ++i) {
+    const KernelDef& k = p.kernels[i];
+    long long nparts = 0;
+    if (k.producer >= 0) nparts = parts[k.producer];
+    if (empty_kernel(k)) continue;
+    int64_t grid = grid_for(k, lm, i);
+    parts[i] = k.kind == KKind::ROW ? grid * k.rows_per_cta : grid;
+    ArgBlock a = make_args(p, inputs, outputs, ws, nparts);
+    void* params[] = {a.bytes.data()};
+    cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, 1, 1, (unsigned)k.nt, 1, 1, 0, st, params, nullptr), "cuLaunchKernel");
+    for (int c : p.collectives) {
+      if (c != (int)i) continue;
+      unsigned char* base = (unsigned char*)ws;
+      nccl_check(nccl().AllGather(base + k.send_offset, base + k.recv_offset, (size_t)k.record_bytes, /*ncclChar*/ 0,
+                                  comm->comm, stream),
+                 "ncclAllGather");
+    }
+  }
+}
+
+template <class F>
+fgt_status guarded(F&& f) {
+  try {
+    f();
+    return FGT_OK;
+  } catch (const Error& e) {
+    return set_error(e.status, e.what());
+  } catch (const std::exception& e) {
+    return set_error(FGT_ERR_INVALID, e.what());
+  }
+}
+
+fgt_status copy_out(const std::string& s, char* buffer, size_t capacity, size_t* needed) {
+  if (needed) *needed = s.size() + 1;
+  if (buffer && capacity) {
+    size_t n = std::min(capacity - 1, s.size());
+    std::memcpy(buffer, s.data(), n);
+    buffer[n] = 0;
+  }
+  return FGT_OK;
+}
+
+}  // namespace
+}  // namespace fgt
+
+using namespace fgt;
+
+extern "C" {
+
+const char* fgt_last_error(void) { return g_last_error.c_str(); }
+
+int32_t fgt_abi_version(void) { return FGT_ABI_VERSION; }
+
+fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_options* options, fgt_spec** out) {
+  if (!out) return set_error(FGT_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  return guarded([&] {
+    Graph g = build_graph(desc);
+    Options opt;
+    const char* cache_dir = nullptr;
+    if (options) {
+      require(options->accumulation == FGT_ACCUM_WIDE || options->accumulation == FGT_ACCUM_STORAGE, "unknown accumulation policy");
+      opt.accumulation = options->accumulation;
+      if (options->shard_world > 1) {
+        require(options->shard_rank >= 0 && options->shard_rank < options->shard_world, "shard_rank out of range");
+        opt.world = options->shard_world;
+        opt.rank = options->shard_rank;
+        opt.shard_inputs = options->shard_inputs;
+      }
+      cache_dir = options->cache_dir;
+    }
+    int sms = current_sm_count();
+    if (sms > 0) opt.num_sms = sms;
+    auto spec = std::make_unique<fgt_spec>();
+    spec->plan = make_plan(g, opt);
+    generate_sources(spec->plan);
+    const std::string dir = cache_root(cache_dir);
+    for (auto& k : spec->plan.kernels) {
+      std::string src = std::string(fgt_device_library_source) + "\n" + k.source;
+      spec->cubins.push_back(compile_cubin(k.name, src, dir));
+    }
+    spec->json = plan_json(spec->plan);
+    *out = spec.release();
+  });
+}
+
+void fgt_spec_destroy(fgt_spec* spec) {
+  if (!spec) return;
+  for (auto& [ctx, lm] : spec->modules) {
+    if (!drv().ok) break;
+    // Modules are released only if their context is still alive.
+    CUcontext cur = nullptr;
+    if (drv().CtxGetCurrent(&cur) == CUDA_SUCCESS && cur == ctx)
+      for (CUmodule m : lm.mods) drv().ModuleUnload(m);
+  }
+  delete spec;
+}
+
+fgt_status fgt_spec_get_info(const fgt_spec* spec, fgt_spec_info* info) {
+  if (!spec || !info) return set_error(FGT_ERR_INVALID, "spec or info is NULL");
+  info->num_inputs = (int32_t)spec->plan.g.input_nodes.size();
+  info->num_outputs = (int32_t)spec->plan.g.outputs.size();
+  info->kernel_count = (int32_t)spec->plan.kernels.size();
+  info->collective_count = (int32_t)spec->plan.collectives.size();
+  info->workspace_bytes = (size_t)spec->plan.workspace_bytes;
+  return FGT_OK;
+}
+
+fgt_status fgt_spec_port(const fgt_spec* spec, int32_t is_output, int32_t index, int32_t* dtype, int32_t* rank,
+                         int64_t* shape) {
+  if (!spec) return set_error(FGT_ERR_INVALID, "spec is NULL");
+  const Graph& g = spec->plan.g;
+  int node;
+  if (is_output) {
+    if (index < 0 || index >= (int)g.outputs.size()) return set_error(FGT_ERR_INVALID, "output port out of range");
+    node = g.outputs[index];
+  } else {
+    if (index < 0 || index >= (int)g.input_nodes.size()) return set_error(FGT_ERR_INVALID, "input port out of range");
+    node = g.input_nodes[index];
+  }
+  const Node& n = g.nodes[node];
+  if (dtype) *dtype = n.dt;
+  if (rank) *rank = n.rank();
+  if (shape)
+    for (int k = 0; k < n.rank(); ++k) shape[k] = n.shape[k];
+  return FGT_OK;
+}
+
+fgt_status fgt_spec_plan_json(const fgt_spec* spec, char* buffer, size_t capacity, size_t* needed) {
+  if (!spec) return set_error(FGT_ERR_INVALID, "spec is NULL");
+  return copy_out(spec->json, buffer, capacity, needed);
+}
+
+fgt_status fgt_spec_kernel_source(const fgt_spec* spec, int32_t index, char* buffer, size_t capacity, size_t* needed) {
+  if (!spec) return set_error(FGT_ERR_INVALID, "spec is NULL");
+  if (index < 0 || index >= (int)spec->plan.kernels.size()) return set_error(FGT_ERR_INVALID, "kernel index out of range");
+  return copy_out(spec->plan.kernels[index].source, buffer, capacity, needed);
+}
+
+fgt_status fgt_spec_launch(const fgt_spec* spec, const void* const* inputs, void* const* outputs, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!spec) return set_error(FGT_ERR_INVALID, "spec is NULL");
+  return guarded([&] { launch_all(const_cast<fgt_spec*>(spec), nullptr, inputs, outputs, workspace, workspace_bytes, stream); });
+}
+
+fgt_status fgt_comm_unique_id(uint8_t id[128]) {
+  return guarded([&] {
+    require(id != nullptr, "id is NULL");
+    require(nccl().ok, nccl().err, FGT_ERR_NCCL);
+    nccl_check(nccl().GetUniqueId(id), "ncclGetUniqueId");
+  });
+}
+
+fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, fgt_comm** out) {
+  if (!out) return set_error(FGT_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  return guarded([&] {
+    require(id != nullptr && world >= 1 && rank >= 0 && rank < world, "invalid communicator arguments");
+    require(nccl().ok, nccl().err, FGT_ERR_NCCL);
+    ensure_context();
+    auto c = std::make_unique<fgt_comm>();
+    c->world = world;
+    c->rank = rank;
+    UniqueId uid;
+    std::memcpy(uid.internal, id, 128);
+    InitRankFn init = (InitRankFn)(void*)nccl().CommInitRank;
+    nccl_check(init(&c->comm, world, uid, rank), "ncclCommInitRank");
+    *out = c.release();
+  });
+}
+
+void fgt_comm_destroy(fgt_comm* comm) {
+  if (!comm) return;
+  if (comm->comm && nccl().ok) nccl().CommDestroy(comm->comm);
+  delete comm;
+}
+
+fgt_status fgt_spec_launch_sharded(const fgt_spec* spec, fgt_comm* comm, const void* const* inputs, void* const* outputs,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (!spec) return set_error(FGT_ERR_INVALID, "spec is NULL");
+  return guarded([&] {
+    require(comm != nullptr, "communicator is NULL");
+    require(spec->plan.opt.world == comm->world, "spec was not created for this communicator's world size");
+    launch_all(const_cast<fgt_spec*>(spec), comm, inputs, outputs, workspace, workspace_bytes, stream);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,212 @@
+/*
+ * fgt.h — C ABI of the B200-native (sm_100a) backend for FugaTensor's fused
+ * elementwise / broadcast / reduction partitions.
+ *
+ * A partition is a small SSA DAG of Fuga primitives (the ops that the
+ * reference lowers to ASK "owned" kernels, src/fugatensor/lowering.py:88-111).
+ * The caller describes it with plain C structs; the library type-checks it
+ * with Fuga's typing rules (src/fugatensor/ir/tensor_rules.py,
+ * src/fugatensor/ir/primitives.py), cuts it into fused kernels, specialises a
+ * hand-written sm_100a kernel template per kernel (dtype, rank, broadcast
+ * pattern, reduce axis), compiles it once and launches it on a caller stream.
+ *
+ * Conventions (kept from the reference runtime, cpp/ask_runtime.cpp:18-24,
+ * src/fugatensor/_ask/cuda.py:118):
+ *   - dtypes bool/i32/i64/f32/f16/bf16, widths 1/4/8/4/2/2 bytes;
+ *   - every buffer is dense, contiguous, row-major; shapes are static;
+ *     0-D and empty tensors are allowed;
+ *   - buffers are caller-owned device memory; the library allocates nothing
+ *     on the launch path (scratch lives in a caller-provided workspace);
+ *   - statuses are integers; no exception crosses the ABI; the message of the
+ *     last failure on the calling thread is returned by fgt_last_error();
+ *   - validation happens before any launch; there is no CPU fallback.
+ *
+ * No torch types appear here: a cgo / ctypes / JNI caller binds this header
+ * directly.
+ */
+#ifndef FGT_H_
+#define FGT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FGT_ABI_VERSION 1
+#define FGT_MAX_RANK 8
+#define FGT_MAX_OPERANDS 3
+
+typedef int32_t fgt_status;
+enum {
+  FGT_OK = 0,
+  FGT_ERR_INVALID = 1,      /* malformed descriptor, type error, bad argument   */
+  FGT_ERR_UNSUPPORTED = 2,  /* well-formed but outside what the backend plans   */
+  FGT_ERR_COMPILE = 3,      /* kernel specialisation failed to compile          */
+  FGT_ERR_CUDA = 4,         /* a CUDA driver call failed                         */
+  FGT_ERR_NCCL = 5,         /* a collective failed or timed out                  */
+  FGT_ERR_WORKSPACE = 6     /* workspace missing or smaller than required        */
+};
+
+/* Element types; numbering is part of the ABI. */
+typedef enum fgt_dtype {
+  FGT_BOOL = 0, FGT_I32 = 1, FGT_I64 = 2, FGT_F32 = 3, FGT_F16 = 4, FGT_BF16 = 5
+} fgt_dtype;
+
+/* Opcodes: one per Fuga primitive on the path. Numbering is part of the ABI. */
+typedef enum fgt_opcode {
+  /* leaves and views */
+  FGT_OP_PARAMETER = 0,       /* attrs[0] = input port index                           */
+  FGT_OP_CONSTANT = 1,        /* rank 0; constant_bits = value in dtype's encoding     */
+  FGT_OP_SPLAT = 2,           /* rank-0 operand -> shape                               */
+  FGT_OP_RESHAPE = 3,         /* same element count, row-major relinearisation         */
+  FGT_OP_BROADCAST_IN_DIM = 4,/* attrs = dimensions (operand axis -> result axis)      */
+  FGT_OP_TRANSPOSE = 5,       /* attrs = permutation                                   */
+  FGT_OP_STOP_GRADIENT = 6,   /* identity                                              */
+  FGT_OP_IOTA = 7,            /* attrs[0] = dimension                                  */
+  FGT_OP_CAST = 8,            /* dtype conversion (saturating float->int, NaN->0)      */
+  /* binary elementwise (operands: equal shape and dtype) */
+  FGT_OP_ADD = 10, FGT_OP_MUL = 11, FGT_OP_DIV = 12, FGT_OP_MAXIMUM = 13,
+  FGT_OP_MINIMUM = 14, FGT_OP_POW = 15, FGT_OP_FLOORDIV = 16, FGT_OP_MOD = 17,
+  FGT_OP_BITWISE_AND = 18, FGT_OP_BITWISE_OR = 19, FGT_OP_BITWISE_XOR = 20,
+  FGT_OP_SHIFT_LEFT = 21, FGT_OP_SHIFT_RIGHT = 22,
+  /* unary elementwise */
+  FGT_OP_EXP = 30, FGT_OP_LOG = 31, FGT_OP_SQRT = 32, FGT_OP_SIN = 33, FGT_OP_COS = 34,
+  FGT_OP_TANH = 35, FGT_OP_ERF = 36, FGT_OP_ABS = 37, FGT_OP_FLOOR = 38, FGT_OP_CEIL = 39,
+  FGT_OP_ROUND = 40, FGT_OP_BITWISE_NOT = 41,
+  /* predicates */
+  FGT_OP_COMPARE = 50,        /* predicate field; result bool                          */
+  FGT_OP_SELECT = 51,         /* (bool cond, a, b)                                     */
+  /* reductions: attrs = sorted reduced axes (argmax/argmin: attrs[0] = axis) */
+  FGT_OP_REDUCE_SUM = 60, FGT_OP_REDUCE_MAX = 61, FGT_OP_REDUCE_MIN = 62,
+  FGT_OP_REDUCE_PROD = 63, FGT_OP_REDUCE_ANY = 64, FGT_OP_REDUCE_ALL = 65,
+  FGT_OP_ARGMAX = 66, FGT_OP_ARGMIN = 67
+} fgt_opcode;
+
+typedef enum fgt_predicate {
+  FGT_CMP_EQ = 0, FGT_CMP_NE = 1, FGT_CMP_LT = 2, FGT_CMP_LE = 3, FGT_CMP_GT = 4, FGT_CMP_GE = 5
+} fgt_predicate;
+
+/* One SSA value. Operands refer to earlier nodes (topological order). The
+ * declared dtype/shape must equal what Fuga's typing rule infers. */
+typedef struct fgt_node {
+  int32_t opcode;
+  int32_t dtype;
+  int32_t rank;
+  int32_t num_operands;
+  int64_t shape[FGT_MAX_RANK];
+  int32_t operands[FGT_MAX_OPERANDS];
+  int32_t num_attrs;
+  int64_t attrs[FGT_MAX_RANK];
+  int32_t predicate;
+  int32_t reserved;
+  uint64_t constant_bits;
+} fgt_node;
+
+typedef struct fgt_partition_desc {
+  int32_t abi_version;        /* FGT_ABI_VERSION                                       */
+  int32_t num_nodes;
+  const fgt_node* nodes;
+  int32_t num_outputs;
+  const int32_t* outputs;     /* node ids, in output-port order (repeats allowed)      */
+} fgt_partition_desc;
+
+/* How floating reductions accumulate. */
+typedef enum fgt_accumulation {
+  /* f16/bf16 sums accumulate in f32 and f32 sums in f32 spans folded into f64;
+   * the result is rounded once to the reduction's dtype (default). */
+  FGT_ACCUM_WIDE = 0,
+  /* every partial sum is rounded to the reduction's dtype, as the reference's
+   * storage-dtype reductions do (tests/test_tensor_primitives.py:184-192). */
+  FGT_ACCUM_STORAGE = 1
+} fgt_accumulation;
+
+typedef struct fgt_spec_options {
+  int32_t accumulation;       /* fgt_accumulation                                      */
+  int32_t shard_world;        /* 0/1 = unsharded; N>1 = leading-dim shard over N ranks */
+  int32_t shard_rank;
+  int32_t reserved;
+  uint64_t shard_inputs;      /* bit i set: input port i is split along dim 0          */
+  const char* cache_dir;      /* compiled-kernel disk cache (NULL: FGT_CACHE_DIR env)  */
+} fgt_spec_options;
+
+typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
+typedef struct fgt_comm fgt_comm;   /* opaque: one rank of an NCCL communicator   */
+
+typedef struct fgt_spec_info {
+  int32_t num_inputs;
+  int32_t num_outputs;
+  int32_t kernel_count;       /* launches per fgt_spec_launch (collectives excluded)  */
+  int32_t collective_count;   /* NCCL calls per sharded launch                        */
+  size_t workspace_bytes;     /* scratch the caller must pass (256-byte aligned)      */
+} fgt_spec_info;
+
+/* Last error message of the calling thread (never NULL). */
+const char* fgt_last_error(void);
+
+/* ABI version of the loaded library. */
+int32_t fgt_abi_version(void);
+
+/* Type-check, plan, specialise and compile a partition.
+ * Replaces the CUDA branch of Engine._compile (src/fugatensor/engine.py:344-353):
+ * ASK partition (cpp/compiler.cpp:44-48, src/fugatensor/_ask/gpu.py:71) and the
+ * owned-step LLVM->cubin build (src/fugatensor/_ask/gpu.py:160-216,
+ * src/fugatensor/_ask/cuda.py:185-313). options may be NULL. */
+fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_options* options,
+                           fgt_spec** out);
+
+void fgt_spec_destroy(fgt_spec* spec);
+
+fgt_status fgt_spec_get_info(const fgt_spec* spec, fgt_spec_info* info);
+
+/* Shape/dtype of an input or output port (is_output 0/1). */
+fgt_status fgt_spec_port(const fgt_spec* spec, int32_t is_output, int32_t index,
+                         int32_t* dtype, int32_t* rank, int64_t* shape);
+
+/* Execution Plan v1 JSON (src/fugatensor/_ask/plan.py:21-86) of the launch plan,
+ * plus a cuda_lowering report. Copies at most capacity bytes (NUL-terminated);
+ * *needed receives the full length + 1. */
+fgt_status fgt_spec_plan_json(const fgt_spec* spec, char* buffer, size_t capacity, size_t* needed);
+
+/* Generated CUDA source of kernel `index` (diagnostics; same copy contract). */
+fgt_status fgt_spec_kernel_source(const fgt_spec* spec, int32_t index, char* buffer,
+                                  size_t capacity, size_t* needed);
+
+/* Launch every kernel of the partition on `stream` (a cudaStream_t/CUstream,
+ * NULL = legacy default stream), in stream order, asynchronously.
+ * Replaces ProgramPorts::runFastCore -> PreparedProgram::run
+ * (cpp/ask_runtime.cpp:412-463) and the cache-hit dispatch at
+ * cpp/lazy.cpp:946-948. inputs/outputs are device pointers in port order;
+ * workspace must hold fgt_spec_info.workspace_bytes (may be NULL when 0).
+ * Outputs may alias each other when the partition repeats a node; they must
+ * not overlap inputs. Capturable in a CUDA graph. */
+fgt_status fgt_spec_launch(const fgt_spec* spec, const void* const* inputs, void* const* outputs,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- leading-dimension sharding across GPUs (one process per GPU) ------- */
+
+/* 128-byte NCCL unique id, created on one rank and shared by the caller. */
+fgt_status fgt_comm_unique_id(uint8_t id[128]);
+
+/* Join a communicator of `world` ranks on the current device. No reference
+ * counterpart: the reference binds one Engine to one device
+ * (src/fugatensor/engine.py:145,237-239). */
+fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, fgt_comm** out);
+
+void fgt_comm_destroy(fgt_comm* comm);
+
+/* Sharded launch of a spec created with options.shard_world == world of comm.
+ * inputs flagged in shard_inputs hold this rank's contiguous dim-0 slab; other
+ * inputs are replicated. Row-local outputs are this rank's slab; outputs that
+ * reduce over the sharded dimension are combined across ranks (NCCL
+ * all-gather of per-rank partials + an ordered on-device combine) and are
+ * replicated, identical on every rank. */
+fgt_status fgt_spec_launch_sharded(const fgt_spec* spec, fgt_comm* comm, const void* const* inputs,
+                                   void* const* outputs, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FGT_H_ */

@@ -1,0 +1,595 @@
+/*
+ * fgt_oracle.c — TEST INFRASTRUCTURE ONLY: a CPU restatement of the
+ * reference's semantics for fused elementwise / broadcast / reduction
+ * partitions, used as the parity checker and as the timed CPU baseline.
+ * Nothing in the product (fugatensor_b200/) links, imports or calls it.
+ *
+ * The reference evaluates these partitions through the external ASK SDK
+ * 0.1.0 (CMakeLists.txt:15), which is not in the reference tree; its CPU JIT
+ * (src/fugatensor/backends/host.py:239-264) cannot be built or run here.
+ * This file restates the semantics the reference's own tests pin, per op:
+ *   - every IR-visible op rounds to its result dtype; f16/bf16 arithmetic is
+ *     f32 arithmetic rounded once (RNE, subnormals, overflow -> inf)
+ *     (src/fugatensor/_ask/numerics.py:28-78, tests/backend/support/pointwise.py:147-200);
+ *   - no FMA contraction (tests/backend/test_host_compiler.py:127-138);
+ *   - casts: float->int saturating with NaN -> 0 and truncation, x->bool is
+ *     x != 0 (tests/backend/support/pointwise.py:239-253);
+ *   - integer arithmetic wraps; floordiv/mod/shift per tests/support/stage2.py:36-67;
+ *   - reduce_max/min are IEEE: NaN propagates, +0 beats -0 for max
+ *     (tests/support/reduction_max.py:64-70);
+ *   - argmax/argmin: first occurrence, NaN counts as the extremum, i64
+ *     (tests/test_stage2_ops.py:148-157, src/fugatensor/ir/tensor_rules.py:95-108);
+ *   - reduce_sum in mode LITERAL accumulates left to right in the storage
+ *     dtype (tests/test_tensor_primitives.py:184-192); in mode ACCURATE it
+ *     accumulates in f64 and rounds once (the definition used to check the
+ *     large configurations, where the literal order is not pinned).
+ * Transcendentals use the C library's f32 functions (expf, logf, ...).
+ */
+#include <float.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../include/fgt.h"
+
+#define MODE_LITERAL 0
+#define MODE_ACCURATE 1
+
+typedef struct {
+  int dt;
+  int rank;
+  int64_t shape[FGT_MAX_RANK];
+  int64_t n;
+  void* v; /* bool: uint8, i32: int32, i64: int64, floats: float (exact value) */
+} Buf;
+
+static int is_float(int dt) { return dt == FGT_F32 || dt == FGT_F16 || dt == FGT_BF16; }
+static size_t vsize(int dt) {
+  switch (dt) {
+    case FGT_BOOL: return 1;
+    case FGT_I32: return 4;
+    case FGT_I64: return 8;
+    default: return 4;
+  }
+}
+
+/* ------------------------------------------------------------ rounding -- */
+/* Round an exact long double (64-bit significand) once to a binary format
+ * with p significand bits and minimum normal exponent emin; RNE. */
+static float round_format(long double x, int p, int emin, long double maxv) {
+  if (x != x || x == 0 || isinf(x)) return (float)x;
+  int e = ilogbl(x);
+  if (e < emin) e = emin;
+  long double q = ldexpl(x, p - 1 - e);
+  q = nearbyintl(q);
+  long double r = ldexpl(q, e - (p - 1));
+  if (fabsl(r) > maxv) return x < 0 ? -INFINITY : INFINITY;
+  return (float)r;
+}
+static float rnd_dt(long double x, int dt) {
+  switch (dt) {
+    case FGT_F16: return round_format(x, 11, -14, 65504.0L);
+    case FGT_BF16: return round_format(x, 8, -126, ldexpl(255.0L, 120));
+    default: return round_format(x, 24, -126, (long double)FLT_MAX);
+  }
+}
+static float f16_decode(uint16_t h) {
+  int s = h >> 15, e = (h >> 10) & 31, f = h & 1023;
+  float v;
+  if (e == 31) v = f ? NAN : INFINITY;
+  else if (e == 0) v = ldexpf((float)f, -24);
+  else v = ldexpf((float)(f | 1024), e - 25);
+  return s ? -v : v;
+}
+static uint16_t f16_encode(float x) { /* x already exactly representable */
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  uint16_t s = (uint16_t)((u >> 16) & 0x8000);
+  if (x != x) return s | 0x7e00;
+  float a = fabsf(x);
+  if (isinf(a)) return s | 0x7c00;
+  if (a == 0) return s;
+  int e = ilogbf(a);
+  if (e < -14) return s | (uint16_t)lrintf(ldexpf(a, 24));
+  uint16_t frac = (uint16_t)lrintf(ldexpf(a, 10 - e)) & 1023;
+  return s | (uint16_t)((e + 15) << 10) | frac;
+}
+static float bf16_decode(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+static uint16_t bf16_encode(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if (x != x) return (uint16_t)((u >> 16) | 0x40);
+  return (uint16_t)(u >> 16);
+}
+
+/* ----------------------------------------------------------- helpers ----- */
+static int64_t numel(const int64_t* s, int r) {
+  int64_t n = 1;
+  for (int i = 0; i < r; ++i) n *= s[i];
+  return n;
+}
+static void strides(const int64_t* s, int r, int64_t* st) {
+  int64_t a = 1;
+  for (int i = r - 1; i >= 0; --i) {
+    st[i] = a;
+    a *= s[i];
+  }
+}
+static void unravel(int64_t lin, const int64_t* s, int r, int64_t* c) {
+  for (int i = r - 1; i >= 0; --i) {
+    if (s[i]) {
+      c[i] = lin % s[i];
+      lin /= s[i];
+    } else c[i] = 0;
+  }
+}
+
+/* value access as long double (numeric) */
+static long double getf(const Buf* b, int64_t i) {
+  switch (b->dt) {
+    case FGT_BOOL: return ((uint8_t*)b->v)[i];
+    case FGT_I32: return ((int32_t*)b->v)[i];
+    case FGT_I64: return ((int64_t*)b->v)[i];
+    default: return ((float*)b->v)[i];
+  }
+}
+static int64_t geti(const Buf* b, int64_t i) {
+  switch (b->dt) {
+    case FGT_BOOL: return ((uint8_t*)b->v)[i];
+    case FGT_I32: return ((int32_t*)b->v)[i];
+    default: return ((int64_t*)b->v)[i];
+  }
+}
+
+static float fmax_ieee(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return signbit(a) ? b : a;
+  return a > b ? a : b;
+}
+static float fmin_ieee(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return signbit(a) ? a : b;
+  return a < b ? a : b;
+}
+
+static int64_t wrap(int64_t v, int dt) { return dt == FGT_I32 ? (int64_t)(int32_t)(uint32_t)(uint64_t)v : v; }
+static int64_t iminv(int dt) { return dt == FGT_I32 ? INT32_MIN : INT64_MIN; }
+static int bits_of(int dt) { return dt == FGT_I32 ? 32 : 64; }
+
+static int64_t ifloordiv(int64_t a, int64_t b, int dt) {
+  if (b == 0) return 0;
+  if (a == iminv(dt) && b == -1) return iminv(dt);
+  int64_t q = a / b;
+  if ((a % b != 0) && ((a < 0) != (b < 0))) q -= 1;
+  return q;
+}
+static int64_t imod(int64_t a, int64_t b, int dt) {
+  if (b == 0) return 0;
+  if (a == iminv(dt) && b == -1) return 0;
+  int64_t r = a % b;
+  if (r != 0 && ((r < 0) != (b < 0))) r += b;
+  return r;
+}
+static int64_t ipow(int64_t base, int64_t e, int dt) {
+  if (e < 0) {
+    if (base == 1) return 1;
+    if (base == -1) return (e & 1) ? -1 : 1;
+    return 0;
+  }
+  uint64_t r = 1, b = (uint64_t)base;
+  while (e) {
+    if (e & 1) r *= b;
+    b *= b;
+    e >>= 1;
+  }
+  return wrap((int64_t)r, dt);
+}
+
+static void seterr(char* err, size_t cap, const char* m) {
+  if (err && cap) snprintf(err, cap, "%s", m);
+}
+
+/* --------------------------------------------------------------- eval ---- */
+static float f_unary(int op, float a) {
+  switch (op) {
+    case FGT_OP_EXP: return expf(a);
+    case FGT_OP_LOG: return logf(a);
+    case FGT_OP_SQRT: return sqrtf(a);
+    case FGT_OP_SIN: return sinf(a);
+    case FGT_OP_COS: return cosf(a);
+    case FGT_OP_TANH: return tanhf(a);
+    case FGT_OP_ERF: return erff(a);
+    case FGT_OP_ABS: return fabsf(a);
+    case FGT_OP_FLOOR: return floorf(a);
+    case FGT_OP_CEIL: return ceilf(a);
+    case FGT_OP_ROUND: return nearbyintf(a);
+  }
+  return NAN;
+}
+static float f_binary(int op, float a, float b) {
+  switch (op) {
+    case FGT_OP_ADD: return a + b;
+    case FGT_OP_MUL: return a * b;
+    case FGT_OP_DIV: return a / b;
+    case FGT_OP_MAXIMUM: return fmax_ieee(a, b);
+    case FGT_OP_MINIMUM: return fmin_ieee(a, b);
+    case FGT_OP_POW: return powf(a, b);
+    case FGT_OP_FLOORDIV: return floorf(a / b);
+    case FGT_OP_MOD: {
+      float r = fmodf(a, b);
+      if (r != 0.0f && ((r < 0.0f) != (b < 0.0f))) r = r + b;
+      return r;
+    }
+  }
+  return NAN;
+}
+static int64_t i_binary(int op, int64_t a, int64_t b, int dt) {
+  switch (op) {
+    case FGT_OP_ADD: return wrap((int64_t)((uint64_t)a + (uint64_t)b), dt);
+    case FGT_OP_MUL: return wrap((int64_t)((uint64_t)a * (uint64_t)b), dt);
+    case FGT_OP_MAXIMUM: return a > b ? a : b;
+    case FGT_OP_MINIMUM: return a < b ? a : b;
+    case FGT_OP_POW: return ipow(a, b, dt);
+    case FGT_OP_FLOORDIV: return ifloordiv(a, b, dt);
+    case FGT_OP_MOD: return imod(a, b, dt);
+    case FGT_OP_BITWISE_AND: return a & b;
+    case FGT_OP_BITWISE_OR: return a | b;
+    case FGT_OP_BITWISE_XOR: return a ^ b;
+    case FGT_OP_SHIFT_LEFT:
+      if (b < 0 || b >= bits_of(dt)) return 0;
+      return wrap((int64_t)((uint64_t)a << b), dt);
+    case FGT_OP_SHIFT_RIGHT:
+      if (b < 0) return 0;
+      if (b >= bits_of(dt)) return a < 0 ? -1 : 0;
+      return a >> b;
+  }
+  return 0;
+}
+
+/* store a numeric value (already of the node's semantics) into buffer */
+static void put_int(Buf* b, int64_t i, int64_t v) {
+  switch (b->dt) {
+    case FGT_BOOL: ((uint8_t*)b->v)[i] = v != 0; break;
+    case FGT_I32: ((int32_t*)b->v)[i] = (int32_t)v; break;
+    default: ((int64_t*)b->v)[i] = v; break;
+  }
+}
+
+static void cast_one(const Buf* x, int64_t i, Buf* o, int64_t j) {
+  int from = x->dt, to = o->dt;
+  if (to == FGT_BOOL) {
+    ((uint8_t*)o->v)[j] = is_float(from) ? (((float*)x->v)[i] != 0.0f) : (geti(x, i) != 0);
+    return;
+  }
+  if (is_float(to)) {
+    long double v = is_float(from) ? (long double)((float*)x->v)[i] : (long double)geti(x, i);
+    ((float*)o->v)[j] = rnd_dt(v, to);
+    return;
+  }
+  if (is_float(from)) {
+    float f = ((float*)x->v)[i];
+    int64_t lo = iminv(to), hi = to == FGT_I32 ? INT32_MAX : INT64_MAX;
+    int64_t r;
+    if (f != f) r = 0;
+    else if (f <= (long double)lo) r = lo;
+    else if (f >= (long double)hi) r = hi;
+    else r = (int64_t)truncf(f);
+    put_int(o, j, r);
+    return;
+  }
+  put_int(o, j, wrap(geti(x, i), to));
+}
+
+static int arg_better(int is_max, int fl, long double a, int64_t ia, long double b, int64_t ib) {
+  if (fl) {
+    int an = a != a, bn = b != b;
+    if (an || bn) return (an && bn) ? ia < ib : an;
+  }
+  if (is_max ? a > b : a < b) return 1;
+  if (is_max ? a < b : a > b) return 0;
+  return ia < ib;
+}
+
+static int eval_reduce(const fgt_node* nd, const Buf* x, Buf* o, int mode) {
+  int axes[FGT_MAX_RANK] = {0};
+  int nax = 0;
+  int isred[FGT_MAX_RANK] = {0};
+  if (nd->opcode == FGT_OP_ARGMAX || nd->opcode == FGT_OP_ARGMIN) {
+    axes[0] = (int)nd->attrs[0];
+    nax = 1;
+  } else {
+    for (int k = 0; k < nd->num_attrs; ++k) axes[nax++] = (int)nd->attrs[k];
+  }
+  for (int k = 0; k < nax; ++k) isred[axes[k]] = 1;
+  int64_t xs[FGT_MAX_RANK];
+  strides(x->shape, x->rank, xs);
+  int64_t kept[FGT_MAX_RANK], red[FGT_MAX_RANK];
+  int nk = 0, nr = 0;
+  for (int k = 0; k < x->rank; ++k) {
+    if (isred[k]) red[nr++] = x->shape[k];
+    else kept[nk++] = x->shape[k];
+  }
+  int64_t nred = numel(red, nr);
+  const int op = nd->opcode;
+  const int fl = is_float(x->dt);
+  for (int64_t oi = 0; oi < o->n; ++oi) {
+    int64_t oc[FGT_MAX_RANK], rc[FGT_MAX_RANK];
+    unravel(oi, kept, nk, oc);
+    /* base offset from kept coords */
+    int64_t base = 0;
+    {
+      int t = 0;
+      for (int k = 0; k < x->rank; ++k)
+        if (!isred[k]) base += oc[t++] * xs[k];
+    }
+    long double accd = op == FGT_OP_REDUCE_PROD ? 1.0L : 0.0L;
+    float accf = op == FGT_OP_REDUCE_PROD ? 1.0f : 0.0f;
+    int64_t acci = op == FGT_OP_REDUCE_PROD ? 1 : 0;
+    int have = 0;
+    long double best = 0;
+    int64_t besti = 0;
+    float mf = 0;
+    int64_t mi = 0;
+    int bacc = op == FGT_OP_REDUCE_ALL ? 1 : 0;
+    for (int64_t ri = 0; ri < nred; ++ri) {
+      unravel(ri, red, nr, rc);
+      int64_t off = base;
+      {
+        int t = 0;
+        for (int k = 0; k < x->rank; ++k)
+          if (isred[k]) off += rc[t++] * xs[k];
+      }
+      switch (op) {
+        case FGT_OP_REDUCE_SUM:
+        case FGT_OP_REDUCE_PROD:
+          if (fl) {
+            float v = ((float*)x->v)[off];
+            if (mode == MODE_ACCURATE) accd = op == FGT_OP_REDUCE_SUM ? accd + (double)v : (long double)((double)accd * (double)v);
+            else accf = rnd_dt(op == FGT_OP_REDUCE_SUM ? (long double)(accf + v) : (long double)(accf * v), x->dt);
+          } else {
+            int64_t v = geti(x, off);
+            acci = wrap(op == FGT_OP_REDUCE_SUM ? (int64_t)((uint64_t)acci + (uint64_t)v) : (int64_t)((uint64_t)acci * (uint64_t)v), x->dt);
+          }
+          break;
+        case FGT_OP_REDUCE_MAX:
+        case FGT_OP_REDUCE_MIN:
+          if (fl) {
+            float v = ((float*)x->v)[off];
+            mf = !have ? v : (op == FGT_OP_REDUCE_MAX ? fmax_ieee(mf, v) : fmin_ieee(mf, v));
+          } else {
+            int64_t v = geti(x, off);
+            mi = !have ? v : (op == FGT_OP_REDUCE_MAX ? (v > mi ? v : mi) : (v < mi ? v : mi));
+          }
+          have = 1;
+          break;
+        case FGT_OP_REDUCE_ANY: bacc = bacc || ((uint8_t*)x->v)[off]; break;
+        case FGT_OP_REDUCE_ALL: bacc = bacc && ((uint8_t*)x->v)[off]; break;
+        case FGT_OP_ARGMAX:
+        case FGT_OP_ARGMIN: {
+          long double v = getf(x, off);
+          if (!have || arg_better(op == FGT_OP_ARGMAX, fl, v, rc[0], best, besti)) {
+            best = v;
+            besti = rc[0];
+          }
+          have = 1;
+          break;
+        }
+      }
+    }
+    switch (op) {
+      case FGT_OP_REDUCE_SUM:
+      case FGT_OP_REDUCE_PROD:
+        if (fl) ((float*)o->v)[oi] = mode == MODE_ACCURATE ? rnd_dt((long double)(double)accd, x->dt) : accf;
+        else put_int(o, oi, acci);
+        break;
+      case FGT_OP_REDUCE_MAX:
+      case FGT_OP_REDUCE_MIN:
+        if (fl) ((float*)o->v)[oi] = mf;
+        else put_int(o, oi, mi);
+        break;
+      case FGT_OP_REDUCE_ANY:
+      case FGT_OP_REDUCE_ALL: ((uint8_t*)o->v)[oi] = (uint8_t)bacc; break;
+      default: ((int64_t*)o->v)[oi] = besti; break;
+    }
+  }
+  return 0;
+}
+
+static void load_input(Buf* b, const void* src) {
+  for (int64_t i = 0; i < b->n; ++i) {
+    switch (b->dt) {
+      case FGT_BOOL: ((uint8_t*)b->v)[i] = ((const uint8_t*)src)[i] != 0; break;
+      case FGT_I32: ((int32_t*)b->v)[i] = ((const int32_t*)src)[i]; break;
+      case FGT_I64: ((int64_t*)b->v)[i] = ((const int64_t*)src)[i]; break;
+      case FGT_F32: ((float*)b->v)[i] = ((const float*)src)[i]; break;
+      case FGT_F16: ((float*)b->v)[i] = f16_decode(((const uint16_t*)src)[i]); break;
+      case FGT_BF16: ((float*)b->v)[i] = bf16_decode(((const uint16_t*)src)[i]); break;
+    }
+  }
+}
+static void store_output(const Buf* b, void* dst) {
+  for (int64_t i = 0; i < b->n; ++i) {
+    switch (b->dt) {
+      case FGT_BOOL: ((uint8_t*)dst)[i] = ((uint8_t*)b->v)[i]; break;
+      case FGT_I32: ((int32_t*)dst)[i] = ((int32_t*)b->v)[i]; break;
+      case FGT_I64: ((int64_t*)dst)[i] = ((int64_t*)b->v)[i]; break;
+      case FGT_F32: ((float*)dst)[i] = ((float*)b->v)[i]; break;
+      case FGT_F16: ((uint16_t*)dst)[i] = f16_encode(((float*)b->v)[i]); break;
+      case FGT_BF16: ((uint16_t*)dst)[i] = bf16_encode(((float*)b->v)[i]); break;
+    }
+  }
+}
+
+static float const_value_f(int dt, uint64_t bits) {
+  if (dt == FGT_F32) {
+    uint32_t u = (uint32_t)bits;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+  }
+  if (dt == FGT_F16) return f16_decode((uint16_t)bits);
+  return bf16_decode((uint16_t)bits);
+}
+
+/* Evaluate a partition: mode 0 literal, 1 accurate. Returns 0 on success. */
+int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* inputs, void* const* outputs, char* err,
+                    size_t errcap) {
+  const int N = d->num_nodes;
+  Buf* B = (Buf*)calloc((size_t)N, sizeof(Buf));
+  int* last = (int*)malloc(sizeof(int) * (size_t)N);
+  if (!B || !last) {
+    seterr(err, errcap, "out of memory");
+    return 1;
+  }
+  for (int i = 0; i < N; ++i) last[i] = i;
+  for (int i = 0; i < N; ++i)
+    for (int k = 0; k < d->nodes[i].num_operands; ++k) last[d->nodes[i].operands[k]] = i;
+  for (int k = 0; k < d->num_outputs; ++k) last[d->outputs[k]] = N;
+  int rc = 0;
+  for (int i = 0; i < N && !rc; ++i) {
+    const fgt_node* nd = &d->nodes[i];
+    Buf* o = &B[i];
+    o->dt = nd->dtype;
+    o->rank = nd->rank;
+    for (int k = 0; k < nd->rank; ++k) o->shape[k] = nd->shape[k];
+    o->n = numel(o->shape, o->rank);
+    o->v = malloc((size_t)(o->n ? o->n : 1) * vsize(o->dt));
+    if (!o->v) {
+      seterr(err, errcap, "out of memory");
+      rc = 1;
+      break;
+    }
+    const Buf* a = nd->num_operands > 0 ? &B[nd->operands[0]] : NULL;
+    const Buf* b = nd->num_operands > 1 ? &B[nd->operands[1]] : NULL;
+    const Buf* c = nd->num_operands > 2 ? &B[nd->operands[2]] : NULL;
+    const int op = nd->opcode;
+    int64_t os[FGT_MAX_RANK], as[FGT_MAX_RANK], cc[FGT_MAX_RANK], xc[FGT_MAX_RANK];
+    strides(o->shape, o->rank, os);
+    switch (op) {
+      case FGT_OP_PARAMETER: load_input(o, inputs[nd->attrs[0]]); break;
+      case FGT_OP_CONSTANT:
+        if (is_float(o->dt)) ((float*)o->v)[0] = const_value_f(o->dt, nd->constant_bits);
+        else if (o->dt == FGT_I32) ((int32_t*)o->v)[0] = (int32_t)(uint32_t)nd->constant_bits;
+        else if (o->dt == FGT_I64) ((int64_t*)o->v)[0] = (int64_t)nd->constant_bits;
+        else ((uint8_t*)o->v)[0] = (nd->constant_bits & 0xff) != 0;
+        break;
+      case FGT_OP_SPLAT:
+        for (int64_t j = 0; j < o->n; ++j) memcpy((char*)o->v + j * vsize(o->dt), a->v, vsize(o->dt));
+        break;
+      case FGT_OP_RESHAPE:
+      case FGT_OP_STOP_GRADIENT: memcpy(o->v, a->v, (size_t)o->n * vsize(o->dt)); break;
+      case FGT_OP_BROADCAST_IN_DIM:
+        strides(a->shape, a->rank, as);
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, o->rank, cc);
+          int64_t off = 0;
+          for (int k = 0; k < a->rank; ++k) off += (a->shape[k] == 1 ? 0 : cc[nd->attrs[k]]) * as[k];
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)a->v + off * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      case FGT_OP_TRANSPOSE:
+        strides(a->shape, a->rank, as);
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, o->rank, cc);
+          int64_t off = 0;
+          for (int k = 0; k < o->rank; ++k) off += cc[k] * as[nd->attrs[k]];
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)a->v + off * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      case FGT_OP_IOTA:
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, o->rank, cc);
+          int64_t v = cc[nd->attrs[0]];
+          if (is_float(o->dt)) ((float*)o->v)[j] = rnd_dt((long double)v, o->dt);
+          else put_int(o, j, v);
+        }
+        break;
+      case FGT_OP_CAST:
+        for (int64_t j = 0; j < o->n; ++j) cast_one(a, j, o, j);
+        break;
+      case FGT_OP_COMPARE:
+        for (int64_t j = 0; j < o->n; ++j) {
+          int r;
+          if (is_float(a->dt)) {
+            float x = ((float*)a->v)[j], y = ((float*)b->v)[j];
+            switch (nd->predicate) {
+              case FGT_CMP_EQ: r = x == y; break;
+              case FGT_CMP_NE: r = x != y; break;
+              case FGT_CMP_LT: r = x < y; break;
+              case FGT_CMP_LE: r = x <= y; break;
+              case FGT_CMP_GT: r = x > y; break;
+              default: r = x >= y;
+            }
+          } else {
+            int64_t x = geti(a, j), y = geti(b, j);
+            switch (nd->predicate) {
+              case FGT_CMP_EQ: r = x == y; break;
+              case FGT_CMP_NE: r = x != y; break;
+              case FGT_CMP_LT: r = x < y; break;
+              case FGT_CMP_LE: r = x <= y; break;
+              case FGT_CMP_GT: r = x > y; break;
+              default: r = x >= y;
+            }
+          }
+          ((uint8_t*)o->v)[j] = (uint8_t)r;
+        }
+        break;
+      case FGT_OP_SELECT:
+        for (int64_t j = 0; j < o->n; ++j) {
+          const Buf* s = ((uint8_t*)a->v)[j] ? b : c;
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)s->v + j * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      default:
+        if (op >= FGT_OP_REDUCE_SUM && op <= FGT_OP_ARGMIN) {
+          rc = eval_reduce(nd, a, o, mode);
+        } else if (op >= FGT_OP_ADD && op <= FGT_OP_SHIFT_RIGHT) {
+          for (int64_t j = 0; j < o->n; ++j) {
+            if (is_float(o->dt)) ((float*)o->v)[j] = rnd_dt(f_binary(op, ((float*)a->v)[j], ((float*)b->v)[j]), o->dt);
+            else if (o->dt == FGT_BOOL) {
+              int x = ((uint8_t*)a->v)[j], y = ((uint8_t*)b->v)[j], r = 0;
+              if (op == FGT_OP_BITWISE_AND || op == FGT_OP_MINIMUM) r = x && y;
+              else if (op == FGT_OP_BITWISE_OR || op == FGT_OP_MAXIMUM) r = x || y;
+              else if (op == FGT_OP_BITWISE_XOR) r = x != y;
+              ((uint8_t*)o->v)[j] = (uint8_t)r;
+            } else put_int(o, j, i_binary(op, geti(a, j), geti(b, j), o->dt));
+          }
+        } else if (op >= FGT_OP_EXP && op <= FGT_OP_BITWISE_NOT) {
+          for (int64_t j = 0; j < o->n; ++j) {
+            if (is_float(o->dt)) ((float*)o->v)[j] = rnd_dt(f_unary(op, ((float*)a->v)[j]), o->dt);
+            else if (o->dt == FGT_BOOL) ((uint8_t*)o->v)[j] = !((uint8_t*)a->v)[j];
+            else if (op == FGT_OP_ABS) {
+              int64_t x = geti(a, j);
+              put_int(o, j, x < 0 ? wrap((int64_t)(0 - (uint64_t)x), o->dt) : x);
+            } else put_int(o, j, ~geti(a, j));
+          }
+        } else {
+          seterr(err, errcap, "oracle: unsupported opcode");
+          rc = 1;
+        }
+    }
+    (void)xc;
+    for (int k = 0; k < nd->num_operands; ++k) {
+      int a_id = nd->operands[k];
+      if (last[a_id] == i && B[a_id].v) {
+        free(B[a_id].v);
+        B[a_id].v = NULL;
+      }
+    }
+  }
+  if (!rc)
+    for (int k = 0; k < d->num_outputs; ++k) store_output(&B[d->outputs[k]], outputs[k]);
+  for (int i = 0; i < N; ++i) free(B[i].v);
+  free(B);
+  free(last);
+  return rc;
+}
