@@ -1,0 +1,176 @@
+"""Host-side tests (no GPU): the C ABI library, descriptor validation, planning,
+kernel specialisation (NVRTC runs without a GPU) and the Execution Plan v1 shape."""
+import ctypes
+import math
+import re
+from fractions import Fraction
+from pathlib import Path
+
+import pytest
+
+import fugatensor_b200 as ft
+from fugatensor_b200 import _fgt, ir
+from fugatensor_b200 import workloads as W
+import fugatensor_b200.nn.functional as F
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_library_exports_every_declared_symbol():
+    header = (ROOT / "include" / "fgt.h").read_text()
+    declared = set(re.findall(r"^\s*(?:fgt_status|void|const char\*|int32_t)\s+(fgt_\w+)\s*\(", header, re.M))
+    assert declared == set(_fgt.EXPORTED)
+    lib = ctypes.CDLL(str(_fgt.LIB_PATH))
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert _fgt.lib.fgt_abi_version() == ir.ABI_VERSION
+
+
+def _spec(outputs, **kw):
+    return _fgt.Spec(outputs[0].graph.descriptor(outputs), **kw)
+
+
+def test_type_errors_are_reported_before_any_launch():
+    g = ir.Graph()
+    x = g.parameter("f32", (4, 4))
+    y = g.parameter("f32", (4, 4))
+    out = g.add(x, y)
+    desc = g.descriptor([out])
+    # corrupt the declared type: the library re-infers and rejects it
+    desc._nodes[2].shape[1] = 5
+    with pytest.raises(_fgt.FgtError, match="result type must match"):
+        _fgt.Spec(desc)
+    desc = g.descriptor([out])
+    desc._nodes[2].operands[1] = 7
+    with pytest.raises(_fgt.FgtError, match="earlier nodes"):
+        _fgt.Spec(desc)
+
+
+def test_python_builder_enforces_fuga_typing():
+    g = ir.Graph()
+    x = g.parameter("f32", (2, 3))
+    with pytest.raises(TypeError):
+        g.add(x, g.parameter("f32", (3, 2)))
+    with pytest.raises(TypeError):
+        g.div(g.parameter("i32", (2,)), g.parameter("i32", (2,)))
+    with pytest.raises(ValueError):
+        g.reduce_max(g.parameter("f32", (2, 0)), (1,))
+    with pytest.raises(ValueError):
+        g.broadcast_in_dim(x, (2, 4), (0, 1))
+
+
+def test_launch_without_driver_or_with_bad_arguments_fails_loudly():
+    g = ir.Graph()
+    x = g.parameter("f32", (8,))
+    spec = _spec([g.exp(x)])
+    with pytest.raises(_fgt.FgtError):
+        spec.launch([0], [0])  # NULL buffers (or no driver): rejected, nothing runs
+
+
+def test_workspace_too_small_is_rejected():
+    g = ir.Graph()
+    x = g.parameter("f32", (1000,))
+    spec = _spec([g.reduce_sum(x, (0,))])
+    assert spec.workspace_bytes > 0
+    with pytest.raises(_fgt.FgtError, match="workspace"):
+        spec.launch([16], [16], workspace=256, workspace_bytes=spec.workspace_bytes - 1)
+
+
+def _validate_plan_v1(plan):
+    """The structural checks of the reference's validate_plan (src/fugatensor/_ask/plan.py:21-86)."""
+    assert set(plan) == {"schema_version", "kind", "inputs", "outputs", "buffers", "steps", "scheduling"}
+    assert plan["schema_version"] == 1 and plan["kind"] == "ask.cuda.execution_plan"
+    assert plan["scheduling"] == {"policy": "sequential", "stream": "session"}
+    buffers = {b["id"]: b for b in plan["buffers"]}
+    for b in plan["buffers"]:
+        assert set(b) == {"id", "shape", "element_type"} and b["element_type"] in ir.WIDTH
+    producers = dict.fromkeys(plan["inputs"])
+    for step in plan["steps"]:
+        assert set(step) == {"id", "kind", "function", "inputs", "outputs", "depends_on"}
+        assert step["kind"] == "owned"
+        assert all(n in producers for n in step["inputs"])
+        producers.update(dict.fromkeys(step["outputs"], step["id"]))
+    assert all(n in producers for n in plan["outputs"])
+    assert set(plan["inputs"]) | set(plan["outputs"]) <= set(buffers)
+
+
+EXPECTED_KERNELS = {
+    ("c1", "chain_rowsum"): ["row"],
+    ("c2", "softmax_fwd"): ["row"],
+    ("c2", "softmax_vjp"): ["row"],
+    ("c3", "rmsnorm_fwd"): ["row"],
+    ("c3", "rmsnorm_vjp"): ["row", "colfin"],
+    ("c3", "layernorm_fwd"): ["row"],
+    ("c3", "layernorm_vjp"): ["row", "colfin"],
+    ("c4", "global_reductions"): ["elem", "fullfin"],
+    ("c5", "broadcast_select"): ["row"],
+}
+
+
+@pytest.mark.parametrize("cfg,variant", sorted(EXPECTED_KERNELS))
+def test_workloads_fuse_into_one_pass(cfg, variant):
+    """Each workload is one HBM pass: one main kernel (+ a partial-combine kernel for
+    reductions across rows). The reference needs >= 3 owned steps for softmax."""
+    eng = ft.Engine("cuda:0")
+    inp = W.make_inputs(cfg, 16, 256)
+    dts = W.input_dtypes(cfg)
+    t = {k: eng.tensor(v, dtype=dts[k]) for k, v in inp.items()}
+    outs = W.build(cfg, variant, t)
+    spec, desc, leaves, roots = eng.compile(*outs)
+    kinds = [k["name"].split("_")[1] for k in spec.execution_plan["cuda_lowering"]["kernels"]]
+    assert kinds == EXPECTED_KERNELS[(cfg, variant)]
+    plan = dict(spec.execution_plan)
+    plan.pop("cuda_lowering")
+    _validate_plan_v1(plan)
+    # compiled once; a structurally equal partition hits the cache
+    t2 = {k: eng.tensor(v, dtype=dts[k]) for k, v in inp.items()}
+    eng.compile(*W.build(cfg, variant, t2))
+    assert eng.cache_info() == {"compilations": 1, "cache_hits": 1, "specializations": 1}
+
+
+def test_full_size_workloads_specialise():
+    """Planning + sm_100a compilation of every benchmark workload at its full size."""
+    eng = ft.Engine("cuda:0")
+    for cfg, variants in W.VARIANTS.items():
+        rows, cols = W.FULL[cfg]
+        for variant in variants:
+            g = ir.Graph()
+            # build via the public API on tiny placeholders, then re-trace at full size
+            dts = W.input_dtypes(cfg)
+            import torch
+            shapes = {"x": (rows, cols), "y": (rows, cols), "X": (rows, cols), "dY": (rows, cols), "gamma": (cols,),
+                      "beta": (cols,), "A": (rows, cols), "B": (rows, 1), "C": (1, cols)}
+            t = {k: ft.Tensor(eng, dts[k], shapes[k], data=torch.empty(0)) for k in dts}
+            outs = W.build(cfg, variant, t)
+            spec, *_ = eng.compile(*outs)
+            lw = spec.execution_plan["cuda_lowering"]
+            main = lw["kernels"][0]
+            if main["name"].startswith("fgt_row"):
+                assert main["streaming"] is False  # the row stays in registers
+            assert spec.kernel_count == len(EXPECTED_KERNELS[(cfg, variant)])
+
+
+def test_layer_norm_vjp_materialises_no_row_temporaries():
+    eng = ft.Engine("cuda:0")
+    inp = W.make_inputs("c3", 8, 512)
+    t = {k: eng.tensor(v, dtype="bf16") for k, v in inp.items()}
+    outs = W.build("c3", "layernorm_vjp", t)
+    spec, *_ = eng.compile(*outs)
+    assert spec.execution_plan["cuda_lowering"]["temporary_buffer_count"] == 0
+
+
+# ------------------------------------------------------------ codec KATs ---
+def test_encode_float_rne_subnormals_overflow():
+    """tests/backend/test_numerics.py:27-46 restated against the builder's codec."""
+    for dtype, step, smallest in (("f16", 2.0**-10, 2.0**-24), ("bf16", 2.0**-7, 2.0**-133), ("f32", 2.0**-23, 2.0**-149)):
+        assert ir.round_float(1 + step / 2, dtype) == 1
+        assert ir.round_float(1 + 3 * step / 2, dtype) == 1 + 2 * step
+        assert ir.round_float(smallest, dtype) == smallest
+        assert ir.round_float(smallest / 2, dtype) == 0
+        assert ir.round_float(3 * smallest / 2, dtype) == 2 * smallest
+        assert math.copysign(1, ir.round_float(-smallest / 2, dtype)) == -1
+    assert ir.round_float(2**100 + 2**76 + 1, "f32") == float(2**100 + 2**77)
+    assert ir.round_float(Fraction(1) + Fraction(1, 2**24) + Fraction(1, 2**80), "f32") == 1 + 2**-23
+    assert ir.round_float(65504, "f16") == 65504
+    with pytest.raises(ValueError):
+        ir.encode_float(65520, "f16")
