@@ -1,0 +1,452 @@
+#!/usr/bin/env python
+"""Benchmark: achieved HBM GB/s of the fused partitions on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fgt|reference]
+
+One step = the headline workload: row softmax over
+X [16384, 8192] fp32, forward partition then VJP partition (given dY), each
+one fgt kernel. ``value`` is the whole-job algorithmic bytes (inputs read
+once + outputs written once, per partition) / device time, max over ranks;
+with N GPUs every rank runs its own full batch (weak scaling, row-local
+graph, no collective). Inputs (512 MiB each) exceed the 126 MB L2, so no
+flush is needed for the headline; the per-partition table flushes L2
+between iterations for the workloads whose inputs are smaller.
+
+``--impl reference`` times the reference path's CPU semantics on the host
+cores: the reference's CPU JIT cannot be built here (external ASK SDK), so
+this is the repository's C restatement (oracle/), run on a bounded row
+sample of the same workload with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+os.environ.setdefault("FGT_CACHE_DIR", str(ROOT / "fugatensor_b200" / "_kernel_cache"))
+
+HEADLINE = ("c2", ("softmax_fwd", "softmax_vjp"), "f32")
+METRIC = "achieved HBM GB/s (fraction of 8 TB/s) per fused partition at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:  # pragma: no cover
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except (ValueError, IndexError):
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------- helpers ----
+def device_inputs(cfg, rows, cols, dtype, device, seed=0):
+    """Synthetic inputs generated on the device with the workload's distributions."""
+    import torch
+    from fugatensor_b200 import workloads as W, _fgt
+    g = torch.Generator(device=device).manual_seed(seed)
+    dts = W.input_dtypes(cfg, dtype)
+    shapes = {"x": (rows, cols), "y": (rows, cols), "X": (rows, cols), "dY": (rows, cols), "gamma": (cols,),
+              "beta": (cols,), "A": (rows, cols), "B": (rows, 1), "C": (1, cols)}
+    out = {}
+    for k, dt in dts.items():
+        shape = shapes[k]
+        if dt == "i32":
+            v = torch.randint(-1000, 1001, shape, device=device, dtype=torch.int32, generator=g)
+        elif cfg == "c1":
+            v = torch.rand(shape, device=device, generator=g) * 2 - 1
+        elif cfg == "c2" and k == "X":
+            v = torch.randn(shape, device=device, generator=g) * 2
+        elif cfg == "c3" and k == "gamma":
+            v = torch.rand(shape, device=device, generator=g) + 0.5
+        elif cfg == "c3" and k == "beta":
+            v = torch.randn(shape, device=device, generator=g) * 0.1
+        else:
+            v = torch.randn(shape, device=device, generator=g)
+        out[k] = v.to(_fgt.torch_dtype(dt)).contiguous()
+    return out
+
+
+def compile_partition(engine, cfg, variant, rows, cols, dtype, tensors):
+    """Compile one workload partition; returns (spec, ordered input tensors)."""
+    import fugatensor_b200 as ft
+    from fugatensor_b200 import workloads as W
+    dts = W.input_dtypes(cfg, dtype)
+    t = {k: ft.Tensor(engine, dts[k], tuple(v.shape), data=v) for k, v in tensors.items()}
+    outs = W.build(cfg, variant, t)
+    spec, desc, leaves, roots = engine.compile(*outs)
+    return spec, [l._data for l in leaves]
+
+
+class Launcher:
+    """Pre-bound launch of a spec on the current stream (outputs/workspace allocated once)."""
+
+    def __init__(self, spec, inputs, device):
+        import torch
+        from fugatensor_b200 import _fgt
+        self.spec = spec
+        self.inputs = inputs
+        self.outputs = [torch.empty(s, dtype=_fgt.torch_dtype(d), device=device) for d, s in spec.output_types]
+        self.ws = torch.empty(max(1, spec.workspace_bytes), dtype=torch.uint8, device=device)
+        self.in_ptrs = [t.data_ptr() for t in inputs]
+        self.out_ptrs = [t.data_ptr() for t in self.outputs]
+
+    def __call__(self, stream):
+        self.spec.launch(self.in_ptrs, self.out_ptrs, self.ws.data_ptr(), self.spec.workspace_bytes, stream)
+
+
+def flush_l2(buf):
+    buf.add_(1)  # writes 256 MiB: evicts the 126 MB L2
+
+
+# ------------------------------------------------------------------ fgt arm -
+def run_fgt(args):
+    import torch
+    import torch.distributed as dist
+    import fugatensor_b200 as ft
+    from fugatensor_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", world_size=world, rank=rank,
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    engine = ft.Engine(f"cuda:{local}")
+    stream = torch.cuda.current_stream(device)
+    cfg, variants, dtype = HEADLINE
+    rows, cols = W.FULL[cfg]
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # ---- headline: softmax fwd + VJP, device-resident inputs
+    tens = device_inputs(cfg, rows, cols, dtype, device, seed=rank)
+    launchers, bytes_step = [], 0
+    for v in variants:
+        spec, ins = compile_partition(engine, cfg, v, rows, cols, dtype, tens)
+        launchers.append(Launcher(spec, ins, device))
+        bytes_step += W.algorithmic_bytes(cfg, v, rows, cols, dtype)
+    for _ in range(args.warmup):
+        for L in launchers:
+            L(stream.cuda_stream)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(launchers) + 1)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for k in range(args.steps):
+            ev[k][0].record(stream)
+            for j, L in enumerate(launchers):
+                L(stream.cuda_stream)
+                ev[k][j + 1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    per_kernel = [sum(ev[k][j].elapsed_time(ev[k][j + 1]) for k in range(args.steps)) / args.steps
+                  for j in range(len(launchers))]
+    if world > 1:
+        t = torch.tensor([ms_total], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = world * bytes_step / (ms_step * 1e-3) / 1e9
+
+    # roofline of the dominant kernel (the VJP row kernel, 1.5 GiB per launch)
+    peak, peak_kind = measured_peak()
+    dom = max(range(len(launchers)), key=lambda j: per_kernel[j])
+    dom_bytes = W.algorithmic_bytes(cfg, variants[dom], rows, cols, dtype)
+    achieved = dom_bytes / (per_kernel[dom] * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(f"{cfg}/{variants[dom]}/{dtype}")
+
+    # ---- per-partition table (all five configs), rank 0 only at N=1
+    partitions = {}
+    if not args.skip_table and world == 1:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        for c, vs in W.VARIANTS.items():
+            for dt in (("f32", "bf16") if c == "c2" else ("f32",)):
+                r, h = W.FULL[c]
+                tt = device_inputs(c, r, h, dt, device)
+                for v in vs:
+                    spec, ins = compile_partition(engine, c, v, r, h, dt, tt)
+                    L = Launcher(spec, ins, device)
+                    for _ in range(3):
+                        L(stream.cuda_stream)
+                    times = []
+                    for _ in range(args.table_iters):
+                        flush_l2(flush)
+                        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        a.record(stream)
+                        L(stream.cuda_stream)
+                        b.record(stream)
+                        b.synchronize()
+                        times.append(a.elapsed_time(b))
+                    ms = statistics.median(times)
+                    nb = W.algorithmic_bytes(c, v, r, h, dt)
+                    partitions[f"{c}/{v}/{dt}"] = {"shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
+                                                   "frac": round(nb / ms / 1e6 / peak, 4), "kernels": spec.kernel_count,
+                                                   "elements_per_s": round(r * h / (ms * 1e-3), 1)}
+                    del L
+                del tt
+                torch.cuda.empty_cache()
+
+    # ---- e2e through the public API: pinned host -> device, evaluate, device -> host
+    e2e = None
+    if not args.skip_e2e:
+        import numpy as np
+        host = {k: v.cpu().pin_memory() for k, v in tens.items()}
+        outs_host = [torch.empty((rows, cols), dtype=torch.float32).pin_memory() for _ in variants]
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(o.numel() * o.element_size() for o in outs_host)
+
+        def e2e_step():
+            t = {k: ft.Tensor(engine, W.input_dtypes(cfg, dtype)[k], tuple(v.shape),
+                              data=v.to(device, non_blocking=True)) for k, v in host.items()}
+            y = W.build(cfg, variants[0], t)[0]
+            dx = W.build(cfg, variants[1], t)[0]
+            engine.evaluate(y)
+            engine.evaluate(dx)
+            outs_host[0].copy_(y._data, non_blocking=True)
+            outs_host[1].copy_(dx._data, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(2, min(args.steps, 5))
+        a.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n_e2e
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        e2e = {"value": round(world * bytes_step / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.cpu_threads, seconds=args.cpu_seconds)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, device-generated; BASELINE distributions)",
+        "config": {"workload": "c2 row softmax fwd + VJP, X/dY [16384, 8192] fp32 (configs[1]); per-rank full batch",
+                   "rows": rows, "cols": cols, "bytes_per_step_per_rank": bytes_step,
+                   "l2": "inputs 512 MiB each > 126 MB L2 (no flush needed); table entries flush L2 between iterations",
+                   "parallelism": f"replicated rows x{world} (row-local, no collective)"},
+        "gpu_launches": args.steps * sum(L.spec.kernel_count for L in launchers),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": f"{cfg}/{variants[dom]}/{dtype}", "peak_source": peak_kind,
+                     "kernel_ms": round(per_kernel[dom], 5)},
+        "clocks": clocks,
+        "e2e": e2e,
+        "partitions": partitions,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ CPU baseline --
+def cpu_baseline(threads=None, seconds=10.0, impl_line=False):
+    """Oracle (C restatement of the reference semantics) on a row sample of the headline."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle as O
+    import fugatensor_b200 as ft
+    from fugatensor_b200 import workloads as W, ir
+    cfg, variants, dtype = HEADLINE
+    rows, cols = W.FULL[cfg]
+    threads = threads or os.cpu_count() or 1
+    sample_rows = 256
+    inp = W.make_inputs(cfg, sample_rows, cols, dtype)
+
+    def make(variant):
+        def desc_for(r):
+            eng = ft.Engine("cuda:0")
+            import torch
+            t = {k: ft.Tensor(eng, "f32", (r, cols), data=torch.empty(0)) for k in ("X", "dY")}
+            outs = W.build(cfg, variant, t)
+            d, leaves, _ = eng.trace(*outs)
+            order = [next(k for k, v in t.items() if v is l) for l in leaves]
+            return d, order
+        return desc_for
+
+    makers = {v: make(v) for v in variants}
+    done_rows, t0 = 0, time.perf_counter()
+    nbytes = 0
+    while time.perf_counter() - t0 < seconds or done_rows == 0:
+        for v in variants:
+            mk = makers[v]
+            cache = {}
+
+            def md(r, mk=mk, cache=cache):
+                if r not in cache:
+                    cache[r] = mk(r)
+                return cache[r][0]
+
+            d0, order = mk(sample_rows)
+            arrays = [inp[k] for k in order]
+            O.evaluate_rows(md, arrays, [True] * len(arrays), mode=O.ACCURATE, threads=threads)
+            nbytes += W.algorithmic_bytes(cfg, v, sample_rows, cols, dtype)
+        done_rows += sample_rows
+    dt = time.perf_counter() - t0
+    gbs = nbytes / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{done_rows} rows x {cols} of the c2 fp32 softmax fwd+VJP workload, oracle/fgt_oracle.c "
+                      f"(accurate mode), {threads} host threads, {dt:.1f} s"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    samples = []
+    for _ in range(args.warmup):
+        cpu_baseline(threads, seconds=1.0)
+    for _ in range(args.steps):
+        samples.append(cpu_baseline(threads, seconds=max(1.0, args.cpu_seconds / max(1, args.steps))))
+    value = statistics.median(s["value"] for s in samples)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "c2 row softmax fwd + VJP, X/dY [16384, 8192] fp32 (configs[1]); row sample"},
+            "cpu_baseline": dict(samples[-1], value=value),
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference CPU JIT unbuildable here (external ASK SDK 0.1.0 absent); its semantics restated "
+                    "in oracle/fgt_oracle.c", "wall_s": round(time.perf_counter() - t0, 2)}
+    print(json.dumps(line), flush=True)
+
+
+def run_only(args):
+    """Launch one partition `iters` times (used for ncu captures on small cases)."""
+    import torch
+    import fugatensor_b200 as ft
+    from fugatensor_b200 import workloads as W
+    cfg, variant, dtype = args.only.split("/")
+    rows, cols = W.FULL[cfg]
+    rows = args.rows or rows
+    device = torch.device("cuda", 0)
+    engine = ft.Engine("cuda:0")
+    tens = device_inputs(cfg, rows, cols, dtype, device)
+    spec, ins = compile_partition(engine, cfg, variant, rows, cols, dtype, tens)
+    L = Launcher(spec, ins, device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.iters):
+        L(stream.cuda_stream)
+    torch.cuda.synchronize()
+    print(json.dumps({"only": args.only, "rows": rows, "cols": cols, "kernels": spec.kernel_count,
+                      "algorithmic_bytes": W.algorithmic_bytes(cfg, variant, rows, cols, dtype),
+                      "geometry": spec.execution_plan["cuda_lowering"]["kernels"]}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=None, help="cfg/variant/dtype: launch one partition (profiling)")
+    ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="fgt", choices=("fgt", "reference"))
+    ap.add_argument("--table-iters", type=int, default=10)
+    ap.add_argument("--skip-table", action="store_true")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--cpu-threads", type=int, default=None)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_fgt(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -146,7 +146,7 @@ class Spec:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
+        if h and lib is not None:
             lib.fgt_spec_destroy(h)
             self._h = None
 
@@ -170,7 +170,7 @@ class Comm:
         return bytes(buf)
 
     def close(self):
-        if self._h:
+        if getattr(self, "_h", None) and lib is not None:
             lib.fgt_comm_destroy(self._h)
             self._h = None
 

@@ -329,7 +329,19 @@ struct Emitter {
   int nphase = 1;
   int U = 1;
 
-  std::vector<std::string> kdecl, prosites, prolane, rowdecl, rowsites, rowend, kend;
+  std::vector<std::string> kdecl, prosites, prolane, rowdecl, rowend, kend;
+  // Streamed operands of a register-resident row: loaded for the next row
+  // while the current one is computed (software pipelining across rows).
+  struct RowSite {
+    std::string name, st, ptr;
+    Idx addr;      // contiguous: row base (element part zero); uniform: full address
+    bool uniform;
+  };
+  std::vector<RowSite> row_sites;
+  std::string site_load(const RowSite& rs, const std::string& arr, const char* rvar) {
+    if (rs.uniform) return arr + "[c] = " + rs.ptr + "[" + itext(rs.addr, "e0", rvar) + "];";
+    return "fgt_vload(" + arr + "[c], " + rs.ptr + " + " + itext(rs.addr, "e", rvar) + " + e0);";
+  }
   std::vector<std::vector<std::string>> rowsc, lane, chunkpre, chunkpost, post;
   std::vector<std::string> eload;  // ELEM: site loads (per u)
   std::map<std::string, std::string> memo;
@@ -360,22 +372,25 @@ struct Emitter {
 
   // Integer index text in the given scope. Digits collapse to r / e when the
   // coefficients follow the mixed radix (the common, vectorisable case).
-  std::string itext(const Idx& a, const char* evar = "e") {
+  // evar / rvar name the element and row linear indices the text is for; the
+  // digit variables o<k>/i<k> exist only for the current row and element, so
+  // other names get their digits by division.
+  std::string itext(const Idx& a, const char* evar = "e", const char* rvar = "r") {
     if (!a.aff) return "(" + a.code + ")";
     std::ostringstream s;
     s << "(" << a.k << "LL";
     bool prop = d.no() > 0;
-    int64_t alpha = 0;
-    for (int k = 0; k < d.no(); ++k) {
-      if (k == d.no() - 1) alpha = a.c[k];
-    }
+    int64_t alpha = d.no() ? a.c[d.no() - 1] : 0;
     for (int k = 0; k < d.no() && prop; ++k)
       if (a.c[k] != alpha * d.ow[k]) prop = false;
     if (prop) {
-      if (alpha) s << "+" << alpha << "LL*r";
+      if (alpha) s << "+" << alpha << "LL*" << rvar;
     } else {
-      for (int k = 0; k < d.no(); ++k)
-        if (a.c[k]) s << "+" << a.c[k] << "LL*o" << k;
+      for (int k = 0; k < d.no(); ++k) {
+        if (!a.c[k]) continue;
+        if (std::string(rvar) == "r") s << "+" << a.c[k] << "LL*o" << k;
+        else s << "+" << a.c[k] << "LL*((" << rvar << "/" << d.ow[k] << "LL)%" << d.od[k] << "LL)";
+      }
     }
     const int ni = (int)d.id.size();
     bool propi = ni > 0;
@@ -459,8 +474,9 @@ struct Emitter {
         if (prol) {
           prosites.push_back(ST + " " + s + "[" + vec + "]; fgt_vload_keep(" + s + ", " + ptr + " + " + base + " + e0);");
         } else if (cached) {
-          rowdecl.push_back(ST + " " + s + "[" + std::to_string(K.nch) + "][" + vec + "];");
-          rowsites.push_back("fgt_vload(" + s + "[c], " + ptr + " + " + base + " + e0);");
+          Idx b = A;
+          for (int k = 0; k < (int)d.id.size(); ++k) b.c[d.no() + k] = 0;
+          row_sites.push_back(RowSite{s, ST, ptr, b, false});
         } else if (elem) {
           eload.push_back("fgt_vload(" + s + "[u], " + ptr + " + " + base + " + e0);");
           rowdecl.push_back(ST + " " + s + "[" + std::to_string(U) + "][" + vec + "];");
@@ -484,8 +500,7 @@ struct Emitter {
         memo[key] = s;
         if (prol) prosites.push_back("const " + ST + " " + s + " = " + ptr + "[" + at + "];");
         else if (cached) {
-          rowdecl.push_back(ST + " " + s + "[" + std::to_string(K.nch) + "];");
-          rowsites.push_back(s + "[c] = " + ptr + "[" + at + "];");
+          row_sites.push_back(RowSite{s, ST, ptr, A, true});
         } else if (elem) {
           rowdecl.push_back(ST + " " + s + "[" + std::to_string(U) + "];");
           eload.push_back(s + "[u] = " + ptr + "[" + at + "];");
@@ -840,16 +855,32 @@ struct Emitter {
       put(o, prolane, "        ");
       o << "      }\n    }\n  }\n";
     }
-    o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += (fgt_i64)gridDim.x * " << RPC << ") {\n";
-    o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
-    put(o, rowdecl, "    ");
-    if (cached && !rowsites.empty()) {
-      o << "    if (rv) {\n      #pragma unroll\n      for (int c = 0; c < " << NCH << "; ++c) {\n";
-      o << "        const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      o << "        if (e0 < NI) {\n";
-      put(o, rowsites, "          ");
-      o << "        }\n      }\n    }\n";
+    // streamed row operands: current and next row (double-buffered)
+    auto site_loop = [&](std::ostringstream& os, const std::string& ind, const char* rvar, bool next) {
+      os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
+      os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      os << ind << "  if (e0 < NI) {\n";
+      for (auto& rs : row_sites) os << ind << "    " << site_load(rs, next ? rs.name + "_n" : rs.name, rvar) << "\n";
+      os << ind << "  }\n" << ind << "}\n";
+    };
+    for (auto& rs : row_sites) {
+      std::string dims = rs.uniform ? "[" + NCH + "]" : "[" + NCH + "][" + VEC + "]";
+      o << "  " << rs.st << " " << rs.name << dims << "; " << rs.st << " " << rs.name << "_n" << dims << ";\n";
     }
+    const std::string stride = "(fgt_i64)gridDim.x * " + RPC;
+    if (!row_sites.empty()) {
+      o << "  { const fgt_i64 r0_ = (fgt_i64)blockIdx.x * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
+      site_loop(o, "      ", "r0_", false);
+      o << "    }\n  }\n";
+    }
+    o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
+    o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
+    if (!row_sites.empty()) {
+      o << "    const fgt_i64 rn_ = r + " << stride << ";\n    if (rn_ < NR) {\n";
+      site_loop(o, "      ", "rn_", true);
+      o << "    }\n";
+    }
+    put(o, rowdecl, "    ");
     for (int p = 0; p < nphase; ++p) {
       put(o, rowsc[p], "    ");
       o << "    if (rv) {\n";
@@ -869,6 +900,10 @@ struct Emitter {
     }
     put(o, rowsc[nphase], "    ");
     put(o, rowend, "    ");
+    for (auto& rs : row_sites) {
+      if (rs.uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) " << rs.name << "[c] = " << rs.name << "_n[c];\n";
+      else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << VEC << "; ++v) " << rs.name << "[c][v] = " << rs.name << "_n[c][v];\n";
+    }
     o << "  }\n";
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
@@ -897,14 +932,27 @@ struct Emitter {
       kdecl.push_back(t.acc_t + " " + a + " = " + t.ident + ";");
       if (t.arg) kdecl.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
       std::string v = val(g.nodes[rd.node].args[0], rd.opmap, Sc{SC_LANE, 0});
-      if (t.arg) {
-        std::string ix = arg_index(rd);
-        if (rd.index_offset) ix = "(" + ix + "+" + std::to_string(rd.index_offset) + "LL)";
-        lane[0].push_back("{ const fgt_i64 ix = " + ix + "; " + arg_stmt(t, a, a + "i", v, "ix") + " }");
-      } else if (t.acc_t == "double") {
-        lane[0].push_back(comb_stmt(t, a, "(double)(" + v + ")"));
+      // Two-level accumulation: the VEC lanes of a chunk reduce in the value
+      // type with a 32-bit lane index, then the chunk folds into the thread
+      // accumulator (f64 sums, 64-bit indices) once per chunk.
+      const std::string la = a + "l";
+      const std::string lt = t.arg ? t.acc_t : (t.acc_t == "double" ? std::string("float") : t.acc_t);
+      const std::string lident = (t.acc_t == "double") ? (t.op == FGT_OP_REDUCE_SUM ? "0.0f" : "1.0f") : t.ident;
+      const std::string ix = arg_index(rd);
+      if (t.arg && ix == "(0LL+1LL*e)") {
+        chunkpre[0].push_back(lt + " " + la + " = " + t.ident + "; int " + la + "i = 0x7fffffff;");
+        lane[0].push_back(arg_stmt(t, la, la + "i", v, "v"));
+        std::string gi = "e0 + " + la + "i";
+        if (rd.index_offset) gi += " + " + std::to_string(rd.index_offset) + "LL";
+        chunkpost[0].push_back("{ const fgt_i64 gi = " + gi + "; " + arg_stmt(t, a, a + "i", la, "gi") + " }");
+      } else if (t.arg) {
+        std::string gx = ix;
+        if (rd.index_offset) gx = "(" + gx + "+" + std::to_string(rd.index_offset) + "LL)";
+        lane[0].push_back("{ const fgt_i64 ix = " + gx + "; " + arg_stmt(t, a, a + "i", v, "ix") + " }");
       } else {
-        lane[0].push_back(comb_stmt(t, a, v));
+        chunkpre[0].push_back(lt + " " + la + " = " + lident + ";");
+        lane[0].push_back(comb_stmt(t, la, v));
+        chunkpost[0].push_back(comb_stmt(t, a, t.acc_t == "double" ? "(double)" + la : la));
       }
       accs.push_back({t, a});
       std::string ps = "((" + t.part_t + "*)(p.ws+" + std::to_string(rd.part_val) + "LL))[blockIdx.x] = (" + t.part_t + ")" + a + ";";

@@ -96,14 +96,14 @@ template <class T> FGT_DEV T fgt_imin(T a, T b) { return a < b ? a : b; }
 
 // Is (a, ia) strictly preferred over (b, ib) for argmax (MAX=true) / argmin?
 // NaN counts as the extremum; ties keep the lowest index.
-template <bool MAX> FGT_DEV bool fgt_arg_better_f(float a, fgt_i64 ia, float b, fgt_i64 ib) {
+template <bool MAX, class I> FGT_DEV bool fgt_arg_better_f(float a, I ia, float b, I ib) {
   const bool an = a != a, bn = b != b;
   if (an || bn) return (an && bn) ? ia < ib : an;
   if (MAX ? a > b : a < b) return true;
   if (MAX ? a < b : a > b) return false;
   return ia < ib;
 }
-template <bool MAX, class T> FGT_DEV bool fgt_arg_better_i(T a, fgt_i64 ia, T b, fgt_i64 ib) {
+template <bool MAX, class T, class I> FGT_DEV bool fgt_arg_better_i(T a, I ia, T b, I ib) {
   if (MAX ? a > b : a < b) return true;
   if (MAX ? a < b : a > b) return false;
   return ia < ib;

@@ -75,6 +75,38 @@ static float rnd_dt(long double x, int dt) {
     default: return round_format(x, 24, -126, (long double)FLT_MAX);
   }
 }
+/* Fast paths for a value that is already an f32: f32 is the identity; bf16
+ * shares f32's exponent range, so RNE on the bit pattern is exact (overflow
+ * carries into the exponent and yields inf); f16 scales to an integer
+ * significand (exact power-of-two scaling) and rounds with nearbyintf (RNE). */
+static float rnd_bf16_f(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) {
+    if (u & 0x7fffffu) u |= 0x400000u;
+    memcpy(&x, &u, 4);
+    return x;
+  }
+  u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+static float rnd_f16_f(float x) {
+  if (x != x || isinf(x) || x == 0) return x;
+  float a = fabsf(x);
+  int e = ilogbf(a);
+  if (e < -14) e = -14;
+  float q = ldexpf(nearbyintf(ldexpf(a, 10 - e)), e - 10);
+  if (q > 65504.0f) q = INFINITY;
+  return x < 0 ? -q : q;
+}
+static float rnd_f(float x, int dt) {
+  if (dt == FGT_F16) return rnd_f16_f(x);
+  if (dt == FGT_BF16) return rnd_bf16_f(x);
+  return x;
+}
+
 static float f16_decode(uint16_t h) {
   int s = h >> 15, e = (h >> 10) & 31, f = h & 1023;
   float v;
@@ -354,7 +386,7 @@ static int eval_reduce(const fgt_node* nd, const Buf* x, Buf* o, int mode) {
           if (fl) {
             float v = ((float*)x->v)[off];
             if (mode == MODE_ACCURATE) accd = op == FGT_OP_REDUCE_SUM ? accd + (double)v : (long double)((double)accd * (double)v);
-            else accf = rnd_dt(op == FGT_OP_REDUCE_SUM ? (long double)(accf + v) : (long double)(accf * v), x->dt);
+            else accf = rnd_f(op == FGT_OP_REDUCE_SUM ? accf + v : accf * v, x->dt);
           } else {
             int64_t v = geti(x, off);
             acci = wrap(op == FGT_OP_REDUCE_SUM ? (int64_t)((uint64_t)acci + (uint64_t)v) : (int64_t)((uint64_t)acci * (uint64_t)v), x->dt);
@@ -554,7 +586,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
           rc = eval_reduce(nd, a, o, mode);
         } else if (op >= FGT_OP_ADD && op <= FGT_OP_SHIFT_RIGHT) {
           for (int64_t j = 0; j < o->n; ++j) {
-            if (is_float(o->dt)) ((float*)o->v)[j] = rnd_dt(f_binary(op, ((float*)a->v)[j], ((float*)b->v)[j]), o->dt);
+            if (is_float(o->dt)) ((float*)o->v)[j] = rnd_f(f_binary(op, ((float*)a->v)[j], ((float*)b->v)[j]), o->dt);
             else if (o->dt == FGT_BOOL) {
               int x = ((uint8_t*)a->v)[j], y = ((uint8_t*)b->v)[j], r = 0;
               if (op == FGT_OP_BITWISE_AND || op == FGT_OP_MINIMUM) r = x && y;
@@ -565,7 +597,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
           }
         } else if (op >= FGT_OP_EXP && op <= FGT_OP_BITWISE_NOT) {
           for (int64_t j = 0; j < o->n; ++j) {
-            if (is_float(o->dt)) ((float*)o->v)[j] = rnd_dt(f_unary(op, ((float*)a->v)[j]), o->dt);
+            if (is_float(o->dt)) ((float*)o->v)[j] = rnd_f(f_unary(op, ((float*)a->v)[j]), o->dt);
             else if (o->dt == FGT_BOOL) ((uint8_t*)o->v)[j] = !((uint8_t*)a->v)[j];
             else if (op == FGT_OP_ABS) {
               int64_t x = geti(a, j);
