@@ -67,15 +67,17 @@ FGT_DEV float fgt_f64_to_f32_odd(double d) {
   return t;
 }
 
+// Saturating truncation; NaN maps to 0 (the hardware's 64-bit conversion
+// maps NaN to the minimum, so NaN is tested explicitly for both widths).
 FGT_DEV int fgt_f32_to_i32(float f) {
   int r;
   asm("cvt.rzi.sat.s32.f32 %0, %1;" : "=r"(r) : "f"(f));
-  return r;
+  return f != f ? 0 : r;
 }
 FGT_DEV fgt_i64 fgt_f32_to_i64(float f) {
   fgt_i64 r;
   asm("cvt.rzi.sat.s64.f32 %0, %1;" : "=l"(r) : "f"(f));
-  return r;
+  return f != f ? 0 : r;
 }
 
 // ------------------------------------------------------- IEEE extrema ------
