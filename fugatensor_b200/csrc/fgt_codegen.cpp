@@ -299,6 +299,18 @@ std::string arg_stmt(const RedText& t, const std::string& a, const std::string& 
                         : std::string("fgt_arg_better_i<") + (t.is_max ? "true" : "false") + "," + vt_t(t.odt) + ">";
   return "if (" + fn + "(" + b + "," + bi + "," + a + "," + ai + ")) { " + a + " = " + b + "; " + ai + " = " + bi + "; }";
 }
+// Argmax/argmin update for a thread scanning its elements in increasing
+// index order (ties keep the earlier element without comparing indices).
+std::string scan_stmt(const RedText& t, const std::string& a, const std::string& ai, const std::string& b,
+                      const std::string& bi) {
+  std::string fn = t.fl ? std::string("fgt_arg_scan_f<") + (t.is_max ? "true" : "false") + ">"
+                        : std::string("fgt_arg_scan_i<") + (t.is_max ? "true" : "false") + "," + vt_t(t.odt) + ">";
+  // lane-local indices are int (sentinel INT_MAX), others int64 (INT64_MAX)
+  const bool local = bi == "v";
+  const std::string unset = local ? "0x7fffffff" : "9223372036854775807LL";
+  return "if (" + fn + "(" + b + "," + a + "," + ai + "," + unset + ")) { " + a + " = " + b + "; " + ai + " = " + bi + "; }";
+}
+
 // Round a finished accumulator to the reduction's result dtype (once).
 std::string finalize(const RedText& t, const std::string& acc, const std::string& acc_t) {
   if (!t.fl || t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN) return acc;
@@ -336,8 +348,19 @@ struct Emitter {
     std::string name, st, ptr;
     Idx addr;      // contiguous: row base (element part zero); uniform: full address
     bool uniform;
+    int bytes = 0;         // one thread's piece per chunk (VEC elements)
+    bool staged = false;   // copied through the shared-memory stage ring
+    int64_t smem_off = 0;  // region of this operand in the ring
   };
   std::vector<RowSite> row_sites;
+  int stages = 0;                  // shared-memory ring depth (0: register path)
+  int64_t stage_bytes = 0;         // bytes of one stage (all staged operands)
+  // Shared-memory address (bytes from the dynamic base) of a thread's piece.
+  std::string piece_off(const RowSite& rs, const std::string& stg) {
+    return "(" + std::to_string(rs.smem_off) + "u + (unsigned)((((" + stg + ") * " + std::to_string(K.rows_per_cta) +
+           " + grp) * " + std::to_string(K.nch) + " + c) * " + std::to_string(K.tpr) + " + lane) * " +
+           std::to_string(rs.bytes) + "u)";
+  }
   std::string site_load(const RowSite& rs, const std::string& arr, const char* rvar) {
     if (rs.uniform) return arr + "[c] = " + rs.ptr + "[" + itext(rs.addr, "e0", rvar) + "];";
     return "fgt_vload(" + arr + "[c], " + rs.ptr + " + " + itext(rs.addr, "e", rvar) + " + e0);";
@@ -476,7 +499,14 @@ struct Emitter {
         } else if (cached) {
           Idx b = A;
           for (int k = 0; k < (int)d.id.size(); ++k) b.c[d.no() + k] = 0;
-          row_sites.push_back(RowSite{s, ST, ptr, b, false});
+          RowSite rs{s, ST, ptr, b, false};
+          rs.bytes = K.vec * dtype_size(n.dt);
+          // cp.async moves 4, 8 or 16 bytes; a stage (one row of every staged
+          // operand) must leave room for at least two stages in 227 KB.
+          const int64_t piece = (int64_t)K.rows_per_cta * K.nch * K.tpr * rs.bytes;
+          rs.staged = (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) && stage_bytes + piece <= 100 * 1024;
+          if (rs.staged) stage_bytes += piece;
+          row_sites.push_back(rs);
         } else if (elem) {
           eload.push_back("fgt_vload(" + s + "[u], " + ptr + " + " + base + " + e0);");
           rowdecl.push_back(ST + " " + s + "[" + std::to_string(U) + "][" + vec + "];");
@@ -485,7 +515,26 @@ struct Emitter {
         }
       }
       if (prol) return ld_conv(n.dt, s + "[v]");
-      if (cached) return ld_conv(n.dt, s + "[c][v]");
+      if (cached) {
+        const RowSite* rs = nullptr;
+        for (auto& x : row_sites)
+          if (x.name == s) rs = &x;
+        if (rs && rs->staged) {
+          // read this thread's piece of the current stage once per chunk and phase
+          std::string pk = "stv|" + s + "|" + std::to_string(D.p);
+          auto pit = memo.find(pk);
+          std::string sv;
+          if (pit != memo.end()) sv = pit->second;
+          else {
+            sv = s + "_p" + std::to_string(D.p);
+            memo[pk] = sv;
+            chunkpre[D.p].push_back(ST + " " + sv + "[" + std::to_string(K.vec) + "]; fgt_lds(" + sv + ", (const " + ST +
+                                    "*)(fgt_dsmem + @OFF(" + s + ")));");
+          }
+          return ld_conv(n.dt, sv + "[v]");
+        }
+        return ld_conv(n.dt, s + "[c][v]");
+      }
       if (elem) return ld_conv(n.dt, s + "[u][v]");
       return ld_conv(n.dt, s + "[v]");
     }
@@ -771,7 +820,7 @@ struct Emitter {
       rowsc[p].push_back(t.acc_t + " " + a + " = " + t.ident + ";");
       if (t.arg) rowsc[p].push_back("fgt_i64 " + a + "i = " + t.identi + ";");
       std::string v = val(g.nodes[rd->node].args[0], rd->opmap, Sc{SC_LANE, p});
-      if (t.arg) lane[p].push_back("{ const fgt_i64 ix = " + arg_index(*rd) + "; " + arg_stmt(t, a, a + "i", v, "ix") + " }");
+      if (t.arg) lane[p].push_back("{ const fgt_i64 ix = " + arg_index(*rd) + "; " + scan_stmt(t, a, a + "i", v, "ix") + " }");
       else lane[p].push_back(comb_stmt(t, a, v));
       phase_accs[p].push_back({t, a});
       acc_of[rd->node] = a;
@@ -809,7 +858,7 @@ struct Emitter {
       if (t.arg) {
         std::string ix = arg_index(*rd);
         if (rd->index_offset) ix = "(" + ix + "+" + std::to_string(rd->index_offset) + "LL)";
-        lane[p].push_back("{ const fgt_i64 ix = " + ix + "; " + arg_stmt(t, a + "[c][v]", a + "i[c][v]", v, "ix") + " }");
+        lane[p].push_back("{ const fgt_i64 ix = " + ix + "; " + scan_stmt(t, a + "[c][v]", a + "i[c][v]", v, "ix") + " }");
       } else {
         lane[p].push_back(comb_stmt(t, a + "[c][v]", v));
       }
@@ -855,32 +904,80 @@ struct Emitter {
       put(o, prolane, "        ");
       o << "      }\n    }\n  }\n";
     }
-    // streamed row operands: current and next row (double-buffered)
+    // ---- streamed row operands
+    // (a) staged: a ring of `stages` rows in shared memory, filled with
+    //     cp.async (stages-1) rows ahead of the row being computed;
+    // (b) otherwise: registers, double-buffered one row ahead.
+    std::vector<RowSite*> staged_sites, reg_sites;
+    for (auto& rs : row_sites) (rs.staged ? staged_sites : reg_sites).push_back(&rs);
+    if (!staged_sites.empty()) {
+      stages = (int)std::min<int64_t>(4, std::max<int64_t>(2, (200 * 1024) / std::max<int64_t>(1, stage_bytes)));
+      int64_t off = 0;
+      for (auto* rs : staged_sites) {
+        rs->smem_off = off;
+        off += (int64_t)stages * K.rows_per_cta * K.nch * K.tpr * rs->bytes;
+      }
+    }
+    const std::string stride = "(fgt_i64)gridDim.x * " + RPC;
     auto site_loop = [&](std::ostringstream& os, const std::string& ind, const char* rvar, bool next) {
       os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
       os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
       os << ind << "  if (e0 < NI) {\n";
-      for (auto& rs : row_sites) os << ind << "    " << site_load(rs, next ? rs.name + "_n" : rs.name, rvar) << "\n";
+      for (auto* rs : reg_sites) os << ind << "    " << site_load(*rs, next ? rs->name + "_n" : rs->name, rvar) << "\n";
       os << ind << "  }\n" << ind << "}\n";
     };
-    for (auto& rs : row_sites) {
-      std::string dims = rs.uniform ? "[" + NCH + "]" : "[" + NCH + "][" + VEC + "]";
-      o << "  " << rs.st << " " << rs.name << dims << "; " << rs.st << " " << rs.name << "_n" << dims << ";\n";
+    auto issue = [&](std::ostringstream& os, const std::string& ind, const char* rvar, const std::string& stg) {
+      os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
+      os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      os << ind << "  if (e0 < NI) {\n";
+      for (auto* rs : staged_sites)
+        os << ind << "    fgt_cp_async<" << rs->bytes << ">(sbase_ + " << piece_off(*rs, stg) << ", " << rs->ptr << " + "
+           << itext(rs->addr, "e", rvar) << " + e0);\n";
+      os << ind << "  }\n" << ind << "}\n";
+    };
+    for (auto* rs : reg_sites) {
+      std::string dims = rs->uniform ? "[" + NCH + "]" : "[" + NCH + "][" + VEC + "]";
+      o << "  " << rs->st << " " << rs->name << dims << "; " << rs->st << " " << rs->name << "_n" << dims << ";\n";
     }
-    const std::string stride = "(fgt_i64)gridDim.x * " + RPC;
-    if (!row_sites.empty()) {
+    if (!reg_sites.empty()) {
       o << "  { const fgt_i64 r0_ = (fgt_i64)blockIdx.x * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
       site_loop(o, "      ", "r0_", false);
       o << "    }\n  }\n";
     }
+    const std::string S = std::to_string(stages);
+    if (stages) {
+      o << "  extern __shared__ __align__(16) unsigned char fgt_dsmem[];\n";
+      o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n  int stg = 0;\n";
+      o << "  for (int k_ = 0; k_ < " << stages - 1 << "; ++k_) {\n";
+      o << "    const fgt_i64 rk_ = (fgt_i64)blockIdx.x * " << RPC << " + grp + (fgt_i64)k_ * " << stride << ";\n";
+      o << "    if (rk_ < NR) {\n";
+      issue(o, "      ", "rk_", "k_");
+      o << "    }\n    fgt_cp_commit();\n  }\n";
+    }
     o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
     o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
-    if (!row_sites.empty()) {
+    if (stages) {
+      o << "    { const fgt_i64 rp_ = r + (fgt_i64)" << stages - 1 << " * " << stride << ";\n";
+      o << "      const int sp_ = stg + " << stages - 1 << " >= " << S << " ? stg - 1 : stg + " << stages - 1 << ";\n";
+      o << "      if (rp_ < NR) {\n";
+      issue(o, "        ", "rp_", "sp_");
+      o << "      }\n      fgt_cp_commit();\n    }\n";
+      o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
+    }
+    if (!reg_sites.empty()) {
       o << "    const fgt_i64 rn_ = r + " << stride << ";\n    if (rn_ < NR) {\n";
       site_loop(o, "      ", "rn_", true);
       o << "    }\n";
     }
     put(o, rowdecl, "    ");
+    // resolve the shared-memory piece offsets of staged operands
+    for (auto& list : chunkpre)
+      for (auto& stmt : list)
+        for (auto* rs : staged_sites) {
+          const std::string tag = "@OFF(" + rs->name + ")";
+          size_t pos;
+          while ((pos = stmt.find(tag)) != std::string::npos) stmt.replace(pos, tag.size(), piece_off(*rs, "stg"));
+        }
     for (int p = 0; p < nphase; ++p) {
       put(o, rowsc[p], "    ");
       o << "    if (rv) {\n";
@@ -900,11 +997,13 @@ struct Emitter {
     }
     put(o, rowsc[nphase], "    ");
     put(o, rowend, "    ");
-    for (auto& rs : row_sites) {
-      if (rs.uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) " << rs.name << "[c] = " << rs.name << "_n[c];\n";
-      else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << VEC << "; ++v) " << rs.name << "[c][v] = " << rs.name << "_n[c][v];\n";
+    for (auto* rs : reg_sites) {
+      if (rs->uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) " << rs->name << "[c] = " << rs->name << "_n[c];\n";
+      else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << VEC << "; ++v) " << rs->name << "[c][v] = " << rs->name << "_n[c][v];\n";
     }
+    if (stages) o << "    stg = stg + 1 == " << S << " ? 0 : stg + 1;\n";
     o << "  }\n";
+    if (stages) o << "  fgt_cp_wait<0>();\n";
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
@@ -941,14 +1040,14 @@ struct Emitter {
       const std::string ix = arg_index(rd);
       if (t.arg && ix == "(0LL+1LL*e)") {
         chunkpre[0].push_back(lt + " " + la + " = " + t.ident + "; int " + la + "i = 0x7fffffff;");
-        lane[0].push_back(arg_stmt(t, la, la + "i", v, "v"));
+        lane[0].push_back(scan_stmt(t, la, la + "i", v, "v"));
         std::string gi = "e0 + " + la + "i";
         if (rd.index_offset) gi += " + " + std::to_string(rd.index_offset) + "LL";
-        chunkpost[0].push_back("{ const fgt_i64 gi = " + gi + "; " + arg_stmt(t, a, a + "i", la, "gi") + " }");
+        chunkpost[0].push_back("{ const fgt_i64 gi = " + gi + "; " + scan_stmt(t, a, a + "i", la, "gi") + " }");
       } else if (t.arg) {
         std::string gx = ix;
         if (rd.index_offset) gx = "(" + gx + "+" + std::to_string(rd.index_offset) + "LL)";
-        lane[0].push_back("{ const fgt_i64 ix = " + gx + "; " + arg_stmt(t, a, a + "i", v, "ix") + " }");
+        lane[0].push_back("{ const fgt_i64 ix = " + gx + "; " + scan_stmt(t, a, a + "i", v, "ix") + " }");
       } else {
         chunkpre[0].push_back(lt + " " + la + " = " + lident + ";");
         lane[0].push_back(comb_stmt(t, la, v));
@@ -1136,6 +1235,7 @@ void generate_sources(Plan& plan) {
     k.stores = keep;
     Emitter em(plan, k, &loaded);
     k.source = em.build();
+    k.smem_bytes = (int64_t)em.stages * em.stage_bytes;
   }
 }
 

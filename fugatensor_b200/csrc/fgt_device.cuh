@@ -192,6 +192,38 @@ template <class T, int N> FGT_DEV void fgt_vstore(T* __restrict__ dst, const T (
   __stcs(reinterpret_cast<V*>(dst), u.v);
 }
 
+// --------------------------------------------- shared-memory row staging ---
+// Streamed row operands are copied global -> shared with cp.async in a ring of
+// stages, several rows ahead of the row being computed. Every thread copies
+// and later reads back only its own pieces, so completion is tracked per
+// thread (cp.async.wait_group) and no block barrier is involved; data in
+// flight occupies shared memory, not registers.
+FGT_DEV unsigned fgt_smem_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+template <int BYTES> FGT_DEV void fgt_cp_async(unsigned dst, const void* src) {
+  if (BYTES == 16) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+  else asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(dst), "l"(src), "n"(BYTES) : "memory");
+}
+FGT_DEV void fgt_cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> FGT_DEV void fgt_cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+template <class T, int N> FGT_DEV void fgt_lds(T (&dst)[N], const T* src) {
+  typedef typename fgt_vec_t<sizeof(T) * N>::type V;
+  union { V v; T e[N]; } u;
+  u.v = *reinterpret_cast<const V*>(src);
+#pragma unroll
+  for (int k = 0; k < N; ++k) dst[k] = u.e[k];
+}
+
+// Ascending-order scans (a thread visits its elements in increasing index):
+// a later element replaces the running extremum only if strictly better, or
+// if it is the first NaN. Equivalent to fgt_arg_better_* for such scans.
+// `unset` is the sentinel index of an accumulator that holds no element yet.
+template <bool MAX, class I> FGT_DEV bool fgt_arg_scan_f(float v, float best, I bi, I unset) {
+  return bi == unset || (MAX ? v > best : v < best) || (v != v && best == best);
+}
+template <bool MAX, class T, class I> FGT_DEV bool fgt_arg_scan_i(T v, T best, I bi, I unset) {
+  return bi == unset || (MAX ? v > best : v < best);
+}
+
 // ------------------------------------------------------- shuffles ---------
 FGT_DEV float fgt_shfl_xor(float v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
 FGT_DEV double fgt_shfl_xor(double v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }

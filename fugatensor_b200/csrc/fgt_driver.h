@@ -29,6 +29,7 @@ struct Driver {
   CUresult (*ModuleUnload)(CUmodule) = nullptr;
   CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
   CUresult (*OccupancyMaxActiveBlocksPerMultiprocessor)(int*, CUfunction, int, size_t) = nullptr;
+  CUresult (*FuncSetAttribute)(CUfunction, CUfunction_attribute, int) = nullptr;
   CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
                            void**, void**) = nullptr;
 };
@@ -61,6 +62,7 @@ inline Driver& drv() {
     sym(d.ModuleGetFunction, "cuModuleGetFunction");
     sym(d.OccupancyMaxActiveBlocksPerMultiprocessor, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
     sym(d.LaunchKernel, "cuLaunchKernel");
+    sym(d.FuncSetAttribute, "cuFuncSetAttribute");
     d.ok = all;
     if (!all) d.err = "libcuda.so.1 lacks a required driver entry point";
   });

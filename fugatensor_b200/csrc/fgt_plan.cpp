@@ -976,7 +976,7 @@ std::string plan_json(const Plan& plan) {
     const KernelDef& k = plan.kernels[i];
     j << (i ? "," : "") << "{\"name\":\"" << k.name << "\",\"rows\":" << k.dom.NR << ",\"row_elements\":" << k.dom.NI
       << ",\"threads\":" << k.nt << ",\"threads_per_row\":" << k.tpr << ",\"vector\":" << k.vec
-      << ",\"chunks\":" << k.nch << ",\"streaming\":" << (k.streaming ? "true" : "false")
+      << ",\"chunks\":" << k.nch << ",\"smem_bytes\":" << k.smem_bytes << ",\"streaming\":" << (k.streaming ? "true" : "false")
       << ",\"reductions\":" << k.reds.size() << "}";
   }
   j << "]}}";

@@ -103,6 +103,7 @@ struct KernelDef {
   bool streaming = false;
   int64_t rows_per_cta = 1;
   int64_t max_ctas = 0;           // partial slots reserved (grid upper bound)
+  int64_t smem_bytes = 0;         // dynamic shared memory (row staging ring)
   int64_t partials = 0;           // P for FIN kernels
   // rank exchange (sharded): record bytes gathered by NCCL after stage 1
   int64_t send_offset = -1, recv_offset = -1, record_bytes = 0;

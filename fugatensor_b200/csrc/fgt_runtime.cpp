@@ -240,8 +240,12 @@ LoadedModule& module_for(fgt_spec* s) {
     cu_check(drv().ModuleLoadData(&m, s->cubins[i].data()), "cuModuleLoadData");
     CUfunction f;
     cu_check(drv().ModuleGetFunction(&f, m, s->plan.kernels[i].name.c_str()), "cuModuleGetFunction");
+    const int smem = (int)s->plan.kernels[i].smem_bytes;
+    if (smem > 48 * 1024)
+      cu_check(drv().FuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, smem), "cuFuncSetAttribute");
     int occ = 1;
-    cu_check(drv().OccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, s->plan.kernels[i].nt, 0), "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    cu_check(drv().OccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, s->plan.kernels[i].nt, (size_t)smem),
+             "cuOccupancyMaxActiveBlocksPerMultiprocessor");
     lm.mods.push_back(m);
     lm.fn.push_back(f);
     lm.occupancy.push_back(std::max(1, occ));
@@ -334,7 +338,9 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
     parts[i] = k.kind == KKind::ROW ? grid * k.rows_per_cta : grid;
     ArgBlock a = make_args(p, inputs, outputs, ws, nparts);
     void* params[] = {a.bytes.data()};
-    cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, 1, 1, (unsigned)k.nt, 1, 1, 0, st, params, nullptr), "cuLaunchKernel");
+    cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, 1, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
+                                nullptr),
+             "cuLaunchKernel");
     for (int c : p.collectives) {
       if (c != (int)i) continue;
       unsigned char* base = (unsigned char*)ws;

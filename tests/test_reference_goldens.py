@@ -324,3 +324,13 @@ def test_no_fma_contraction(backend):
     y = x * (1.0 - 2**-23) + (-1.0)
     (v,) = run(backend, y)
     assert float(v[0]) == 0.0
+
+
+def test_argmax_rows_of_identity_values(backend):
+    """First-occurrence argmax/argmin where every element equals the scan identity (+-inf) or ties."""
+    x = T([[-math.inf] * 5, [math.inf] * 5, [2.0] * 5, [-math.inf, -math.inf, 3.0, -math.inf, 3.0]])
+    a, b, c = run(backend, x.argmax(axis=1), x.argmin(axis=1), x.argmax())
+    assert a.tolist() == [0, 0, 0, 2] and b.tolist() == [0, 0, 0, 0] and int(c) == 5
+    big = T([[-math.inf] * 3000])
+    (d,) = run(backend, big.argmax())
+    assert int(d) == 0
