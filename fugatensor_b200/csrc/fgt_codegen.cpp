@@ -504,7 +504,8 @@ struct Emitter {
           // cp.async moves 4, 8 or 16 bytes; a stage (one row of every staged
           // operand) must leave room for at least two stages in 227 KB.
           const int64_t piece = (int64_t)K.rows_per_cta * K.nch * K.tpr * rs.bytes;
-          rs.staged = (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) && stage_bytes + piece <= 100 * 1024;
+          rs.staged = P.opt.row_staging && (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) &&
+                      stage_bytes + piece <= 100 * 1024;
           if (rs.staged) stage_bytes += piece;
           row_sites.push_back(rs);
         } else if (elem) {
@@ -637,7 +638,28 @@ struct Emitter {
     for (size_t k = 0; k < n.args.size(); ++k) a.push_back(val(n.args[k], ms[k], D));
     std::string expr;
     const int odt = g.nodes[n.args[0]].dt;
-    if (n.op == FGT_OP_CAST) expr = cast_expr(odt, n.dt, a[0]);
+    if (n.op == FGT_OP_DIV) {
+      // A divisor that is constant across the row's elements (a row statistic
+      // or a kernel constant) gets its reciprocal once, in its own scope; the
+      // per-element division is then the corrected reciprocal product, which
+      // equals the IEEE quotient (fgt_div_by).
+      const Level la = an.run(n.args[0], ms[0]), lb = an.run(n.args[1], ms[1]);
+      if ((lb.kind & 2) == 0 && (la.kind & 2) != 0) {
+        const Sc db = lb.kind == 0 ? Sc{SC_PRO, 0} : Sc{SC_ROW, lb.phase};
+        const std::string rk = "rcp|" + a[1] + "#" + std::to_string((int)db.k) + ":" + std::to_string(db.p);
+        auto it = memo.find(rk);
+        std::string rcp;
+        if (it != memo.end()) rcp = it->second;
+        else {
+          rcp = fresh("rcp");
+          memo[rk] = rcp;
+          add(db, "const float " + rcp + " = fgt_recip_for_div(" + a[1] + ");");
+        }
+        expr = rnd(n.dt, "fgt_div_by(" + a[0] + "," + a[1] + "," + rcp + ")");
+      }
+    }
+    if (!expr.empty()) {
+    } else if (n.op == FGT_OP_CAST) expr = cast_expr(odt, n.dt, a[0]);
     else if (n.op == FGT_OP_COMPARE) expr = "(" + a[0] + cmp_op(n.pred) + a[1] + ")";
     else if (n.op == FGT_OP_SELECT) expr = "(" + a[0] + "?" + a[1] + ":" + a[2] + ")";
     else if (is_binary(n.op)) expr = binary_expr(n.op, n.dt, a[0], a[1]);

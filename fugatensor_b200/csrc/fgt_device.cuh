@@ -81,17 +81,39 @@ FGT_DEV fgt_i64 fgt_f32_to_i64(float f) {
 }
 
 // ------------------------------------------------------- IEEE extrema ------
+// max.NaN / min.NaN return the canonical NaN if either input is NaN and
+// order -0 below +0 (checked on sm_100a for every signed-zero and NaN pair),
+// which is exactly the reference's IEEE maximum/minimum.
 FGT_DEV float fgt_fmax(float a, float b) {
-  if (a != a) return a;
-  if (b != b) return b;
-  if (a == b) return (__float_as_uint(a) & 0x80000000u) ? b : a;
-  return a > b ? a : b;
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 FGT_DEV float fgt_fmin(float a, float b) {
-  if (a != a) return a;
-  if (b != b) return b;
-  if (a == b) return (__float_as_uint(a) & 0x80000000u) ? a : b;
-  return a < b ? a : b;
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Division by a value that is constant over many elements (a row statistic,
+// a broadcast parameter): y = RN(1/d) is computed once with an IEEE division;
+// per element q = RN(x*y), r = x - q*d (exact, by FMA), q' = RN(q + r*y).
+// By Markstein's theorem (P. Markstein, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) q' is
+// the correctly rounded x/d when no intermediate underflows or overflows; the
+// guard sends zero, tiny, huge, inf and NaN quotients (and non-normal d, for
+// which y is made NaN) to the IEEE division, so the result always equals
+// __fdiv_rn(x, d).
+FGT_DEV float fgt_recip_for_div(float d) {
+  const float a = fabsf(d);
+  return (a >= 1.17549435e-38f && a <= 3.40282347e+38f) ? __fdiv_rn(1.0f, d) : __int_as_float(0x7fc00000);
+}
+FGT_DEV float fgt_div_by(float x, float d, float y) {
+  const float q = __fmul_rn(x, y);
+  const float r = __fmaf_rn(-q, d, x);
+  const float q2 = __fmaf_rn(r, y, q);
+  const float a = fabsf(q2);
+  return (a >= 7.52316385e-37f && a <= 1.32922800e+36f) ? q2 : __fdiv_rn(x, d);
 }
 template <class T> FGT_DEV T fgt_imax(T a, T b) { return a > b ? a : b; }
 template <class T> FGT_DEV T fgt_imin(T a, T b) { return a < b ? a : b; }

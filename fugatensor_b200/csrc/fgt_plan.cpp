@@ -546,9 +546,12 @@ struct Planner {
   void geometry_row(KernelDef& k) {
     const int64_t NI = k.dom.NI;
     const int64_t nvec = std::max<int64_t>(1, (NI + k.vec - 1) / k.vec);
+    // ~16 elements per thread per operand: enough independent work per
+    // thread, and as many threads per row as that allows (up to 1024).
+    const int64_t per_thread_chunks = std::max<int64_t>(1, (16 + k.vec - 1) / k.vec);
     if (nvec >= 256) {
       int64_t nt = 128;
-      while (nt * 2 <= 1024 && nt * 2 * 4 <= nvec) nt *= 2;
+      while (nt * 2 <= 1024 && nt * 2 * per_thread_chunks <= nvec) nt *= 2;
       k.nt = (int)nt;
       k.tpr = (int)nt;
       k.rows_per_cta = 1;

@@ -402,6 +402,9 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       }
       cache_dir = options->cache_dir;
     }
+    // FGT_ROW_STAGING=0 keeps streamed row operands in registers
+    // (double-buffered) instead of the shared-memory ring.
+    if (const char* st = std::getenv("FGT_ROW_STAGING")) opt.row_staging = std::atoi(st) != 0;
     int sms = current_sm_count();
     if (sms > 0) opt.num_sms = sms;
     auto spec = std::make_unique<fgt_spec>();

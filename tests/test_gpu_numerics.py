@@ -1,0 +1,61 @@
+"""Bit-level GPU checks of the kernel arithmetic against the oracle's IEEE arithmetic."""
+import numpy as np
+import pytest
+
+import fugatensor_b200 as ft
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def _random_floats(rng, n, lo_exp, hi_exp):
+    mant = rng.integers(0, 1 << 23, n, dtype=np.uint32)
+    exp = rng.integers(lo_exp, hi_exp, n, dtype=np.uint32)
+    sign = rng.integers(0, 2, n, dtype=np.uint32) << 31
+    return (sign | (exp << 23) | mant).view(np.float32)
+
+
+@pytest.mark.parametrize("lo,hi", [(1, 254), (100, 156), (1, 30), (225, 254)])
+def test_division_by_row_constant_is_ieee(lo, hi):
+    """x / broadcast(d[row]) uses a per-row reciprocal + correction: must equal x / d bitwise."""
+    rng = np.random.default_rng(lo * 1000 + hi)
+    rows, cols = 257, 1024
+    x = _random_floats(rng, rows * cols, lo, hi).reshape(rows, cols)
+    d = _random_floats(rng, rows, lo, hi).reshape(rows, 1)
+    x[0, :8] = [0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 3.4e38]
+    d[1, 0], d[2, 0], d[3, 0], d[4, 0] = 0.0, np.inf, np.nan, 1e-40
+    X, D = ft.tensor(x), ft.tensor(d)
+    q = X / ft.broadcast_to(D, X.shape)
+    desc, leaves, roots = q.engine.trace(q)
+    (ref,) = O.evaluate(desc, [x, d])
+    got = q.numpy()
+    both_nan = np.isnan(got) & np.isnan(ref)
+    mism = (_bits(got) != _bits(ref)) & ~both_nan
+    assert not mism.any(), f"{mism.sum()} mismatches, e.g. x={x[mism][:3]} d={np.broadcast_to(d, x.shape)[mism][:3]}"
+
+
+def test_division_by_kernel_constant_is_ieee():
+    rng = np.random.default_rng(7)
+    x = _random_floats(rng, 1 << 20, 1, 254)
+    X = ft.tensor(x)
+    got = (X / 3.0).numpy()
+    ref = x / np.float32(3.0)
+    both_nan = np.isnan(got) & np.isnan(ref)
+    assert not ((_bits(got) != _bits(ref)) & ~both_nan).any()
+
+
+def test_softmax_rows_match_oracle_bitwise_except_exp():
+    """Row softmax: max, shift and division are exact; only expf may differ in the last ulp."""
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((64, 8192)) * 2).astype(np.float32)
+    X = ft.tensor(x)
+    y = ft.nn.functional.softmax(X, axis=-1)
+    desc, leaves, roots = y.engine.trace(y)
+    (ref,) = O.evaluate(desc, [x])
+    got = y.numpy()
+    rel = np.abs(got.astype(np.float64) - ref) / np.abs(ref)
+    assert rel.max() < 2e-6
