@@ -14,6 +14,7 @@
 // rounded once per operation, exp/log/tanh/erf through CUDA's f32 math
 // library (the reference links libdevice, src/fugatensor/_ask/cuda.py:215-229).
 #include <cstring>
+#include <functional>
 #include <sstream>
 
 #include "fgt_plan.h"
@@ -52,10 +53,12 @@ std::string ld_conv(int dt, const std::string& x) {
     default: return x;
   }
 }
+// Every value of a narrow dtype is exactly representable (each operation
+// rounds), so a bf16 store is the high half of its f32 image.
 std::string st_conv(int dt, const std::string& x) {
   switch (dt) {
     case FGT_F16: return "fgt_f32_to_f16(" + x + ")";
-    case FGT_BF16: return "fgt_f32_to_bf16(" + x + ")";
+    case FGT_BF16: return "fgt_bf16_bits_exact(" + x + ")";
     case FGT_BOOL: return "(fgt_u8)(" + x + ")";
     default: return x;
   }
@@ -202,7 +205,6 @@ bool expensive(int op) {
     case FGT_OP_TANH:
     case FGT_OP_ERF:
     case FGT_OP_POW:
-    case FGT_OP_DIV:
       return true;
   }
   return false;
@@ -505,7 +507,7 @@ struct Emitter {
           // operand) must leave room for at least two stages in 227 KB.
           const int64_t piece = (int64_t)K.rows_per_cta * K.nch * K.tpr * rs.bytes;
           rs.staged = P.opt.row_staging && (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) &&
-                      stage_bytes + piece <= 100 * 1024;
+                      stage_bytes + piece <= 96 * 1024;
           if (rs.staged) stage_bytes += piece;
           row_sites.push_back(rs);
         } else if (elem) {
@@ -516,26 +518,7 @@ struct Emitter {
         }
       }
       if (prol) return ld_conv(n.dt, s + "[v]");
-      if (cached) {
-        const RowSite* rs = nullptr;
-        for (auto& x : row_sites)
-          if (x.name == s) rs = &x;
-        if (rs && rs->staged) {
-          // read this thread's piece of the current stage once per chunk and phase
-          std::string pk = "stv|" + s + "|" + std::to_string(D.p);
-          auto pit = memo.find(pk);
-          std::string sv;
-          if (pit != memo.end()) sv = pit->second;
-          else {
-            sv = s + "_p" + std::to_string(D.p);
-            memo[pk] = sv;
-            chunkpre[D.p].push_back(ST + " " + sv + "[" + std::to_string(K.vec) + "]; fgt_lds(" + sv + ", (const " + ST +
-                                    "*)(fgt_dsmem + @OFF(" + s + ")));");
-          }
-          return ld_conv(n.dt, sv + "[v]");
-        }
-        return ld_conv(n.dt, s + "[c][v]");
-      }
+      if (cached) return ld_conv(n.dt, s + "[c][v]");
       if (elem) return ld_conv(n.dt, s + "[u][v]");
       return ld_conv(n.dt, s + "[v]");
     }
@@ -926,80 +909,79 @@ struct Emitter {
       put(o, prolane, "        ");
       o << "      }\n    }\n  }\n";
     }
-    // ---- streamed row operands
-    // (a) staged: a ring of `stages` rows in shared memory, filled with
-    //     cp.async (stages-1) rows ahead of the row being computed;
-    // (b) otherwise: registers, double-buffered one row ahead.
+    // ---- streamed row operands: the current row is in registers, the next
+    // row is in flight while the current one is computed:
+    // (a) staged operands travel global -> shared memory with cp.async (no
+    //     registers held by data in flight) and are copied to registers when
+    //     the row starts; every thread copies and reads only its own pieces;
+    // (b) other operands are double-buffered in registers.
     std::vector<RowSite*> staged_sites, reg_sites;
     for (auto& rs : row_sites) (rs.staged ? staged_sites : reg_sites).push_back(&rs);
     if (!staged_sites.empty()) {
-      stages = (int)std::min<int64_t>(4, std::max<int64_t>(2, (200 * 1024) / std::max<int64_t>(1, stage_bytes)));
+      stages = 1;
       int64_t off = 0;
       for (auto* rs : staged_sites) {
         rs->smem_off = off;
-        off += (int64_t)stages * K.rows_per_cta * K.nch * K.tpr * rs->bytes;
+        off += (int64_t)K.rows_per_cta * K.nch * K.tpr * rs->bytes;
       }
     }
     const std::string stride = "(fgt_i64)gridDim.x * " + RPC;
-    auto site_loop = [&](std::ostringstream& os, const std::string& ind, const char* rvar, bool next) {
+    auto chunk_loop = [&](std::ostringstream& os, const std::string& ind, const std::function<void(const std::string&)>& body) {
       os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
       os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
       os << ind << "  if (e0 < NI) {\n";
-      for (auto* rs : reg_sites) os << ind << "    " << site_load(*rs, next ? rs->name + "_n" : rs->name, rvar) << "\n";
+      body(ind + "    ");
       os << ind << "  }\n" << ind << "}\n";
     };
-    auto issue = [&](std::ostringstream& os, const std::string& ind, const char* rvar, const std::string& stg) {
-      os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
-      os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      os << ind << "  if (e0 < NI) {\n";
-      for (auto* rs : staged_sites)
-        os << ind << "    fgt_cp_async<" << rs->bytes << ">(sbase_ + " << piece_off(*rs, stg) << ", " << rs->ptr << " + "
-           << itext(rs->addr, "e", rvar) << " + e0);\n";
-      os << ind << "  }\n" << ind << "}\n";
+    auto reg_loads = [&](std::ostringstream& os, const std::string& ind, const char* rvar, bool next) {
+      chunk_loop(os, ind, [&](const std::string& in) {
+        for (auto* rs : reg_sites) os << in << site_load(*rs, next ? rs->name + "_n" : rs->name, rvar) << "\n";
+      });
     };
-    for (auto* rs : reg_sites) {
-      std::string dims = rs->uniform ? "[" + NCH + "]" : "[" + NCH + "][" + VEC + "]";
-      o << "  " << rs->st << " " << rs->name << dims << "; " << rs->st << " " << rs->name << "_n" << dims << ";\n";
+    auto issue = [&](std::ostringstream& os, const std::string& ind, const char* rvar) {
+      chunk_loop(os, ind, [&](const std::string& in) {
+        for (auto* rs : staged_sites)
+          os << in << "fgt_cp_async<" << rs->bytes << ">(sbase_ + " << piece_off(*rs, "0") << ", " << rs->ptr << " + "
+             << itext(rs->addr, "e", rvar) << " + e0);\n";
+      });
+    };
+    auto smem_to_regs = [&](std::ostringstream& os, const std::string& ind) {
+      chunk_loop(os, ind, [&](const std::string& in) {
+        for (auto* rs : staged_sites)
+          os << in << "fgt_lds(" << rs->name << "[c], (const " << rs->st << "*)(fgt_dsmem + " << piece_off(*rs, "0") << "));\n";
+      });
+    };
+    for (auto& rs : row_sites) {
+      std::string dims = rs.uniform ? "[" + NCH + "]" : "[" + NCH + "][" + VEC + "]";
+      o << "  " << rs.st << " " << rs.name << dims << ";";
+      if (!rs.staged) o << " " << rs.st << " " << rs.name << "_n" << dims << ";";
+      o << "\n";
     }
-    if (!reg_sites.empty()) {
-      o << "  { const fgt_i64 r0_ = (fgt_i64)blockIdx.x * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
-      site_loop(o, "      ", "r0_", false);
-      o << "    }\n  }\n";
-    }
-    const std::string S = std::to_string(stages);
     if (stages) {
       o << "  extern __shared__ __align__(16) unsigned char fgt_dsmem[];\n";
-      o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n  int stg = 0;\n";
-      o << "  for (int k_ = 0; k_ < " << stages - 1 << "; ++k_) {\n";
-      o << "    const fgt_i64 rk_ = (fgt_i64)blockIdx.x * " << RPC << " + grp + (fgt_i64)k_ * " << stride << ";\n";
-      o << "    if (rk_ < NR) {\n";
-      issue(o, "      ", "rk_", "k_");
-      o << "    }\n    fgt_cp_commit();\n  }\n";
+      o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n";
+    }
+    if (!row_sites.empty()) {
+      o << "  { const fgt_i64 r0_ = (fgt_i64)blockIdx.x * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
+      reg_loads(o, "      ", "r0_", false);
+      if (stages) issue(o, "      ", "r0_");
+      o << "    }\n";
+      if (stages) {
+        o << "    fgt_cp_commit();\n    fgt_cp_wait<0>();\n";
+        smem_to_regs(o, "    ");
+      }
+      o << "  }\n";
     }
     o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
     o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
-    if (stages) {
-      o << "    { const fgt_i64 rp_ = r + (fgt_i64)" << stages - 1 << " * " << stride << ";\n";
-      o << "      const int sp_ = stg + " << stages - 1 << " >= " << S << " ? stg - 1 : stg + " << stages - 1 << ";\n";
-      o << "      if (rp_ < NR) {\n";
-      issue(o, "        ", "rp_", "sp_");
-      o << "      }\n      fgt_cp_commit();\n    }\n";
-      o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
-    }
-    if (!reg_sites.empty()) {
+    if (!row_sites.empty()) {
       o << "    const fgt_i64 rn_ = r + " << stride << ";\n    if (rn_ < NR) {\n";
-      site_loop(o, "      ", "rn_", true);
+      reg_loads(o, "      ", "rn_", true);
+      if (stages) issue(o, "      ", "rn_");
       o << "    }\n";
+      if (stages) o << "    fgt_cp_commit();\n";
     }
     put(o, rowdecl, "    ");
-    // resolve the shared-memory piece offsets of staged operands
-    for (auto& list : chunkpre)
-      for (auto& stmt : list)
-        for (auto* rs : staged_sites) {
-          const std::string tag = "@OFF(" + rs->name + ")";
-          size_t pos;
-          while ((pos = stmt.find(tag)) != std::string::npos) stmt.replace(pos, tag.size(), piece_off(*rs, "stg"));
-        }
     for (int p = 0; p < nphase; ++p) {
       put(o, rowsc[p], "    ");
       o << "    if (rv) {\n";
@@ -1023,9 +1005,11 @@ struct Emitter {
       if (rs->uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) " << rs->name << "[c] = " << rs->name << "_n[c];\n";
       else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << VEC << "; ++v) " << rs->name << "[c][v] = " << rs->name << "_n[c][v];\n";
     }
-    if (stages) o << "    stg = stg + 1 == " << S << " ? 0 : stg + 1;\n";
+    if (stages) {
+      o << "    fgt_cp_wait<0>();\n";
+      smem_to_regs(o, "    ");
+    }
     o << "  }\n";
-    if (stages) o << "  fgt_cp_wait<0>();\n";
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";

@@ -117,7 +117,7 @@ struct Options {
   uint64_t shard_inputs = 0;
   int num_sms = 148;              // partial buffers are sized for this many SMs
   int max_ctas_per_sm = 8;
-  int row_staging = 0;            // stage streamed row operands in shared memory (FGT_ROW_STAGING=1)
+  int row_staging = 1;            // next row arrives via cp.async into shared memory (FGT_ROW_STAGING=0: registers)
 };
 
 struct Plan {
