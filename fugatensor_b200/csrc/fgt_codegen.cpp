@@ -918,11 +918,12 @@ struct Emitter {
     std::vector<RowSite*> staged_sites, reg_sites;
     for (auto& rs : row_sites) (rs.staged ? staged_sites : reg_sites).push_back(&rs);
     if (!staged_sites.empty()) {
-      stages = 1;
+      // rows in flight per CTA: as many as fit ~96 KB (two CTAs per SM)
+      stages = (int)std::min<int64_t>(8, std::max<int64_t>(1, (96 * 1024) / std::max<int64_t>(1, stage_bytes)));
       int64_t off = 0;
       for (auto* rs : staged_sites) {
         rs->smem_off = off;
-        off += (int64_t)K.rows_per_cta * K.nch * K.tpr * rs->bytes;
+        off += (int64_t)stages * K.rows_per_cta * K.nch * K.tpr * rs->bytes;
       }
     }
     const std::string stride = "(fgt_i64)gridDim.x * " + RPC;
@@ -938,17 +939,17 @@ struct Emitter {
         for (auto* rs : reg_sites) os << in << site_load(*rs, next ? rs->name + "_n" : rs->name, rvar) << "\n";
       });
     };
-    auto issue = [&](std::ostringstream& os, const std::string& ind, const char* rvar) {
+    auto issue = [&](std::ostringstream& os, const std::string& ind, const char* rvar, const std::string& stg) {
       chunk_loop(os, ind, [&](const std::string& in) {
         for (auto* rs : staged_sites)
-          os << in << "fgt_cp_async<" << rs->bytes << ">(sbase_ + " << piece_off(*rs, "0") << ", " << rs->ptr << " + "
+          os << in << "fgt_cp_async<" << rs->bytes << ">(sbase_ + " << piece_off(*rs, stg) << ", " << rs->ptr << " + "
              << itext(rs->addr, "e", rvar) << " + e0);\n";
       });
     };
-    auto smem_to_regs = [&](std::ostringstream& os, const std::string& ind) {
+    auto smem_to_regs = [&](std::ostringstream& os, const std::string& ind, const std::string& stg) {
       chunk_loop(os, ind, [&](const std::string& in) {
         for (auto* rs : staged_sites)
-          os << in << "fgt_lds(" << rs->name << "[c], (const " << rs->st << "*)(fgt_dsmem + " << piece_off(*rs, "0") << "));\n";
+          os << in << "fgt_lds(" << rs->name << "[c], (const " << rs->st << "*)(fgt_dsmem + " << piece_off(*rs, stg) << "));\n";
       });
     };
     for (auto& rs : row_sites) {
@@ -961,25 +962,33 @@ struct Emitter {
       o << "  extern __shared__ __align__(16) unsigned char fgt_dsmem[];\n";
       o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n";
     }
+    // Ring invariant at the top of iteration i: registers hold row i, ring
+    // stage (i+k) % S holds row i+k for k = 1..S (S cp.async groups pending).
+    const std::string S = std::to_string(stages);
     if (!row_sites.empty()) {
       o << "  { const fgt_i64 r0_ = (fgt_i64)blockIdx.x * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
       reg_loads(o, "      ", "r0_", false);
-      if (stages) issue(o, "      ", "r0_");
       o << "    }\n";
       if (stages) {
-        o << "    fgt_cp_commit();\n    fgt_cp_wait<0>();\n";
-        smem_to_regs(o, "    ");
+        o << "    for (int k_ = 0; k_ < " << S << "; ++k_) {\n";
+        o << "      const fgt_i64 rk_ = r0_ + (fgt_i64)k_ * " << stride << ";\n      if (rk_ < NR) {\n";
+        issue(o, "        ", "rk_", "k_");
+        o << "      }\n      fgt_cp_commit();\n    }\n";
+        o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
+        smem_to_regs(o, "    ", "0");
+        o << "    { const fgt_i64 rk_ = r0_ + (fgt_i64)" << S << " * " << stride << ";\n      if (rk_ < NR) {\n";
+        issue(o, "        ", "rk_", "0");
+        o << "      }\n      fgt_cp_commit();\n    }\n";
       }
       o << "  }\n";
+      if (stages) o << "  int stg = " << (stages > 1 ? 1 : 0) << ";\n";
     }
     o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
     o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
-    if (!row_sites.empty()) {
+    if (!reg_sites.empty()) {
       o << "    const fgt_i64 rn_ = r + " << stride << ";\n    if (rn_ < NR) {\n";
       reg_loads(o, "      ", "rn_", true);
-      if (stages) issue(o, "      ", "rn_");
       o << "    }\n";
-      if (stages) o << "    fgt_cp_commit();\n";
     }
     put(o, rowdecl, "    ");
     for (int p = 0; p < nphase; ++p) {
@@ -1006,10 +1015,16 @@ struct Emitter {
       else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << VEC << "; ++v) " << rs->name << "[c][v] = " << rs->name << "_n[c][v];\n";
     }
     if (stages) {
-      o << "    fgt_cp_wait<0>();\n";
-      smem_to_regs(o, "    ");
+      // row i+1 -> registers; its stage refills with row i+1+S
+      o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
+      smem_to_regs(o, "    ", "stg");
+      o << "    { const fgt_i64 rk_ = r + (fgt_i64)" << stages + 1 << " * " << stride << ";\n      if (rk_ < NR) {\n";
+      issue(o, "        ", "rk_", "stg");
+      o << "      }\n      fgt_cp_commit();\n    }\n";
+      o << "    stg = stg + 1 == " << S << " ? 0 : stg + 1;\n";
     }
     o << "  }\n";
+    if (stages) o << "  fgt_cp_wait<0>();\n";
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";

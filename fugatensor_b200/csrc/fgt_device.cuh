@@ -45,15 +45,7 @@ FGT_DEV fgt_u16 fgt_f32_to_bf16(float f) {
 // Values of f16/bf16 type are carried in f32 registers, always exactly
 // representable in the narrow format: every operation rounds once.
 FGT_DEV float fgt_rnd_f16(float f) { return fgt_f16_to_f32(fgt_f32_to_f16(f)); }
-// bf16 shares f32's exponent range, so round-to-nearest-even is integer
-// arithmetic on the f32 bit pattern (a carry out of the significand moves
-// into the exponent; past the largest finite value it yields inf). Integer
-// pipes have several times the throughput of the conversion unit.
-FGT_DEV float fgt_rnd_bf16(float f) {
-  const fgt_u32 u = __float_as_uint(f);
-  const fgt_u32 r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
-  return f != f ? __int_as_float(0x7fc00000) : __uint_as_float(r);
-}
+FGT_DEV float fgt_rnd_bf16(float f) { return fgt_bf16_to_f32(fgt_f32_to_bf16(f)); }
 // Storage of a value that is already an exact bf16: its high half.
 FGT_DEV fgt_u16 fgt_bf16_bits_exact(float f) { return (fgt_u16)(__float_as_uint(f) >> 16); }
 
