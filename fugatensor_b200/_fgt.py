@@ -76,7 +76,8 @@ lib.fgt_spec_launch_sharded.argtypes = [_vp, _vp, ctypes.POINTER(_vp), ctypes.PO
 
 EXPORTED = ("fgt_last_error", "fgt_abi_version", "fgt_spec_create", "fgt_spec_destroy", "fgt_spec_get_info",
             "fgt_spec_port", "fgt_spec_plan_json", "fgt_spec_kernel_source", "fgt_spec_launch",
-            "fgt_comm_unique_id", "fgt_comm_create", "fgt_comm_destroy", "fgt_spec_launch_sharded")
+            "fgt_comm_unique_id", "fgt_comm_create", "fgt_comm_destroy", "fgt_spec_launch_sharded",
+            "fgt_reduce_f32_noalloc")
 
 
 def check(status):

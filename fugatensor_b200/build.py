@@ -24,6 +24,7 @@ CUDA = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 LIB = PKG / "libfgt.so"
 
 CPP_SOURCES = ["fgt_graph.cpp", "fgt_plan.cpp", "fgt_codegen.cpp", "fgt_runtime.cpp"]
+CU_SOURCES = ["fgt_noalloc.cu"]
 HEADERS = ["fgt_internal.h", "fgt_plan.h", "fgt_driver.h", "fgt_device.cuh"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -89,9 +90,17 @@ def build(verbose: bool = False) -> Path:
             _run(["g++", "-std=c++17", "-O2", "-fPIC", "-Wall", "-Wno-unused-function", f"-I{ROOT / 'include'}",
                   f"-I{CSRC}", f"-I{CUDA / 'include'}", "-c", str(src), "-o", str(obj)])
         objs.append(obj)
+    # statically compiled kernels (nvcc, sm_100a)
+    for src in CU_SOURCES:
+        src = CSRC / src
+        obj = BUILD / (src.stem + ".o")
+        if _stale(obj, [src, CSRC / "fgt_device.cuh", ROOT / "include" / "fgt.h"]):
+            _run([str(CUDA / "bin" / "nvcc"), *GENCODE, "-lineinfo", "-O3", "-fmad=false", "-std=c++17",
+                  "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)])
+        objs.append(obj)
     if _stale(LIB, objs + deps):
-        _run(["g++", "-shared", "-o", str(LIB), *map(str, objs), f"-L{CUDA / 'lib64'}", "-lnvrtc", "-ldl", "-lpthread",
-              f"-Wl,-rpath,{CUDA / 'lib64'}", "-Wl,--no-undefined"])
+        _run(["g++", "-shared", "-o", str(LIB), *map(str, objs), f"-L{CUDA / 'lib64'}", "-lnvrtc", "-lcudart_static",
+              "-lrt", "-ldl", "-lpthread", f"-Wl,-rpath,{CUDA / 'lib64'}", "-Wl,--no-undefined"])
     if verbose:
         print(f"built {LIB}")
     return LIB

@@ -374,6 +374,10 @@ fgt_status copy_out(const std::string& s, char* buffer, size_t capacity, size_t*
 }
 
 }  // namespace
+
+// Status + thread-local message for entry points defined in other files.
+fgt_status record_error(fgt_status s, const std::string& m) { return set_error(s, m); }
+
 }  // namespace fgt
 
 using namespace fgt;

@@ -206,6 +206,35 @@ fgt_status fgt_spec_launch_sharded(const fgt_spec* spec, fgt_comm* comm, const v
                                    void* const* outputs, void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* ---- allocation-free whole-tensor reduction ----------------------------- */
+
+/* Scratch limits of fgt_reduce_f32_noalloc. */
+#define FGT_NOALLOC_SLOTS 2048
+#define FGT_NOALLOC_ELEMS_PER_SLOT (1LL << 20)
+#define FGT_NOALLOC_SCRATCH_BYTES (FGT_NOALLOC_SLOTS * 32)
+
+/* No counterpart in the reference: for callers that cannot allocate device
+ * memory (code running inside an allocator or memory manager, services that
+ * must not touch the device allocator after start-up, hosts that own all
+ * device memory and pass only input/output buffers). Computes the sum, IEEE
+ * max, first-occurrence argmax (NaN counts as the maximum) and mean (sum / n)
+ * of x[0..n), like the whole-tensor reduction partition through
+ * fgt_spec_launch, but keeps its per-CTA partials in a static 64 KiB device
+ * array instead of a caller workspace; it calls no allocator.
+ *   - x: device pointer, 16-byte aligned; sum/max/mean: device f32 scalars;
+ *     argmax: device i64 scalar; stream: cudaStream_t (NULL = default).
+ *   - n must be in [1, 2^31] (FGT_NOALLOC_SLOTS x FGT_NOALLOC_ELEMS_PER_SLOT);
+ *     larger n is rejected with FGT_ERR_INVALID before any launch.
+ *   - The array is loaded on every GPU that uses the library and stays until
+ *     exit. All calls on a device share it: calls that overlap on the GPU
+ *     race. Nothing in it needs to start at zero (each call writes every slot
+ *     it reads).
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, once per device); make it before any stream
+ *     capture. */
+fgt_status fgt_reduce_f32_noalloc(const float* x, int64_t n, float* sum, float* max, int64_t* argmax, float* mean,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif
