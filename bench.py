@@ -258,6 +258,49 @@ def run_fgt(args):
                 del tt
                 torch.cuda.empty_cache()
 
+    # ---- sharded partitions (N > 1): the global problem split along dim 0,
+    # reductions over it combined by one NCCL all-gather (strong scaling)
+    if world > 1 and not args.skip_table:
+        from fugatensor_b200 import sharded
+        group = sharded.ShardGroup(world, rank)
+        peak_, _ = measured_peak()
+        for c, v, dt in (("c4", "global_reductions", "f32"), ("c3", "layernorm_vjp", "f32")):
+            r, h = W.FULL[c]
+            tt = device_inputs(c, r // world, h, dt, device, seed=rank)
+            dts = W.input_dtypes(c, dt)
+            full = {k: ft.Tensor(engine, dts[k], ((r,) + tuple(x.shape[1:])) if k in ("x", "X", "dY") else tuple(x.shape),
+                                 data=torch.empty(0)) for k, x in tt.items()}
+            desc, leaves, _ = engine.trace(*W.build(c, v, full))
+            names = [next(k for k, x in full.items() if x is l) for l in leaves]
+            split = [i for i, k in enumerate(names) if k in ("x", "X", "dY")]
+            spec = sharded.shard_spec(desc, world, rank, split)
+            ins = [tt[k] for k in names]
+            outs = [torch.empty(s, dtype=__import__("fugatensor_b200")._fgt.torch_dtype(d), device=device)
+                    for d, s in spec.output_types]
+            ws = torch.empty(max(1, spec.workspace_bytes), dtype=torch.uint8, device=device)
+            for _ in range(3):
+                sharded.run_sharded(spec, group, *ins, outputs=outs, workspace=ws)
+            torch.cuda.synchronize()
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(args.table_iters):
+                sharded.run_sharded(spec, group, *ins, outputs=outs, workspace=ws)
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / args.table_iters
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            nb = W.algorithmic_bytes(c, v, r, h, dt)
+            partitions[f"{c}/{v}/{dt}/sharded{world}"] = {
+                "global_shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
+                "per_gpu_frac": round(nb / ms / 1e6 / world / peak_, 4), "kernels": spec.kernel_count,
+                "collectives": spec.collective_count, "scaling": "strong"}
+            del tt, ins, outs, ws
+            torch.cuda.empty_cache()
+        group.close()
+
     # ---- e2e through the public API: pinned host -> device, evaluate, device -> host
     e2e = None
     if not args.skip_e2e:
