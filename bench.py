@@ -63,7 +63,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -188,6 +188,10 @@ def run_fgt(args):
         spec, ins = compile_partition(engine, cfg, v, rows, cols, dtype, tens)
         launchers.append(Launcher(spec, ins, device))
         bytes_step += W.algorithmic_bytes(cfg, v, rows, cols, dtype)
+    # clocks: sampled from before the warm-up through the partition table
+    # (the timed steps alone can be shorter than nvidia-smi's first sample)
+    clk = ClockSampler(local).__enter__()
+    time.sleep(0.5)
     for _ in range(args.warmup):
         for L in launchers:
             L(stream.cuda_stream)
@@ -195,7 +199,7 @@ def run_fgt(args):
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(launchers) + 1)] for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    if True:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
@@ -257,6 +261,8 @@ def run_fgt(args):
                     del L
                 del tt
                 torch.cuda.empty_cache()
+
+    clk.__exit__(None, None, None)
 
     # ---- sharded partitions (N > 1): the global problem split along dim 0,
     # reductions over it combined by one NCCL all-gather (strong scaling)
