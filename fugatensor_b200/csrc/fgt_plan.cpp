@@ -10,6 +10,7 @@
 #include "fgt_plan.h"
 
 #include <algorithm>
+#include <cstdio>
 #include <functional>
 #include <sstream>
 
@@ -642,10 +643,13 @@ struct Planner {
         rd.role = ROLE_FULL;
         rd.opmap = red_opmap(g, r, k.dom, false, true);
       } else {
-        if (s.kept == k.dom.od && s.red == k.dom.id) {
+        // Orientation follows which axes are reduced (the signature's form),
+        // not extents alone: on square shapes a column reduction also matches
+        // the row extents, transposed.
+        if (s.form == 0 && s.kept == k.dom.od && s.red == k.dom.id) {
           rd.role = ROLE_ROW;
           rd.opmap = red_opmap(g, r, k.dom, true, false);
-        } else if (s.kept == k.dom.id && s.red == k.dom.od && !s.kept.empty()) {
+        } else if (s.form == 1 && s.kept == k.dom.id && s.red == k.dom.od && !s.kept.empty()) {
           rd.role = ROLE_COL;
           rd.opmap = red_opmap(g, r, k.dom, false, false);
         } else {
@@ -896,10 +900,35 @@ struct Planner {
     plan.workspace_bytes = ws;
     plan.loc = loc;
     plan.iota_offsets = iota_offsets;
+    // Kernel names carry a hash of the partition (nodes, outputs, options), so
+    // that launch lists and profiler filters tell the partitions apart.
+    uint64_t h = 1469598103934665603ULL;
+    auto mix = [&](int64_t v) {
+      for (int b = 0; b < 8; ++b) {
+        h ^= (uint64_t)((v >> (8 * b)) & 0xff);
+        h *= 1099511628211ULL;
+      }
+    };
+    for (const Node& n : g.nodes) {
+      mix(n.op);
+      mix(n.dt);
+      mix(n.pred);
+      mix((int64_t)n.cbits);
+      for (int64_t e : n.shape) mix(e);
+      for (int a : n.args) mix(a);
+      for (int64_t a : n.attrs) mix(a);
+      mix(-1);
+    }
+    for (int o : g.outputs) mix(o);
+    mix(opt.accumulation);
+    mix(opt.world);
+    mix(opt.rank);
+    char tag[16];
+    std::snprintf(tag, sizeof tag, "%08x", (unsigned)(h ^ (h >> 32)));
     for (size_t i = 0; i < plan.kernels.size(); ++i) {
       KernelDef& k = plan.kernels[i];
       const char* fam = k.kind == KKind::ELEM ? "elem" : k.kind == KKind::ROW ? "row" : k.kind == KKind::COLFIN ? "colfin" : "fullfin";
-      k.name = std::string("fgt_") + fam + "_" + std::to_string(i);
+      k.name = std::string("fgt_") + fam + "_" + std::to_string(i) + "_" + tag;
     }
     return plan;
   }

@@ -128,6 +128,23 @@ def test_workloads_fuse_into_one_pass(cfg, variant):
     assert eng.cache_info() == {"compilations": 1, "cache_hits": 1, "specializations": 1}
 
 
+@pytest.mark.parametrize("cfg,variant", sorted(EXPECTED_KERNELS))
+@pytest.mark.parametrize("n", [64, 8192])
+def test_square_shapes_keep_column_reductions_in_one_pass(cfg, variant, n):
+    """With rows == columns a column reduction also matches the row extents
+    transposed; orientation must follow the reduced axes, so square shapes plan
+    the same kernels as rectangular ones (no second, strided row kernel)."""
+    import torch
+    eng = ft.Engine("cuda:0")
+    dts = W.input_dtypes(cfg)
+    shapes = {"x": (n, n), "y": (n, n), "X": (n, n), "dY": (n, n), "gamma": (n,), "beta": (n,), "A": (n, n),
+              "B": (n, 1), "C": (1, n)}
+    t = {k: ft.Tensor(eng, dts[k], shapes[k], data=torch.empty(0)) for k in dts}
+    spec, *_ = eng.compile(*W.build(cfg, variant, t))
+    kinds = [k["name"].split("_")[1] for k in spec.execution_plan["cuda_lowering"]["kernels"]]
+    assert kinds == EXPECTED_KERNELS[(cfg, variant)]
+
+
 def test_full_size_workloads_specialise():
     """Planning + sm_100a compilation of every benchmark workload at its full size."""
     eng = ft.Engine("cuda:0")

@@ -14,7 +14,7 @@ for cfg, variants in W.VARIANTS.items():
     for var in variants:
         dtypes = ("f32", "bf16") if cfg == "c2" else ("f32",)
         for dt in dtypes:
-            for rows, cols in ((3, 5), (7, 33), (64, 1000), (40, 8192)):
+            for rows, cols in ((3, 5), (7, 33), (64, 1000), (40, 8192), (256, 256)):
                 CASES.append((cfg, var, dt, rows, cols))
 
 

@@ -40,7 +40,8 @@ def _plan(rank, world):
         split = [i for i, k in enumerate(names) if k in ("x", "y", "X", "dY", "A", "B")]
         spec = sharded.shard_spec(desc, world, rank, split)
         out[(cfg, var)] = {
-            "kernels": [k["name"] for k in spec.execution_plan["cuda_lowering"]["kernels"]],
+            # family and index; the trailing partition hash differs per rank (rank offsets)
+            "kernels": [k["name"].rsplit("_", 1)[0] for k in spec.execution_plan["cuda_lowering"]["kernels"]],
             "collectives": spec.collective_count, "workspace": spec.workspace_bytes,
             "inputs": spec.input_types, "outputs": spec.output_types,
             "global_inputs": desc.input_types(), "global_outputs": desc.output_types(), "split": split,
