@@ -700,11 +700,18 @@ struct Emitter {
     return ptr + "[" + itext(A) + "] = " + st_conv(n.dt, v) + ";";
   }
 
-  // Butterfly within TW lanes then (if the group spans warps) a sequential
-  // combine of the warp partials in warp order, so every lane ends with the
-  // same deterministic value.
+  // Butterfly within TW lanes then (if the group spans warps) a combine of
+  // the warp partials, so every lane ends with the same deterministic value.
+  // The warp partials are combined either sequentially in warp order, or
+  // (butterfly, NW a power of two) by every warp reading partial lane % NW and
+  // running an xor butterfly over NW lanes: each node of that tree combines
+  // the same two operands on every lane, only commuted, so all lanes of all
+  // warps agree bit for bit. trailing_sync=false drops the barrier that
+  // protects the partials from the next write; callers do that only when
+  // another barrier always lies between this read and that write.
   void group_reduce(std::vector<std::string>& out, const std::vector<std::pair<RedText, std::string>>& accs,
-                    int TW, bool cross_warp, int NW, const std::string& tag) {
+                    int TW, bool cross_warp, int NW, const std::string& tag, bool butterfly = false,
+                    bool trailing_sync = true) {
     if (accs.empty()) return;
     out.push_back("#pragma unroll");
     out.push_back("for (int m_ = 1; m_ < " + std::to_string(TW) + "; m_ <<= 1) {");
@@ -729,6 +736,26 @@ struct Emitter {
     }
     out.push_back("}");
     out.push_back("__syncthreads();");
+    if (butterfly && NW > 1 && (NW & (NW - 1)) == 0 && NW <= 32) {
+      const std::string mask = std::to_string(NW - 1);
+      for (auto& [t, a] : accs) {
+        out.push_back(a + " = sm_" + a + tag + "[tid & " + mask + "];");
+        if (t.arg) out.push_back(a + "i = smi_" + a + tag + "[tid & " + mask + "];");
+      }
+      out.push_back("#pragma unroll");
+      out.push_back("for (int m_ = 1; m_ < " + std::to_string(NW) + "; m_ <<= 1) {");
+      for (auto& [t, a] : accs) {
+        if (t.arg) {
+          out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); const fgt_i64 oi = fgt_shfl_xor(" + a +
+                        "i, m_); " + arg_stmt(t, a, a + "i", "ov", "oi") + " }");
+        } else {
+          out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); " + comb_stmt(t, a, "ov") + " }");
+        }
+      }
+      out.push_back("}");
+      if (trailing_sync) out.push_back("__syncthreads();");
+      return;
+    }
     for (auto& [t, a] : accs) {
       out.push_back(a + " = sm_" + a + tag + "[0];");
       if (t.arg) out.push_back(a + "i = smi_" + a + tag + "[0];");
@@ -825,15 +852,34 @@ struct Emitter {
       rowsc[p].push_back(t.acc_t + " " + a + " = " + t.ident + ";");
       if (t.arg) rowsc[p].push_back("fgt_i64 " + a + "i = " + t.identi + ";");
       std::string v = val(g.nodes[rd->node].args[0], rd->opmap, Sc{SC_LANE, p});
-      if (t.arg) lane[p].push_back("{ const fgt_i64 ix = " + arg_index(*rd) + "; " + scan_stmt(t, a, a + "i", v, "ix") + " }");
-      else lane[p].push_back(comb_stmt(t, a, v));
+      // Value reductions over a register-resident row run four independent
+      // accumulator chains (element k of the thread's row pieces feeds chain
+      // k % 4), folded pairwise before the group combine: four dependent
+      // chains instead of one. Storage-dtype accumulation keeps one chain.
+      const bool chains = !t.arg && !t.storage && !K.streaming && K.nch * K.vec >= 4;
+      if (t.arg) {
+        lane[p].push_back("{ const fgt_i64 ix = " + arg_index(*rd) + "; " + scan_stmt(t, a, a + "i", v, "ix") + " }");
+      } else if (chains) {
+        rowsc[p].push_back(t.acc_t + " " + a + "_s[4] = {" + t.ident + ", " + t.ident + ", " + t.ident + ", " + t.ident +
+                           "};");
+        lane[p].push_back(comb_stmt(t, a + "_s[(c * " + std::to_string(K.vec) + " + v) & 3]", v));
+        post[p].push_back(comb_stmt(t, a + "_s[0]", a + "_s[1]"));
+        post[p].push_back(comb_stmt(t, a + "_s[2]", a + "_s[3]"));
+        post[p].push_back(comb_stmt(t, a + "_s[0]", a + "_s[2]"));
+        post[p].push_back(comb_stmt(t, a, a + "_s[0]"));
+      } else {
+        lane[p].push_back(comb_stmt(t, a, v));
+      }
       phase_accs[p].push_back({t, a});
       acc_of[rd->node] = a;
       std::string rv = fresh("red");
       red_var[rd->node] = rv;
     }
+    // With two or more cross-warp phases per row, the barrier of the next
+    // phase separates each phase's partial reads from its next row's writes.
+    const bool trailing = phase_accs.size() < 2;
     for (auto& [p, accs] : phase_accs) {
-      group_reduce(post[p], accs, TW, xw, NW, "_p" + std::to_string(p));
+      group_reduce(post[p], accs, TW, xw, NW, "_p" + std::to_string(p), true, trailing);
     }
     for (auto* rd : rows) {
       int p = rphase[rd->node];

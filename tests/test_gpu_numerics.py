@@ -59,3 +59,33 @@ def test_softmax_rows_match_oracle_bitwise_except_exp():
     got = y.numpy()
     rel = np.abs(got.astype(np.float64) - ref) / np.abs(ref)
     assert rel.max() < 2e-6
+
+
+def _special_floats():
+    sp = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 3.4028235e38, -3.4028235e38, 65504.0, 65520.0,
+                   6.1e-5, 5.96e-8, 2.98e-8, 1.0 + 2.0**-8, 1.0 + 3 * 2.0**-8, 1.0 + 2.0**-11, 1.0 + 3 * 2.0**-11],
+                  dtype=np.float32)
+    # bf16 ties (low 16 bits exactly 0x8000) with even and odd kept bits, both signs
+    ties = (np.arange(64, dtype=np.uint32) << 16 | 0x3f808000).view(np.float32)
+    return np.concatenate([sp, ties, -ties])
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_narrowing_casts_are_rne_bitwise(dtype):
+    """f32 -> bf16/f16 casts (packed conversions with a zero partner) against the oracle's RNE codec,
+    over random patterns of every exponent, ties, overflow, subnormals, signed zeros and NaN."""
+    rng = np.random.default_rng(5 if dtype == "bf16" else 6)
+    x = np.concatenate([_special_floats(), _random_floats(rng, 1 << 20, 0, 256)]).astype(np.float32)
+    X = ft.tensor(x)
+    y = X.astype(dtype)
+    desc, leaves, roots = y.engine.trace(y)
+    (ref,) = O.evaluate(desc, [x])
+    got = y.numpy()
+    gb = got.view(np.uint16)
+    rb = np.ascontiguousarray(ref).view(np.uint16)
+    if dtype == "bf16":
+        nan = np.isnan(O.bf16_bits_to_f32(gb)) & np.isnan(O.bf16_bits_to_f32(rb))
+    else:
+        nan = np.isnan(got) & np.isnan(ref)
+    mism = (gb != rb) & ~nan
+    assert not mism.any(), f"{mism.sum()} mismatches, e.g. x={x[mism][:4]} got={gb[mism][:4]} ref={rb[mism][:4]}"
