@@ -335,6 +335,7 @@ struct Emitter {
   const Plan& P;
   const Graph& g;
   const KernelDef& K;
+  int row_phases = 0;  // levels holding row reductions (one block barrier each per row)
   const Domain& d;
   std::set<int64_t>* temps_loaded;
   std::vector<RedDef> fin_reds;
@@ -878,6 +879,7 @@ struct Emitter {
     // With two or more cross-warp phases per row, the barrier of the next
     // phase separates each phase's partial reads from its next row's writes.
     const bool trailing = phase_accs.size() < 2;
+    row_phases = (int)phase_accs.size();
     for (auto& [p, accs] : phase_accs) {
       group_reduce(post[p], accs, TW, xw, NW, "_p" + std::to_string(p), true, trailing);
     }
@@ -1303,6 +1305,7 @@ void generate_sources(Plan& plan) {
     Emitter em(plan, k, &loaded);
     k.source = em.build();
     k.smem_bytes = (int64_t)em.stages * em.stage_bytes;
+    k.row_phases = em.row_phases;
   }
 }
 

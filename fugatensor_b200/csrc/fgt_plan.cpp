@@ -547,9 +547,9 @@ struct Planner {
   void geometry_row(KernelDef& k) {
     const int64_t NI = k.dom.NI;
     const int64_t nvec = std::max<int64_t>(1, (NI + k.vec - 1) / k.vec);
-    // ~16 elements per thread per operand: enough independent work per
-    // thread, and as many threads per row as that allows (up to 1024).
-    const int64_t per_thread_chunks = std::max<int64_t>(1, (16 + k.vec - 1) / k.vec);
+    // ~row_elems (16) elements per thread per operand: enough independent
+    // work per thread, and as many threads per row as that allows (up to 1024).
+    const int64_t per_thread_chunks = std::max<int64_t>(1, (opt.row_elems + k.vec - 1) / k.vec);
     if (nvec >= 256) {
       int64_t nt = 128;
       while (nt * 2 <= 1024 && nt * 2 * per_thread_chunks <= nvec) nt *= 2;
@@ -923,6 +923,8 @@ struct Planner {
     mix(opt.accumulation);
     mix(opt.world);
     mix(opt.rank);
+    mix(opt.row_elems);
+    mix(opt.row_staging);
     char tag[16];
     std::snprintf(tag, sizeof tag, "%08x", (unsigned)(h ^ (h >> 32)));
     for (size_t i = 0; i < plan.kernels.size(); ++i) {
@@ -1009,7 +1011,8 @@ std::string plan_json(const Plan& plan) {
     j << (i ? "," : "") << "{\"name\":\"" << k.name << "\",\"rows\":" << k.dom.NR << ",\"row_elements\":" << k.dom.NI
       << ",\"threads\":" << k.nt << ",\"threads_per_row\":" << k.tpr << ",\"vector\":" << k.vec
       << ",\"chunks\":" << k.nch << ",\"smem_bytes\":" << k.smem_bytes << ",\"streaming\":" << (k.streaming ? "true" : "false")
-      << ",\"reductions\":" << k.reds.size() << "}";
+      << ",\"reductions\":" << k.reds.size() << ",\"row_phases\":" << k.row_phases << ",\"registers\":" << k.regs
+      << ",\"spill_bytes\":" << k.spill_bytes << "}";
   }
   j << "]}}";
   return j.str();

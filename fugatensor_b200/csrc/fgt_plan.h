@@ -109,6 +109,8 @@ struct KernelDef {
   int64_t send_offset = -1, recv_offset = -1, record_bytes = 0;
   std::string source;
   std::string signature;          // human-readable kernel summary
+  int row_phases = 0;             // ROW: dependency levels holding row reductions (block barriers per row)
+  int regs = -1, spill_bytes = -1;  // from the sm_100a compile (-1: unknown)
 };
 
 struct Options {
@@ -118,6 +120,7 @@ struct Options {
   int num_sms = 148;              // partial buffers are sized for this many SMs
   int max_ctas_per_sm = 8;
   int row_staging = 1;            // next row arrives via cp.async into shared memory (FGT_ROW_STAGING=0: registers)
+  int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
 };
 
 struct Plan {

@@ -12,6 +12,7 @@
 //     plan's kernels with caller-owned buffers and workspace.
 #include <nvrtc.h>
 
+#include <cctype>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -73,9 +74,48 @@ void mkdirs(const std::string& path) {
 }
 
 const char* kNvrtcOptions[] = {"-arch=sm_100a", "-fmad=false", "-std=c++17", "-default-device", "-lineinfo",
-                               "-prec-div=true", "-prec-sqrt=true", "-ftz=false"};
+                               "-prec-div=true", "-prec-sqrt=true", "-ftz=false", "-Xptxas=-v"};
 
-std::string compile_cubin(const std::string& name, const std::string& src, const std::string& cache_dir) {
+struct Compiled {
+  std::string cubin;
+  int regs = -1, spill_bytes = -1;  // from ptxas's verbose report (-1: not reported)
+};
+
+// ptxas -v reports "Used N registers" and "N bytes spill stores".
+void parse_ptxas_report(const std::string& log, Compiled* c) {
+  size_t p = log.find("Used ");
+  int v = 0;
+  if (p != std::string::npos && std::sscanf(log.c_str() + p, "Used %d registers", &v) == 1) c->regs = v;
+  p = log.find(" bytes spill stores");
+  if (p != std::string::npos) {
+    size_t b = p;
+    while (b > 0 && std::isdigit((unsigned char)log[b - 1])) --b;
+    if (b < p) c->spill_bytes = std::atoi(log.c_str() + b);
+  }
+}
+
+std::string read_file(const std::string& path) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return std::string();
+  std::stringstream ss;
+  ss << f.rdbuf();
+  return ss.str();
+}
+
+// Atomic publish: write a private file, then rename.
+void publish(const std::string& path, const std::string& data) {
+  const std::string tmp = path + ".tmp." + std::to_string(getpid());
+  {
+    std::ofstream f(tmp, std::ios::binary);
+    f.write(data.data(), (std::streamsize)data.size());
+  }
+  std::rename(tmp.c_str(), path.c_str());
+}
+
+// NVRTC compile of one kernel, cached on disk by a hash of the compiler
+// version, options and source. The ptxas register report is cached beside
+// the cubin (".regs": "<registers> <spill bytes>").
+Compiled compile_cubin(const std::string& name, const std::string& src, const std::string& cache_dir) {
   int maj = 0, min = 0;
   nvrtcVersion(&maj, &min);
   std::string opts;
@@ -84,14 +124,12 @@ std::string compile_cubin(const std::string& name, const std::string& src, const
   char hex[32];
   std::snprintf(hex, sizeof hex, "%016llx", (unsigned long long)fnv1a(key));
   const std::string path = cache_dir + "/" + name + "-" + hex + ".cubin";
-  {
-    std::ifstream f(path, std::ios::binary);
-    if (f) {
-      std::stringstream ss;
-      ss << f.rdbuf();
-      std::string data = ss.str();
-      if (!data.empty()) return data;
-    }
+  Compiled c;
+  c.cubin = read_file(path);
+  if (!c.cubin.empty()) {
+    std::string info = read_file(path + ".regs");
+    if (!info.empty()) std::sscanf(info.c_str(), "%d %d", &c.regs, &c.spill_bytes);
+    return c;
   }
   nvrtcProgram prog;
   if (nvrtcCreateProgram(&prog, src.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) != NVRTC_SUCCESS)
@@ -107,18 +145,14 @@ std::string compile_cubin(const std::string& name, const std::string& src, const
   }
   size_t n = 0;
   nvrtcGetCUBINSize(prog, &n);
-  std::string cubin(n, '\0');
-  nvrtcGetCUBIN(prog, &cubin[0]);
+  c.cubin.assign(n, '\0');
+  nvrtcGetCUBIN(prog, &c.cubin[0]);
   nvrtcDestroyProgram(&prog);
-  // Atomic publish: write a private file, then rename.
+  parse_ptxas_report(log, &c);
   mkdirs(cache_dir);
-  const std::string tmp = path + ".tmp." + std::to_string(getpid());
-  {
-    std::ofstream f(tmp, std::ios::binary);
-    f.write(cubin.data(), (std::streamsize)cubin.size());
-  }
-  std::rename(tmp.c_str(), path.c_str());
-  return cubin;
+  publish(path + ".regs", std::to_string(c.regs) + " " + std::to_string(c.spill_bytes) + "\n");
+  publish(path, c.cubin);
+  return c;
 }
 
 // ---------------------------------------------------------------- NCCL ----
@@ -409,15 +443,54 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
     // FGT_ROW_STAGING=0 keeps streamed row operands in registers
     // (double-buffered) instead of the shared-memory ring.
     if (const char* st = std::getenv("FGT_ROW_STAGING")) opt.row_staging = std::atoi(st) != 0;
+    bool row_elems_forced = false;
+    if (const char* re = std::getenv("FGT_ROW_ELEMS")) {
+      opt.row_elems = std::max(1, std::min(64, std::atoi(re)));
+      row_elems_forced = true;
+    }
     int sms = current_sm_count();
     if (sms > 0) opt.num_sms = sms;
     auto spec = std::make_unique<fgt_spec>();
-    spec->plan = make_plan(g, opt);
-    generate_sources(spec->plan);
     const std::string dir = cache_root(cache_dir);
-    for (auto& k : spec->plan.kernels) {
-      std::string src = std::string(fgt_device_library_source) + "\n" + k.source;
-      spec->cubins.push_back(compile_cubin(k.name, src, dir));
+    auto specialise = [&](const Options& o, Plan* plan, std::vector<std::string>* cubins) {
+      *plan = make_plan(g, o);
+      generate_sources(*plan);
+      cubins->clear();
+      for (auto& k : plan->kernels) {
+        Compiled c = compile_cubin(k.name, std::string(fgt_device_library_source) + "\n" + k.source, dir);
+        k.regs = c.regs;
+        k.spill_bytes = c.spill_bytes;
+        cubins->push_back(std::move(c.cubin));
+      }
+    };
+    specialise(opt, &spec->plan, &spec->cubins);
+    // Row geometry from the compile report. A block-per-row kernel of 512
+    // threads above 64 registers fits one CTA (16 warps) per SM. With a single
+    // barrier phase per row and no column partials, 8 elements per thread
+    // (1024 threads) then runs faster (measured on the broadcast-select
+    // workload: 74 -> 40 registers, 0.51 -> 0.62 of HBM peak); kernels with
+    // more phases lose more to the extra barriers per element than they gain.
+    if (!row_elems_forced && opt.row_elems > 8) {
+      bool retry = false;
+      for (auto& k : spec->plan.kernels) {
+        bool col = false;
+        for (auto& rd : k.reds) col = col || rd.role == ROLE_COL;
+        if (k.kind == KKind::ROW && k.tpr >= 512 && k.nt == 512 && k.regs > 64 && k.row_phases <= 1 && !col) retry = true;
+      }
+      if (retry) {
+        Options o8 = opt;
+        o8.row_elems = 8;
+        Plan p8;
+        std::vector<std::string> c8;
+        specialise(o8, &p8, &c8);
+        bool better = true;
+        for (auto& k : p8.kernels)
+          if (k.kind == KKind::ROW && (k.regs < 0 || k.regs > 64 || k.spill_bytes != 0)) better = false;
+        if (better) {
+          spec->plan = std::move(p8);
+          spec->cubins = std::move(c8);
+        }
+      }
     }
     spec->json = plan_json(spec->plan);
     *out = spec.release();

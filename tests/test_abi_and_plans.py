@@ -164,6 +164,8 @@ def test_full_size_workloads_specialise():
             main = lw["kernels"][0]
             if main["name"].startswith("fgt_row"):
                 assert main["streaming"] is False  # the row stays in registers
+            for k in lw["kernels"]:  # the sm_100a compile report travels with the plan
+                assert 0 < k["registers"] <= 255 and k["spill_bytes"] == 0, k
             assert spec.kernel_count == len(EXPECTED_KERNELS[(cfg, variant)])
 
 
