@@ -7,7 +7,7 @@ The native library (libfgt.so, C ABI in include/fgt.h) is loaded lazily on
 first compile/evaluate; ``import fugatensor_b200`` itself needs no GPU.
 """
 from .dtypes import DType, bool, int32, int64, fp32, fp16, bf16  # noqa: A004
-from .engine import Engine, current_engine, evaluate, get_default_device, set_default_device, synchronize, tensor
+from .engine import Engine, current_engine, evaluate, evaluate_host, get_default_device, set_default_device, synchronize, tensor
 from .tensor import Tensor
 from .autograd import grad, stop_gradient
 from .ops import (add, multiply, subtract, negative, square, abs, floor, ceil, round, cast, reshape,  # noqa: A004
@@ -18,6 +18,6 @@ from .ops import (add, multiply, subtract, negative, square, abs, floor, ceil, r
                   argmax, argmin, iota)
 from . import nn, ir  # noqa: F401
 
-__all__ = ["DType", "bool", "int32", "int64", "fp32", "fp16", "bf16", "Engine", "Tensor", "tensor", "evaluate",
+__all__ = ["DType", "bool", "int32", "int64", "fp32", "fp16", "bf16", "Engine", "Tensor", "tensor", "evaluate", "evaluate_host",
            "grad", "stop_gradient", "current_engine", "set_default_device", "get_default_device", "synchronize",
            "nn", "ir"]

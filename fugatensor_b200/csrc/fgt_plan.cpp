@@ -922,7 +922,13 @@ struct Planner {
     for (int o : g.outputs) mix(o);
     mix(opt.accumulation);
     mix(opt.world);
-    mix(opt.rank);
+    // The rank changes the code only through rank offsets (iota along the
+    // split axis, argmax/argmin indices over it); without them every rank's
+    // kernels are the same and share one name (and one cached cubin).
+    bool rank_offsets = !iota_offsets.empty();
+    for (const KernelDef& k : plan.kernels)
+      for (const RedDef& rd : k.reds) rank_offsets = rank_offsets || rd.index_offset != 0;
+    if (rank_offsets) mix(opt.rank);
     mix(opt.row_elems);
     mix(opt.row_staging);
     char tag[16];

@@ -45,6 +45,7 @@ class Engine:
         self.accumulation = accumulation
         self._lock = threading.RLock()
         self._cache = {}
+        self._stream_cache = {}
         self._stats = {"compilations": 0, "cache_hits": 0}
         self.stats = {"launches": 0, "program_submissions": 0}
         self.last_execution_plan = None
@@ -52,7 +53,10 @@ class Engine:
         self.last_spec = None
 
     # -- tensors -----------------------------------------------------------
-    def tensor(self, values, *, dtype=_dt.fp32, shape=None):
+    def tensor(self, values, *, dtype=_dt.fp32, shape=None, host=False):
+        """A leaf tensor. host=True keeps the values in pinned host memory until a
+        computation needs them (``evaluate`` uploads them; ``evaluate_host``
+        streams them row block by row block)."""
         import numpy as np
         import torch
         dtype = _dt.normalize(dtype)
@@ -69,7 +73,11 @@ class Engine:
         if shape is not None:
             data = data.reshape(tuple(shape))
         data = data.contiguous()
-        if torch.cuda.is_available():
+        if host:
+            data = data.cpu()
+            if torch.cuda.is_available():
+                data = data.pin_memory()
+        elif torch.cuda.is_available():
             data = data.to(self.device)
         return Tensor(self, dtype, tuple(data.shape), data=data)
 
@@ -170,6 +178,46 @@ class Engine:
             self.stats["program_submissions"] += 1
             return tensors[0] if len(tensors) == 1 else tensors
 
+    def evaluate_host(self, *tensors):
+        """Materialise `tensors` jointly into pinned host memory.
+
+        Row-local partitions (every output row depends only on the same rows of
+        the inputs split along dim 0) stream row blocks through three CUDA
+        streams, so uploads, kernels and downloads overlap; other partitions
+        are uploaded, run and downloaded whole. Returns when the host values
+        are ready."""
+        import torch
+        from . import _fgt, streaming
+        with self._lock:
+            desc, leaves, roots = self.trace(*tensors)
+            if not torch.cuda.is_available():
+                raise _fgt.CUDAError(4, "no CUDA device: fugatensor_b200 has no CPU execution path")
+            device = torch.device(self.device)
+            rs = streaming.plan(self, desc, leaves, roots) if roots else None
+            with torch.cuda.device(device):
+                if rs is None:
+                    if roots:
+                        self.evaluate(*tensors)
+                    for t in tensors:
+                        if t._data.is_cuda:
+                            h = torch.empty(t._data.shape, dtype=t._data.dtype, pin_memory=True)
+                            h.copy_(t._data, non_blocking=True)
+                            t._data = h
+                else:
+                    outs = streaming.run(self, rs, leaves, desc.output_types(), device)
+                    for r, o in zip(roots, outs):
+                        r._data = o
+                        r._expr = None
+                    plan = dict(rs.spec.execution_plan)
+                    lowering = plan.pop("cuda_lowering")
+                    self.last_execution_plan = plan
+                    self.last_report = {"cuda_lowering": lowering, "row_chunks": rs.chunks}
+                    self.last_spec = rs.spec
+                    self.stats["launches"] += rs.spec.kernel_count * rs.chunks
+                    self.stats["program_submissions"] += rs.chunks
+                torch.cuda.current_stream(device).synchronize()
+            return tensors[0] if len(tensors) == 1 else tensors
+
     def cache_info(self):
         with self._lock:
             return {"compilations": self._stats["compilations"], "cache_hits": self._stats["cache_hits"],
@@ -178,6 +226,7 @@ class Engine:
     def clear_cache(self):
         with self._lock:
             self._cache.clear()
+            self._stream_cache.clear()
             self.last_execution_plan = self.last_report = self.last_spec = None
 
 
@@ -265,14 +314,21 @@ def get_default_device():
     return _DEFAULT[0]
 
 
-def tensor(data, *, dtype=_dt.fp32, engine=None, device=None):
-    return (engine or current_engine(device)).tensor(data, dtype=dtype)
+def tensor(data, *, dtype=_dt.fp32, engine=None, device=None, host=False):
+    return (engine or current_engine(device)).tensor(data, dtype=dtype, host=host)
 
 
 def evaluate(*tensors):
     if not tensors:
         return None
     return tensors[0].engine.evaluate(*tensors)
+
+
+def evaluate_host(*tensors):
+    """Engine.evaluate_host on the tensors' engine."""
+    if not tensors:
+        return None
+    return tensors[0].engine.evaluate_host(*tensors)
 
 
 def synchronize():
