@@ -256,7 +256,7 @@ def run_fgt(args):
                     ms = statistics.median(times)
                     nb = W.algorithmic_bytes(c, v, r, h, dt)
                     partitions[f"{c}/{v}/{dt}"] = {"shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
-                                                   "frac": round(nb / ms / 1e6 / peak, 4), "kernels": spec.kernel_count,
+                                                   "frac": round(nb / ms / 1e6 / peak, 4), "kernels": spec.kernel_count, "geometry": list(spec.geometry),
                                                    "elements_per_s": round(r * h / (ms * 1e-3), 1)}
                     del L
                 del tt

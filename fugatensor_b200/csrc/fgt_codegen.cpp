@@ -505,10 +505,10 @@ struct Emitter {
           RowSite rs{s, ST, ptr, b, false};
           rs.bytes = K.vec * dtype_size(n.dt);
           // cp.async moves 4, 8 or 16 bytes; a stage (one row of every staged
-          // operand) must leave room for at least two stages in 227 KB.
+          // operand) must fit the ring budget.
           const int64_t piece = (int64_t)K.rows_per_cta * K.nch * K.tpr * rs.bytes;
           rs.staged = P.opt.row_staging && (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) &&
-                      stage_bytes + piece <= 96 * 1024;
+                      stage_bytes + piece <= (int64_t)P.opt.ring_kb * 1024;
           if (rs.staged) stage_bytes += piece;
           row_sites.push_back(rs);
         } else if (elem) {
@@ -966,8 +966,8 @@ struct Emitter {
     std::vector<RowSite*> staged_sites, reg_sites;
     for (auto& rs : row_sites) (rs.staged ? staged_sites : reg_sites).push_back(&rs);
     if (!staged_sites.empty()) {
-      // rows in flight per CTA: as many as fit ~96 KB (two CTAs per SM)
-      stages = (int)std::min<int64_t>(8, std::max<int64_t>(1, (96 * 1024) / std::max<int64_t>(1, stage_bytes)));
+      // rows in flight per CTA: as many as fit the ring budget (96 KB: two CTAs per SM)
+      stages = (int)std::min<int64_t>(8, std::max<int64_t>(1, ((int64_t)P.opt.ring_kb * 1024) / std::max<int64_t>(1, stage_bytes)));
       int64_t off = 0;
       for (auto* rs : staged_sites) {
         rs->smem_off = off;

@@ -931,6 +931,7 @@ struct Planner {
     if (rank_offsets) mix(opt.rank);
     mix(opt.row_elems);
     mix(opt.row_staging);
+    mix(opt.ring_kb);
     char tag[16];
     std::snprintf(tag, sizeof tag, "%08x", (unsigned)(h ^ (h >> 32)));
     for (size_t i = 0; i < plan.kernels.size(); ++i) {

@@ -121,6 +121,7 @@ struct Options {
   int max_ctas_per_sm = 8;
   int row_staging = 1;            // next row arrives via cp.async into shared memory (FGT_ROW_STAGING=0: registers)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
+  int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)
 };
 
 struct Plan {

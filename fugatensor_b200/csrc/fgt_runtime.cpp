@@ -275,7 +275,9 @@ LoadedModule& module_for(fgt_spec* s) {
     CUfunction f;
     cu_check(drv().ModuleGetFunction(&f, m, s->plan.kernels[i].name.c_str()), "cuModuleGetFunction");
     const int smem = (int)s->plan.kernels[i].smem_bytes;
-    if (smem > 48 * 1024)
+    // Dynamic plus static shared memory above 48 KB needs the opt-in; set it
+    // for every kernel with a ring (static reduction buffers come on top).
+    if (smem > 0)
       cu_check(drv().FuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, smem), "cuFuncSetAttribute");
     int occ = 1;
     cu_check(drv().OccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, s->plan.kernels[i].nt, (size_t)smem),
@@ -439,15 +441,20 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
         opt.shard_inputs = options->shard_inputs;
       }
       cache_dir = options->cache_dir;
+      require(options->row_elems >= 0 && options->row_elems <= 64, "row_elems must be in [0, 64]");
+      require(options->ring_kb >= 0 && options->ring_kb <= 200, "ring_kb must be in [0, 200]");
+      if (options->row_elems > 0) opt.row_elems = options->row_elems;
+      if (options->ring_kb > 0) opt.ring_kb = options->ring_kb;
     }
     // FGT_ROW_STAGING=0 keeps streamed row operands in registers
     // (double-buffered) instead of the shared-memory ring.
     if (const char* st = std::getenv("FGT_ROW_STAGING")) opt.row_staging = std::atoi(st) != 0;
-    bool row_elems_forced = false;
+    bool row_elems_forced = options && options->row_elems > 0;
     if (const char* re = std::getenv("FGT_ROW_ELEMS")) {
       opt.row_elems = std::max(1, std::min(64, std::atoi(re)));
       row_elems_forced = true;
     }
+    if (const char* rk = std::getenv("FGT_RING_KB")) opt.ring_kb = std::max(4, std::min(200, std::atoi(rk)));
     int sms = current_sm_count();
     if (sms > 0) opt.num_sms = sms;
     auto spec = std::make_unique<fgt_spec>();

@@ -40,9 +40,12 @@ def _normalize_device(device):
 class Engine:
     """One engine per CUDA device."""
 
-    def __init__(self, device="cuda:0", *, accumulation="wide"):
+    def __init__(self, device="cuda:0", *, accumulation="wide", tune=True):
         self.device = _normalize_device(device)
         self.accumulation = accumulation
+        # tune: measure the row-kernel geometry of large partitions on first
+        # compile (fugatensor_b200/tuning.py); False keeps the default geometry.
+        self.tune = tune
         self._lock = threading.RLock()
         self._cache = {}
         self._stream_cache = {}
@@ -144,7 +147,11 @@ class Engine:
         key = desc.key()
         spec = self._cache.get(key)
         if spec is None:
-            spec = _fgt.Spec(desc, accumulation=self.accumulation)
+            if self.tune:
+                from . import tuning
+                spec = tuning.select(desc, accumulation=self.accumulation, device=self.device)
+            else:
+                spec = _fgt.Spec(desc, accumulation=self.accumulation)
             self._cache[key] = spec
             self._stats["compilations"] += 1
         else:

@@ -323,7 +323,7 @@ class CPartition(ctypes.Structure):
                 ("outputs", ctypes.POINTER(ctypes.c_int32))]
 
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class Descriptor:

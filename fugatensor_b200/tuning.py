@@ -1,0 +1,142 @@
+"""Measured choice of row-kernel geometry per partition.
+
+Block-per-row kernels trade per-row work (barriers, reductions, ring
+management) against occupancy: more elements per thread amortise the
+per-row instructions but hold more registers, and a smaller shared-memory
+ring lets more CTAs share an SM. Which point is fastest depends on the
+partition (measured on B200: LayerNorm forward is fastest at 32 elements per
+thread with a 24 KB ring, the bf16 softmax VJP at 16 with a 32 KB ring), so
+the engine measures instead of guessing. The first compile of a large
+partition on a GPU builds the candidate geometries, times each on synthetic
+inputs of the partition's own types and shapes (CUDA events, L2 flushed
+between launches), and keeps the fastest. The choice is stored in
+``tuning.json`` in the kernel cache directory, keyed by the partition's
+structure, the GPU, and the library build, so later processes skip the
+measurement. All geometries compute the same results; only speed differs.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import threading
+from pathlib import Path
+
+from . import _fgt, ir
+
+# (elements per thread per row operand, shared-memory ring KB); (0, 0) is the library default.
+CANDIDATES = ((0, 0), (16, 32), (16, 24), (32, 96), (32, 32), (32, 24))
+MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
+_lock = threading.Lock()
+
+
+def _lib_tag():
+    st = os.stat(_fgt.LIB_PATH)
+    return f"{st.st_size}-{int(st.st_mtime)}"
+
+
+def _db_path(cache_dir):
+    return Path(cache_dir or _fgt.KERNEL_CACHE) / "tuning.json"
+
+
+def _load(path):
+    try:
+        return json.loads(path.read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def _store(path, key, value):
+    with _lock:
+        db = _load(path)
+        db[key] = value
+        path.parent.mkdir(parents=True, exist_ok=True)
+        tmp = path.with_suffix(f".tmp.{os.getpid()}")
+        tmp.write_text(json.dumps(db, indent=0, sort_keys=True))
+        os.replace(tmp, path)
+
+
+def _moved_bytes(desc):
+    n = 0
+    for dt, shape in list(desc.input_types()) + list(desc.output_types()):
+        k = ir.WIDTH[dt]
+        for s in shape:
+            k *= s
+        n += k
+    return n
+
+
+def _block_rows(spec):
+    return any(k["name"].startswith("fgt_row") and k["threads_per_row"] >= 256
+               for k in spec.execution_plan["cuda_lowering"]["kernels"])
+
+
+def _synthetic(dt, shape, device, gen):
+    import torch
+    tdt = _fgt.torch_dtype(dt)
+    if dt in ("f32", "f16", "bf16"):
+        return torch.randn(shape, device=device, generator=gen).to(tdt)
+    if dt == "bool":
+        return torch.rand(shape, device=device, generator=gen) < 0.5
+    return torch.randint(-1000, 1001, shape, device=device, generator=gen).to(tdt)
+
+
+def _time(spec, inputs, device, flush, reps=5):
+    import torch
+    outs = [torch.empty(s, dtype=_fgt.torch_dtype(dt), device=device) for dt, s in spec.output_types]
+    ws = torch.empty(max(spec.workspace_bytes, 1), dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    ptrs_in = [t.data_ptr() for t in inputs]
+    ptrs_out = [t.data_ptr() for t in outs]
+    times = []
+    for i in range(reps + 2):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        spec.launch(ptrs_in, ptrs_out, ws.data_ptr(), spec.workspace_bytes, stream.cuda_stream)
+        b.record(stream)
+        b.synchronize()
+        if i >= 2:
+            times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
+    """The spec of `desc` with the fastest measured row geometry (default geometry without a GPU)."""
+    import torch
+    default = _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir)
+    if not torch.cuda.is_available() or not _block_rows(default) or _moved_bytes(desc) < MIN_BYTES:
+        return default
+    dev = torch.device(device)
+    name = torch.cuda.get_device_name(dev)
+    key = hashlib.sha256(f"{desc.key()}|{accumulation}|{name}|{_lib_tag()}".encode()).hexdigest()[:32]
+    path = _db_path(cache_dir)
+    hit = _load(path).get(key)
+    if hit is not None:
+        e, r = hit["geometry"]
+        if (e, r) == (0, 0):
+            return default
+        return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r)
+    specs, seen = [], {}
+    for e, r in CANDIDATES:
+        s = default if (e, r) == (0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
+                                                       row_elems=e, ring_kb=r)
+        src = tuple(s.kernel_source(i) for i in range(s.kernel_count))
+        if src in seen:
+            continue
+        seen[src] = True
+        specs.append(((e, r), s))
+    if len(specs) == 1:
+        _store(path, key, {"geometry": [0, 0], "ms": None})
+        return default
+    gen = torch.Generator(device=dev).manual_seed(0)
+    with torch.cuda.device(dev):
+        inputs = [_synthetic(dt, s, dev, gen) for dt, s in default.input_types]
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        timed = [(_time(s, inputs, dev, flush), g, s) for g, s in specs]
+        del inputs, flush
+    ms, geom, best = min(timed, key=lambda t: t[0])
+    _store(path, key, {"geometry": list(geom), "ms": round(ms, 5),
+                       "candidates": {f"{g[0]}x{g[1]}": round(t, 5) for t, g, _ in timed}})
+    return best

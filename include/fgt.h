@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FGT_ABI_VERSION 1
+#define FGT_ABI_VERSION 2
 #define FGT_MAX_RANK 8
 #define FGT_MAX_OPERANDS 3
 
@@ -126,9 +126,13 @@ typedef struct fgt_spec_options {
   int32_t accumulation;       /* fgt_accumulation                                      */
   int32_t shard_world;        /* 0/1 = unsharded; N>1 = leading-dim shard over N ranks */
   int32_t shard_rank;
-  int32_t reserved;
+  int32_t row_elems;          /* block-per-row kernels: elements per thread per row    */
+                              /* operand (0: the library's choice)                     */
   uint64_t shard_inputs;      /* bit i set: input port i is split along dim 0          */
   const char* cache_dir;      /* compiled-kernel disk cache (NULL: FGT_CACHE_DIR env)  */
+  int32_t ring_kb;            /* row kernels: shared-memory row ring budget per CTA in */
+                              /* KB (0: the library's choice, 96)                      */
+  int32_t reserved;
 } fgt_spec_options;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
