@@ -336,6 +336,7 @@ struct Emitter {
   const Graph& g;
   const KernelDef& K;
   int row_phases = 0;  // levels holding row reductions (one block barrier each per row)
+  std::map<std::string, std::pair<std::string, Sc>> unrounded;  // bf16 temp -> (f32 expression, scope)
   const Domain& d;
   std::set<int64_t>* temps_loaded;
   std::vector<RedDef> fin_reds;
@@ -651,6 +652,11 @@ struct Emitter {
     else fail(FGT_ERR_UNSUPPORTED, std::string("generator cannot place ") + opcode_name(n.op));
     std::string v = fresh("t");
     add(D, "const " + vt_t(n.dt) + " " + v + " = " + expr + ";");
+    // A bf16 value is the rounding of an f32 expression; a store of it may
+    // round pairs at once instead (store_stmt_elem).
+    static const std::string kRnd = "fgt_rnd_bf16(";
+    if (n.dt == FGT_BF16 && expr.compare(0, kRnd.size(), kRnd) == 0 && expr.back() == ')')
+      unrounded[v] = {expr.substr(kRnd.size(), expr.size() - kRnd.size() - 1), D};
     return v;
   }
 
@@ -693,6 +699,15 @@ struct Emitter {
     std::string ptr = ptr_of(st.node, true, st.port, st.temp_offset);
     std::string base;
     if (contiguous(A, &base)) {
+      auto un = unrounded.find(v);
+      if (n.dt == FGT_BF16 && K.vec % 2 == 0 && un != unrounded.end() && un->second.second.k == SC_LANE &&
+          un->second.second.p == phase) {
+        // the unrounded f32 values go out in pairs, rounded by the packed conversion
+        std::string ob = fresh("obf");
+        chunkpre[phase].push_back("float " + ob + "[" + std::to_string(K.vec) + "];");
+        chunkpost[phase].push_back("fgt_vstore_bf16_rn(" + ptr + " + " + base + " + e0, " + ob + ");");
+        return ob + "[v] = " + un->second.first + ";";
+      }
       std::string ob = fresh("ob");
       chunkpre[phase].push_back(st_t(n.dt) + " " + ob + "[" + std::to_string(K.vec) + "];");
       chunkpost[phase].push_back("fgt_vstore(" + ptr + " + " + base + " + e0, " + ob + ");");

@@ -221,6 +221,16 @@ template <class T, int N> FGT_DEV void fgt_vstore(T* __restrict__ dst, const T (
   for (int k = 0; k < N; ++k) u.e[k] = src[k];
   __stcs(reinterpret_cast<V*>(dst), u.v);
 }
+// Store N f32 values rounded to bf16: each pair is rounded and packed by one
+// cvt.rn.bf16x2.f32 (the same RNE as the one-value rounding).
+template <int N> FGT_DEV void fgt_vstore_bf16_rn(fgt_u16* __restrict__ dst, const float (&src)[N]) {
+  static_assert(N % 2 == 0, "pairs");
+  typedef typename fgt_vec_t<2 * N>::type V;
+  union { V v; fgt_u32 w[N / 2]; } u;
+#pragma unroll
+  for (int k = 0; k < N / 2; ++k) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(u.w[k]) : "f"(src[2 * k + 1]), "f"(src[2 * k]));
+  __stcs(reinterpret_cast<V*>(dst), u.v);
+}
 
 // --------------------------------------------- shared-memory row staging ---
 // Streamed row operands are copied global -> shared with cp.async in a ring of
