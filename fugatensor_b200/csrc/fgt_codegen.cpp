@@ -337,6 +337,9 @@ struct Emitter {
   const KernelDef& K;
   int row_phases = 0;  // levels holding row reductions (one block barrier each per row)
   std::map<std::string, std::pair<std::string, Sc>> unrounded;  // bf16 temp -> (f32 expression, scope)
+  std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
+  std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
+  std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
   const Domain& d;
   std::set<int64_t>* temps_loaded;
   std::vector<RedDef> fin_reds;
@@ -640,7 +643,20 @@ struct Emitter {
           memo[rk] = rcp;
           add(db, "const float " + rcp + " = fgt_recip_for_div(" + a[1] + ");");
         }
-        expr = rnd(n.dt, "fgt_div_by(" + a[0] + "," + a[1] + "," + rcp + ")");
+        if (D.k == SC_LANE) {
+          // Per element: the corrected reciprocal product, and a note of |q|
+          // in the phase's range trackers. The phase is redone with IEEE
+          // division by any thread whose trackers leave the range where the
+          // product is exact (see the phase assembly in build_row); kernels
+          // that cannot redo a phase get the per-element guarded form.
+          const std::string q = fresh("q");
+          add(D, "const float " + q + " = @DIVQ@(" + a[0] + "," + a[1] + "," + rcp + ");");
+          add(D, "@NOTE@(" + q + ");");
+          div_phases.insert(D.p);
+          expr = rnd(n.dt, q);
+        } else {
+          expr = rnd(n.dt, "fgt_div_by(" + a[0] + "," + a[1] + "," + rcp + ")");
+        }
       }
     }
     if (!expr.empty()) {
@@ -873,6 +889,10 @@ struct Emitter {
       // k % 4), folded pairwise before the group combine: four dependent
       // chains instead of one. Storage-dtype accumulation keeps one chain.
       const bool chains = !t.arg && !t.storage && !K.streaming && K.nch * K.vec >= 4;
+      resets[p].push_back(a + " = " + t.ident + ";");
+      if (t.arg) resets[p].push_back(a + "i = " + t.identi + ";");
+      if (chains)
+        for (int k = 0; k < 4; ++k) resets[p].push_back(a + "_s[" + std::to_string(k) + "] = " + t.ident + ";");
       if (t.arg) {
         lane[p].push_back("{ const fgt_i64 ix = " + arg_index(*rd) + "; " + scan_stmt(t, a, a + "i", v, "ix") + " }");
       } else if (chains) {
@@ -915,6 +935,7 @@ struct Emitter {
     for (auto* rd : cols) {
       RedText t = red_text(g, rd->node, P.opt.accumulation, CTX_COL);
       int p = cphase[rd];
+      col_phases.insert(p);
       std::string a = fresh("cacc");
       std::string dims = "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "]";
       kdecl.push_back(t.acc_t + " " + a + dims + ";");
@@ -1054,21 +1075,41 @@ struct Emitter {
       o << "    }\n";
     }
     put(o, rowdecl, "    ");
+    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind) {
+      if (cached) o << ind << "  #pragma unroll\n";
+      else o << ind << "  #pragma unroll 1\n";
+      o << ind << "  for (int c = 0; c < " << NCH << "; ++c) {\n";
+      o << ind << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << ind << "    if (e0 < NI) {\n";
+      put(o, chunkpre[p], ind + "      ");
+      o << ind << "      #pragma unroll\n" << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+      put(o, body, ind + "        ");
+      o << ind << "      }\n";
+      put(o, chunkpost[p], ind + "      ");
+      o << ind << "    }\n" << ind << "  }\n";
+    };
     for (int p = 0; p < nphase; ++p) {
       put(o, rowsc[p], "    ");
+      // Divisions of a phase without column updates are checked once per
+      // thread and phase: trackers of min/max |q| (NaN propagates into the
+      // max); a thread whose quotients left the exact range resets its row
+      // accumulators and redoes the phase with IEEE division. Redoing is
+      // safe: the phase's other effects (cached values, element stores) are
+      // overwritten with the same values.
+      const bool track = div_phases.count(p) && !col_phases.count(p) && cached;
+      const std::string dx = "dgx" + std::to_string(p), dn = "dgn" + std::to_string(p);
+      if (track) o << "    float " << dx << " = 0.0f, " << dn << " = __int_as_float(0x7f800000);\n";
       o << "    if (rv) {\n";
-      if (cached) o << "      #pragma unroll\n";
-      else o << "      #pragma unroll 1\n";
-      o << "      for (int c = 0; c < " << NCH << "; ++c) {\n";
-      o << "        const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      o << "        if (e0 < NI) {\n";
-      put(o, chunkpre[p], "          ");
-      o << "          #pragma unroll\n          for (int v = 0; v < " << VEC << "; ++v) {\n";
-      o << "            const fgt_i64 e = e0 + v; " << digits_i() << "\n";
-      put(o, lane[p], "            ");
-      o << "          }\n";
-      put(o, chunkpost[p], "          ");
-      o << "        }\n      }\n    }\n";
+      phase_loop(p, div_form(lane[p], track ? "fgt_div_q" : "fgt_div_by", track ? "fgt_div_note(" + dx + ", " + dn + ", " : ""),
+                 "    ");
+      o << "    }\n";
+      if (track) {
+        o << "    if (rv && !fgt_div_ok(" << dx << ", " << dn << ")) {\n";
+        put(o, resets[p], "      ");
+        phase_loop(p, div_form(lane[p], "fgt_div_ieee", ""), "    ");
+        o << "    }\n";
+      }
       put(o, post[p], "    ");
     }
     put(o, rowsc[nphase], "    ");
@@ -1299,10 +1340,36 @@ struct Emitter {
     return o.str();
   }
 
+  // Lane statements with the division placeholders resolved: @DIVQ@ becomes
+  // `fn`, and the @NOTE@(q) statements become `note` + "q);" (dropped when
+  // note is empty).
+  static std::vector<std::string> div_form(const std::vector<std::string>& v, const std::string& fn,
+                                           const std::string& note) {
+    std::vector<std::string> out;
+    for (const std::string& s0 : v) {
+      std::string s = s0;
+      if (s.compare(0, 7, "@NOTE@(") == 0) {
+        if (!note.empty()) out.push_back(note + s.substr(7));
+        continue;
+      }
+      for (size_t at; (at = s.find("@DIVQ@")) != std::string::npos;) s.replace(at, 6, fn);
+      out.push_back(s);
+    }
+    return out;
+  }
+
   std::string build() {
-    if (row) return build_row();
-    if (elem) return build_elem();
-    return build_fin();
+    std::string src = row ? build_row() : elem ? build_elem() : build_fin();
+    // kernels without per-phase tracking keep the per-element guarded division
+    std::istringstream in(src);
+    std::ostringstream out;
+    for (std::string line; std::getline(in, line);) {
+      const size_t k = line.find_first_not_of(' ');
+      if (k != std::string::npos && line.compare(k, 7, "@NOTE@(") == 0) continue;
+      for (size_t at; (at = line.find("@DIVQ@")) != std::string::npos;) line.replace(at, 6, "fgt_div_by");
+      out << line << "\n";
+    }
+    return out.str();
   }
 };
 

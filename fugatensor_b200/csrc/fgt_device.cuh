@@ -123,6 +123,22 @@ FGT_DEV float fgt_div_by(float x, float d, float y) {
   const float a = fabsf(q2);
   return (a >= 7.52316385e-37f && a <= 1.32922800e+36f) ? q2 : __fdiv_rn(x, d);
 }
+// The same corrected product without the guard, for phases that check the
+// range once per thread (fgt_div_note / fgt_div_ok) and redo the phase with
+// IEEE division (fgt_div_ieee) when a quotient left it. NaN in the max
+// tracker (max.NaN) and zero or tiny quotients in the min tracker fail the
+// check, so every case the guard sends to __fdiv_rn is redone.
+FGT_DEV float fgt_div_q(float x, float d, float y) {
+  const float q = __fmul_rn(x, y);
+  const float r = __fmaf_rn(-q, d, x);
+  return __fmaf_rn(r, y, q);
+}
+FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
+  mx = fgt_fmax(mx, fabsf(q));
+  mn = fminf(mn, fabsf(q));
+}
+FGT_DEV bool fgt_div_ok(float mx, float mn) { return mx <= 1.32922800e+36f && mn >= 7.52316385e-37f; }
+FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 template <class T> FGT_DEV T fgt_imax(T a, T b) { return a > b ? a : b; }
 template <class T> FGT_DEV T fgt_imin(T a, T b) { return a < b ? a : b; }
 

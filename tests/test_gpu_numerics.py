@@ -89,3 +89,39 @@ def test_narrowing_casts_are_rne_bitwise(dtype):
         nan = np.isnan(got) & np.isnan(ref)
     mism = (gb != rb) & ~nan
     assert not mism.any(), f"{mism.sum()} mismatches, e.g. x={x[mism][:4]} got={gb[mism][:4]} ref={rb[mism][:4]}"
+
+
+def test_phase_redo_on_out_of_range_quotients():
+    """Row phases check their quotients once per thread; threads whose quotients leave the
+    exact range (zero, signed zero, subnormal, huge, inf, NaN, subnormal divisor) redo the
+    phase with IEEE division. Quotients stay bitwise IEEE, the phase's row sums and maxima
+    are rebuilt from scratch, and benign rows beside them are unaffected."""
+    from tests._util import assert_matches
+    rng = np.random.default_rng(3)
+    rows, cols = 600, 4096
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    d = (rng.random((rows, 1)) + 0.5).astype(np.float32)
+    x[3, 7] = -0.0
+    x[5, :] = 0.0
+    x[9, 100] = np.inf
+    x[11, 5] = 1e-38
+    x[13, 9] = np.nan
+    x[17, 1] = 3e38
+    d[19, 0] = 1e-39
+    d[21, 0] = 0.0
+    x[300:310, 4000] = -1e-40
+    X, D = ft.tensor(x), ft.tensor(d)
+    q = X / ft.broadcast_to(D, X.shape)
+    s = ft.sum(q, axis=1)
+    m = ft.amax(q, axis=1)
+    desc, leaves, roots = q.engine.trace(q, s, m)
+    ref_q, ref_s, ref_m = O.evaluate(desc, [x, d])
+    ft.evaluate(q, s, m)
+    got_q, got_s, got_m = q.numpy(), s.numpy(), m.numpy()
+    nan = np.isnan(got_q) & np.isnan(ref_q)
+    assert not ((_bits(got_q) != _bits(ref_q)) & ~nan).any()
+    nan = np.isnan(got_m) & np.isnan(ref_m)
+    assert not ((_bits(got_m) != _bits(ref_m)) & ~nan).any()
+    fin = np.isfinite(ref_s)
+    assert np.array_equal(np.isnan(got_s), np.isnan(ref_s)) and np.array_equal(got_s[~fin & ~np.isnan(ref_s)], ref_s[~fin & ~np.isnan(ref_s)])
+    assert_matches(got_s[fin], ref_s[fin], "f32", what="row sums of quotients")
