@@ -127,6 +127,10 @@ std::string cast_expr(int from, int to, const std::string& a) {
   if (is_int(from) && is_int(to)) return "((" + vt_t(to) + ")(" + a + "))";
   if (is_int(from)) {
     if (to == FGT_F32) return "((float)(" + a + "))";
+    // From i32: f16 overflows below 2^24, where the f32 image is still exact,
+    // so one f32 conversion and one f16 rounding suffice; bf16 needs the
+    // round-to-odd image, taken in 32 bits.
+    if (from == FGT_I32) return to == FGT_F16 ? "fgt_i32_to_f16v(" + a + ")" : "fgt_i32_to_bf16v(" + a + ")";
     if (to == FGT_F16) return "fgt_i64_to_f16v((fgt_i64)(" + a + "))";
     return "fgt_i64_to_bf16v((fgt_i64)(" + a + "))";
   }
@@ -152,7 +156,14 @@ std::string binary_expr(int op, int dt, const std::string& a, const std::string&
   const bool f = is_float(dt);
   switch (op) {
     case FGT_OP_ADD: return f ? rnd(dt, "__fadd_rn(" + a + "," + b + ")") : "fgt_wrap_add<" + T + "," + U + ">(" + a + "," + b + ")";
-    case FGT_OP_MUL: return f ? rnd(dt, "__fmul_rn(" + a + "," + b + ")") : "fgt_wrap_mul<" + T + "," + U + ">(" + a + "," + b + ")";
+    case FGT_OP_MUL: {
+      if (!f) return "fgt_wrap_mul<" + T + "," + U + ">(" + a + "," + b + ")";
+      // x * (+-1) of a value exact in its dtype is exact (it is how the
+      // reference spells negation and subtraction), so it needs no rounding.
+      static const std::string one = "__uint_as_float(0x3f800000u)", neg = "__uint_as_float(0xbf800000u)";
+      if (a == one || a == neg || b == one || b == neg) return "__fmul_rn(" + a + "," + b + ")";
+      return rnd(dt, "__fmul_rn(" + a + "," + b + ")");
+    }
     case FGT_OP_DIV: return rnd(dt, "__fdiv_rn(" + a + "," + b + ")");
     case FGT_OP_MAXIMUM:
       if (f) return "fgt_fmax(" + a + "," + b + ")";
@@ -836,6 +847,9 @@ struct Emitter {
   }
 
   std::string build_row() {
+    // every chunk of the row is in range when the row is a whole number of
+    // thread-chunks; the bound check is then left out
+    const std::string CHK = d.NI % ((int64_t)K.tpr * K.vec) == 0 ? "if (true)" : "if (e0 < NI)";
     // Phases: one element loop per dependency level of the row reductions.
     std::vector<const RedDef*> rows, cols;
     for (auto& rd : K.reds) (rd.role == ROLE_ROW ? rows : cols).push_back(&rd);
@@ -986,7 +1000,7 @@ struct Emitter {
     if (cached && !prolane.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      o << "    if (e0 < NI) {\n";
+      o << "    " << CHK << " {\n";
       put(o, prosites, "      ");
       o << "      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
@@ -1014,7 +1028,7 @@ struct Emitter {
     auto chunk_loop = [&](std::ostringstream& os, const std::string& ind, const std::function<void(const std::string&)>& body) {
       os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
       os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      os << ind << "  if (e0 < NI) {\n";
+      os << ind << "  " << CHK << " {\n";
       body(ind + "    ");
       os << ind << "  }\n" << ind << "}\n";
     };
@@ -1080,7 +1094,7 @@ struct Emitter {
       else o << ind << "  #pragma unroll 1\n";
       o << ind << "  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << ind << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      o << ind << "    if (e0 < NI) {\n";
+      o << ind << "    " << CHK << " {\n";
       put(o, chunkpre[p], ind + "      ");
       o << ind << "      #pragma unroll\n" << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
@@ -1132,7 +1146,7 @@ struct Emitter {
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
-      o << "    if (e0 < NI) {\n      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << "    " << CHK << " {\n      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << "        const fgt_i64 e = e0 + v;\n";
       put(o, colfin, "        ");
       o << "      }\n    }\n  }\n";

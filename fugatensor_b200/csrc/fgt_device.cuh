@@ -67,6 +67,17 @@ FGT_DEV float fgt_i64_to_f32_odd(fgt_i64 x) {
 }
 FGT_DEV float fgt_i64_to_f16v(fgt_i64 x) { return fgt_rnd_f16(fgt_i64_to_f32_odd(x)); }
 FGT_DEV float fgt_i64_to_bf16v(fgt_i64 x) { return fgt_rnd_bf16(fgt_i64_to_f32_odd(x)); }
+// i32 -> f16: |x| < 2^24 converts to f32 exactly (one f16 rounding follows);
+// |x| >= 2^24 is beyond f16's range and rounds to +-inf either way.
+FGT_DEV float fgt_i32_to_f16v(int x) { return fgt_rnd_f16((float)x); }
+FGT_DEV float fgt_i32_to_bf16v(int x) {
+  float t;
+  asm("cvt.rz.f32.s32 %0, %1;" : "=f"(t) : "r"(x));
+  int back;
+  asm("cvt.rzi.s32.f32 %0, %1;" : "=r"(back) : "f"(t));
+  if (back != x) t = __uint_as_float(__float_as_uint(t) | 1u);
+  return fgt_rnd_bf16(t);
+}
 
 // Round-to-odd f32 image of a double (same single-rounding argument).
 FGT_DEV float fgt_f64_to_f32_odd(double d) {
