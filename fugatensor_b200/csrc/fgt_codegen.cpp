@@ -347,6 +347,8 @@ struct Emitter {
   const Graph& g;
   const KernelDef& K;
   int row_phases = 0;  // levels holding row reductions (one block barrier each per row)
+  bool parity_rows = false;  // row reductions alternate two partial buffers (it_ counts rows)
+  std::vector<std::string> rowpf, rowpf_first, rowpf_next;  // row-scope loads, one row ahead
   std::map<std::string, std::pair<std::string, Sc>> unrounded;  // bf16 temp -> (f32 expression, scope)
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
@@ -497,6 +499,17 @@ struct Emitter {
     }
     if (D.k == SC_ROW) {
       std::string v = fresh("w");
+      if (row && cached) {
+        // Loaded one row ahead: the raw value of row r+stride is requested
+        // while row r is computed, and converted when that row starts.
+        const std::string pf = v + "_pf";
+        kdecl.push_back(ST + " " + pf + " = (" + ST + ")0;");
+        const std::string ld = pf + " = rv ? " + ptr + "[" + itext(A) + "] : (" + ST + ")0;";
+        rowpf_first.push_back(ld);
+        rowpf_next.push_back(ld);
+        rowpf.push_back("const " + VT + " " + v + " = " + ld_conv(n.dt, pf) + ";");
+        return v;
+      }
       add(D, "const " + VT + " " + v + " = rv ? " + ld_conv(n.dt, ptr + "[" + itext(A) + "]") + " : (" + VT + ")0;");
       return v;
     }
@@ -754,7 +767,11 @@ struct Emitter {
   // another barrier always lies between this read and that write.
   void group_reduce(std::vector<std::string>& out, const std::vector<std::pair<RedText, std::string>>& accs,
                     int TW, bool cross_warp, int NW, const std::string& tag, bool butterfly = false,
-                    bool trailing_sync = true) {
+                    bool trailing_sync = true, bool parity = false) {
+    // parity: two partial buffers used on alternate rows (it_ & 1), so the
+    // next row writes the other buffer and no trailing barrier is needed.
+    const std::string PB = parity ? "[it_ & 1]" : "";
+    const std::string PD = parity ? "[2]" : "";
     if (accs.empty()) return;
     out.push_back("#pragma unroll");
     out.push_back("for (int m_ = 1; m_ < " + std::to_string(TW) + "; m_ <<= 1) {");
@@ -769,21 +786,21 @@ struct Emitter {
     out.push_back("}");
     if (!cross_warp) return;
     for (auto& [t, a] : accs) {
-      kdecl.push_back("__shared__ " + t.acc_t + " sm_" + a + tag + "[" + std::to_string(NW) + "];");
-      if (t.arg) kdecl.push_back("__shared__ fgt_i64 smi_" + a + tag + "[" + std::to_string(NW) + "];");
+      kdecl.push_back("__shared__ " + t.acc_t + " sm_" + a + tag + PD + "[" + std::to_string(NW) + "];");
+      if (t.arg) kdecl.push_back("__shared__ fgt_i64 smi_" + a + tag + PD + "[" + std::to_string(NW) + "];");
     }
     out.push_back("if ((tid & 31) == 0) {");
     for (auto& [t, a] : accs) {
-      out.push_back("  sm_" + a + tag + "[tid >> 5] = " + a + ";");
-      if (t.arg) out.push_back("  smi_" + a + tag + "[tid >> 5] = " + a + "i;");
+      out.push_back("  sm_" + a + tag + PB + "[tid >> 5] = " + a + ";");
+      if (t.arg) out.push_back("  smi_" + a + tag + PB + "[tid >> 5] = " + a + "i;");
     }
     out.push_back("}");
     out.push_back("__syncthreads();");
     if (butterfly && NW > 1 && (NW & (NW - 1)) == 0 && NW <= 32) {
       const std::string mask = std::to_string(NW - 1);
       for (auto& [t, a] : accs) {
-        out.push_back(a + " = sm_" + a + tag + "[tid & " + mask + "];");
-        if (t.arg) out.push_back(a + "i = smi_" + a + tag + "[tid & " + mask + "];");
+        out.push_back(a + " = sm_" + a + tag + PB + "[tid & " + mask + "];");
+        if (t.arg) out.push_back(a + "i = smi_" + a + tag + PB + "[tid & " + mask + "];");
       }
       out.push_back("#pragma unroll");
       out.push_back("for (int m_ = 1; m_ < " + std::to_string(NW) + "; m_ <<= 1) {");
@@ -927,10 +944,12 @@ struct Emitter {
     }
     // With two or more cross-warp phases per row, the barrier of the next
     // phase separates each phase's partial reads from its next row's writes.
-    const bool trailing = phase_accs.size() < 2;
+    // A single cross-warp phase alternates two partial buffers by row instead.
+    const bool single = phase_accs.size() == 1 && xw && (NW & (NW - 1)) == 0;
+    parity_rows = single;
     row_phases = (int)phase_accs.size();
     for (auto& [p, accs] : phase_accs) {
-      group_reduce(post[p], accs, TW, xw, NW, "_p" + std::to_string(p), true, trailing);
+      group_reduce(post[p], accs, TW, xw, NW, "_p" + std::to_string(p), true, false, single);
     }
     for (auto* rd : rows) {
       int p = rphase[rd->node];
@@ -1081,8 +1100,21 @@ struct Emitter {
       o << "  }\n";
       if (stages) o << "  int stg = " << (stages > 1 ? 1 : 0) << ";\n";
     }
+    if (!rowpf_first.empty()) {
+      o << "  { const fgt_i64 r = (fgt_i64)blockIdx.x * " << RPC << " + grp; const bool rv = r < NR; " << digits_o() << "\n";
+      put(o, rowpf_first, "    ");
+      o << "  }\n";
+    }
+    if (parity_rows) o << "  int it_ = 0;\n";
     o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
     o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
+    if (!rowpf.empty()) {
+      put(o, rowpf, "    ");
+      o << "    { const fgt_i64 rpf_ = r + " << stride << ";\n";
+      o << "      { const fgt_i64 r = rpf_; const bool rv = r < NR; " << digits_o() << "\n";
+      put(o, rowpf_next, "        ");
+      o << "      }\n    }\n";
+    }
     if (!reg_sites.empty()) {
       o << "    const fgt_i64 rn_ = r + " << stride << ";\n    if (rn_ < NR) {\n";
       reg_loads(o, "      ", "rn_", true);
@@ -1141,6 +1173,7 @@ struct Emitter {
       o << "      }\n      fgt_cp_commit();\n    }\n";
       o << "    stg = stg + 1 == " << S << " ? 0 : stg + 1;\n";
     }
+    if (parity_rows) o << "    ++it_;\n";
     o << "  }\n";
     if (stages) o << "  fgt_cp_wait<0>();\n";
     if (!colfin.empty()) {
