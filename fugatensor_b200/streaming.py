@@ -25,6 +25,14 @@ from . import _fgt, ir
 # Chunk size target: inputs plus outputs of one chunk.
 CHUNK_BYTES = 64 << 20
 BUFFERS = 3  # device buffer sets in rotation
+WHOLE_LIMIT = 16 << 30  # partitions above this are not specialised whole (no device-size tuning run)
+
+
+def _moved_bytes(desc):
+    n = 0
+    for dt, shape in list(desc.input_types()) + list(desc.output_types()):
+        n += ir.WIDTH[dt] * _numel(shape)
+    return n
 
 
 def _width(dt):
@@ -72,17 +80,17 @@ def _chunk_count(R, row_bytes, chunk_bytes):
 class RowStream:
     """Chunk specs of one partition (cached per engine)."""
 
-    def __init__(self, desc, rows, split, chunks, accumulation):
+    def __init__(self, desc, rows, split, chunks, accumulation, geometry=(0, 0)):
         self.rows, self.split, self.chunks = rows, split, chunks
-        first = _fgt.Spec(desc, accumulation=accumulation, world=chunks, rank=0, shard_inputs=split)
-        second = _fgt.Spec(desc, accumulation=accumulation, world=chunks, rank=1, shard_inputs=split)
+        e, r = geometry
+        mk = lambda k: _fgt.Spec(desc, accumulation=accumulation, world=chunks, rank=k, shard_inputs=split,
+                                 row_elems=e, ring_kb=r)
+        first, second = mk(0), mk(1)
         names = lambda s: [k["name"] for k in s.execution_plan["cuda_lowering"]["kernels"]]
         if names(first) == names(second):
             self.specs = [first] * chunks  # no rank offsets: one spec serves every chunk
         else:
-            self.specs = [first, second] + [
-                _fgt.Spec(desc, accumulation=accumulation, world=chunks, rank=k, shard_inputs=split)
-                for k in range(2, chunks)]
+            self.specs = [first, second] + [mk(k) for k in range(2, chunks)]
         self.spec = first
 
 
@@ -97,7 +105,14 @@ def plan(engine, desc, leaves, roots):
             row_bytes = sum(_width(dt) * _numel(s[1:]) for i, (dt, s) in enumerate(in_types) if i in split)
             row_bytes += sum(_width(dt) * _numel(s[1:]) for dt, s in out_types)
             chunks = _chunk_count(R, row_bytes, CHUNK_BYTES)
-            rs = RowStream(desc, R, split, chunks, engine.accumulation) if chunks else None
+            # The chunks run the row geometry the engine chose for the whole
+            # partition, so streamed results equal evaluate()'s bit for bit
+            # (the geometry fixes each row's summation order). Partitions too
+            # large to measure on the device keep the default geometry.
+            geometry = (0, 0)
+            if _moved_bytes(desc) <= WHOLE_LIMIT:
+                geometry = engine._spec(desc).geometry
+            rs = RowStream(desc, R, split, chunks, engine.accumulation, geometry) if chunks else None
         engine._stream_cache[key] = rs
     return rs
 
