@@ -350,6 +350,7 @@ struct Emitter {
   bool parity_rows = false;  // row reductions alternate two partial buffers (it_ counts rows)
   std::vector<std::string> rowpf, rowpf_first, rowpf_next;  // row-scope loads, one row ahead
   std::map<std::string, std::pair<std::string, Sc>> unrounded;  // bf16 temp -> (f32 expression, scope)
+  std::map<std::string, std::string> texpr;  // temp -> its defining expression
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
@@ -692,6 +693,7 @@ struct Emitter {
     else fail(FGT_ERR_UNSUPPORTED, std::string("generator cannot place ") + opcode_name(n.op));
     std::string v = fresh("t");
     add(D, "const " + vt_t(n.dt) + " " + v + " = " + expr + ";");
+    texpr[v] = expr;
     // A bf16 value is the rounding of an f32 expression; a store of it may
     // round pairs at once instead (store_stmt_elem).
     static const std::string kRnd = "fgt_rnd_bf16(";
@@ -920,7 +922,37 @@ struct Emitter {
       // k % 4), folded pairwise before the group combine: four dependent
       // chains instead of one. Storage-dtype accumulation keeps one chain.
       const bool chains = !t.arg && !t.storage && !K.streaming && K.nch * K.vec >= 4;
+      // max/min of a widened bf16 register row: packed bf16x2 max/min over
+      // the row's 32-bit words (exact: no rounding), folded into the f32
+      // accumulator after the phase.
+      std::string pk_site;
+      {
+        auto te = texpr.find(v);
+        const std::string& ex = te == texpr.end() ? v : te->second;
+        static const std::string pre = "fgt_bf16_to_f32(", suf = "[c][v])";
+        if ((t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN) && t.fl && !t.storage && cached && K.vec % 2 == 0 &&
+            ex.size() > pre.size() + suf.size() && ex.compare(0, pre.size(), pre) == 0 &&
+            ex.compare(ex.size() - suf.size(), suf.size(), suf) == 0) {
+          const std::string site = ex.substr(pre.size(), ex.size() - pre.size() - suf.size());
+          for (auto& rs : row_sites)
+            if (rs.name == site && rs.st == "fgt_u16" && !rs.uniform) pk_site = site;
+        }
+      }
       resets[p].push_back(a + " = " + t.ident + ";");
+      if (!pk_site.empty()) {
+        const bool mx = t.op == FGT_OP_REDUCE_MAX;
+        const std::string init = mx ? "0xff80ff80u" : "0x7f807f80u";
+        rowsc[p].push_back("fgt_u32 " + a + "_pk = " + init + ";");
+        resets[p].push_back(a + "_pk = " + init + ";");
+        chunkpost[p].push_back(a + "_pk = fgt_" + (mx ? std::string("max") : std::string("min")) + "_bf16x2_row(" + a + "_pk, " +
+                               pk_site + "[c]);");
+        post[p].push_back(comb_stmt(t, a, "fgt_bf16_to_f32((fgt_u16)(" + a + "_pk & 0xffffu))"));
+        post[p].push_back(comb_stmt(t, a, "fgt_bf16_to_f32((fgt_u16)(" + a + "_pk >> 16))"));
+        phase_accs[p].push_back({t, a});
+        acc_of[rd->node] = a;
+        red_var[rd->node] = fresh("red");
+        continue;
+      }
       if (t.arg) resets[p].push_back(a + "i = " + t.identi + ";");
       if (chains)
         for (int k = 0; k < 4; ++k) resets[p].push_back(a + "_s[" + std::to_string(k) + "] = " + t.ident + ";");
@@ -1121,17 +1153,20 @@ struct Emitter {
       o << "    }\n";
     }
     put(o, rowdecl, "    ");
-    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind) {
+    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind,
+                          const std::vector<std::string>& vpre = {}, const std::vector<std::string>& vpost = {}) {
       if (cached) o << ind << "  #pragma unroll\n";
       else o << ind << "  #pragma unroll 1\n";
       o << ind << "  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << ind << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
       o << ind << "    " << CHK << " {\n";
       put(o, chunkpre[p], ind + "      ");
+      put(o, vpre, ind + "      ");
       o << ind << "      #pragma unroll\n" << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
       put(o, body, ind + "        ");
       o << ind << "      }\n";
+      put(o, vpost, ind + "      ");
       put(o, chunkpost[p], ind + "      ");
       o << ind << "    }\n" << ind << "  }\n";
     };

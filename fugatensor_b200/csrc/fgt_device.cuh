@@ -150,6 +150,27 @@ FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
 }
 FGT_DEV bool fgt_div_ok(float mx, float mn) { return mx <= 1.32922800e+36f && mn >= 7.52316385e-37f; }
 FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
+// Max / min of a packed accumulator with a register row piece of N bf16
+// values, two values per instruction (max.NaN / min.NaN on bf16x2: NaN wins,
+// exact otherwise). The halves are folded into the f32 accumulator later.
+template <int N> FGT_DEV fgt_u32 fgt_max_bf16x2_row(fgt_u32 acc, const fgt_u16 (&h)[N]) {
+  static_assert(N % 2 == 0, "pairs");
+#pragma unroll
+  for (int k = 0; k < N; k += 2) {
+    const fgt_u32 w = (fgt_u32)h[k] | ((fgt_u32)h[k + 1] << 16);
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(acc) : "r"(acc), "r"(w));
+  }
+  return acc;
+}
+template <int N> FGT_DEV fgt_u32 fgt_min_bf16x2_row(fgt_u32 acc, const fgt_u16 (&h)[N]) {
+  static_assert(N % 2 == 0, "pairs");
+#pragma unroll
+  for (int k = 0; k < N; k += 2) {
+    const fgt_u32 w = (fgt_u32)h[k] | ((fgt_u32)h[k + 1] << 16);
+    asm("min.NaN.bf16x2 %0, %1, %2;" : "=r"(acc) : "r"(acc), "r"(w));
+  }
+  return acc;
+}
 template <class T> FGT_DEV T fgt_imax(T a, T b) { return a > b ? a : b; }
 template <class T> FGT_DEV T fgt_imin(T a, T b) { return a < b ? a : b; }
 

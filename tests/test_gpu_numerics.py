@@ -125,3 +125,31 @@ def test_phase_redo_on_out_of_range_quotients():
     fin = np.isfinite(ref_s)
     assert np.array_equal(np.isnan(got_s), np.isnan(ref_s)) and np.array_equal(got_s[~fin & ~np.isnan(ref_s)], ref_s[~fin & ~np.isnan(ref_s)])
     assert_matches(got_s[fin], ref_s[fin], "f32", what="row sums of quotients")
+
+
+def test_bf16_row_max_min_packed_ieee():
+    """Row max/min of widened bf16 rows run on packed bf16x2 words; they keep the IEEE
+    maximum/minimum of the reference (NaN wins, +0 above -0) bit for bit."""
+    rng = np.random.default_rng(21)
+    rows, cols = 16, 4096
+    x = (rng.standard_normal((rows, cols)) * 4).astype(np.float32)
+    x[0, :] = -0.0
+    x[1, :] = -0.0
+    x[1, 1234] = 0.0
+    x[2, :] = 0.0
+    x[2, 77] = -0.0
+    x[3, 999] = np.nan
+    x[4, :] = -np.inf
+    x[5, :] = np.inf
+    x[6, 4095] = np.nan
+    x[7, :] = -1e-40  # subnormal f32 -> bf16 subnormal
+    bits = O.f32_to_bf16_bits(x)
+    X = ft.tensor(bits, dtype=ft.bf16)
+    w = X.astype(ft.fp32)
+    mx, mn = ft.amax(w, axis=1), ft.amin(w, axis=1)
+    desc, leaves, roots = X.engine.trace(mx, mn)
+    ref = O.evaluate(desc, [bits])
+    ft.evaluate(mx, mn)
+    for got, want in zip((mx.numpy(), mn.numpy()), ref):
+        nan = np.isnan(got) & np.isnan(want)
+        assert not ((_bits(got) != _bits(want)) & ~nan).any(), (got[:8], want[:8])
