@@ -15,7 +15,8 @@ from .ops import (add, multiply, subtract, negative, square, abs, floor, ceil, r
                   exp, log, sqrt, sin, cos, tanh, erf, logical_and, logical_or, logical_xor, logical_not,
                   bitwise_and, bitwise_or, bitwise_xor, bitwise_not, shift_left, shift_right, broadcast_in_dim,
                   broadcast_to, transpose, squeeze, unsqueeze, flatten, sum, amax, amin, prod, mean, any, all,
-                  argmax, argmin, iota)
+                  argmax, argmin, iota, slice, pad, concatenate, cat, stack, split, chunk, gather, take,
+                  scatter_add, getitem, one_hot)
 from . import nn, ir  # noqa: F401
 
 __all__ = ["DType", "bool", "int32", "int64", "fp32", "fp16", "bf16", "Engine", "Tensor", "tensor", "evaluate", "evaluate_host",

@@ -10,12 +10,14 @@ together.
 """
 from __future__ import annotations
 
+import builtins as _builtins
 import math
 
 from . import dtypes as _dt
 from .tensor import Tensor, _prim
 
 FLOAT = ("f32", "f16", "bf16")
+_builtins_any = _builtins.any
 
 
 class DifferentiationError(RuntimeError):
@@ -175,6 +177,67 @@ def _vjp(t, g, active):
             return [None, None]
         return [g if active[0] else None,
                 _neg(_prim("mul", (g, _prim("floordiv", (x, y))))) if active[1] else None]
+    # index transforms (src/fugatensor/ir/tensor_rules.py:521-640)
+    if op == "slice":
+        x = args[0]
+        if x.dtype.ir not in FLOAT:
+            return [None]
+        starts, _, steps = attrs
+        out = t.shape
+        if 0 in out:
+            return [_filled(x.dtype, x.shape, 0, e)]
+        if _builtins_any(st < 0 for st in steps):
+            # reverse the cotangent along the reversed axes first
+            g = _prim("slice", (g,), (tuple(n - 1 if st < 0 else 0 for n, st in zip(out, steps)),
+                                     tuple(-1 if st < 0 else n for n, st in zip(out, steps)),
+                                     tuple(-1 if st < 0 else 1 for st in steps)))
+        low, high, inner = [], [], []
+        for dim, n, st0, step in zip(x.shape, out, starts, steps):
+            first = st0 if step > 0 else st0 + (n - 1) * step
+            low.append(first)
+            inner.append(abs(step) - 1)
+            high.append(dim - 1 - (first + (n - 1) * abs(step)))
+        zero = _filled(x.dtype, (), 0, e)
+        return [_prim("pad", (g, zero), (tuple(low), tuple(high), tuple(inner)))]
+    if op == "pad":
+        x, pv = args
+        if x.dtype.ir not in FLOAT:
+            return [None, None]
+        low, _, inner = attrs
+        dx = dpv = None
+        if active[0]:
+            starts = tuple(l if d > 0 else 0 for d, l in zip(x.shape, low))
+            stops = tuple(l + (d - 1) * (i + 1) + 1 if d > 0 else 0 for d, l, i in zip(x.shape, low, inner))
+            steps = tuple(i + 1 for i in inner)
+            dx = _prim("slice", (g,), (starts, stops, steps)) if x.ndim else g
+        if active[1]:
+            mask = _prim("pad", (_filled(x.dtype, x.shape, 0, e), _filled(x.dtype, (), 1, e)), attrs)
+            dpv = _prim("reduce_sum", (_prim("mul", (g, mask)),), (tuple(range(g.ndim)),)) if g.ndim else g
+        return [dx, dpv]
+    if op == "concatenate":
+        if args[0].dtype.ir not in FLOAT:
+            return [None] * len(args)
+        ax = attrs[0]
+        out, at = [], 0
+        for a, act in zip(args, active):
+            n = a.shape[ax]
+            if act:
+                starts = tuple(at if k == ax else 0 for k in range(g.ndim))
+                stops = tuple(at + n if k == ax else s for k, s in enumerate(g.shape))
+                out.append(_prim("slice", (g,), (starts, stops, (1,) * g.ndim)) if n else _filled(a.dtype, a.shape, 0, e))
+            else:
+                out.append(None)
+            at += n
+        return out
+    if op == "gather":
+        p, ix = args
+        if not active[0] or p.dtype.ir not in FLOAT:
+            return [None, None]
+        return [_prim("scatter_add", (_filled(p.dtype, p.shape, 0, e), ix, g), (attrs[0],)), None]
+    if op == "scatter_add":
+        if args[0].dtype.ir not in FLOAT:
+            return [None, None, None]
+        return [g if active[0] else None, None, _prim("gather", (g, args[1]), (attrs[0],)) if active[2] else None]
     # compare, argmax/argmin, iota, constant, floor/ceil/round, bitwise...: zero derivative
     if op in ("floor", "ceil", "round"):
         return [None]

@@ -493,6 +493,13 @@ struct Emitter {
     Idx A = to_linear(m, n.shape, d);
     const std::string ptr = ptr_of(id);
     const std::string VT = vt_t(n.dt), ST = st_t(n.dt);
+    if (!m.guard.empty()) {
+      // below pad / concatenate / gather: read only where the guard holds
+      std::string v = fresh("x");
+      add(D, "const " + VT + " " + v + " = (" + m.guard + ") ? " + ld_conv(n.dt, "__ldg(" + ptr + " + " + itext(A) + ")") +
+                 " : (" + VT + ")0;");
+      return v;
+    }
     if (D.k == SC_PRO) {
       std::string v = fresh("g");
       add(D, "const " + VT + " " + v + " = " + ld_conv(n.dt, ptr + "[" + itext(A) + "]") + ";");
@@ -591,7 +598,7 @@ struct Emitter {
     else {
       require(s.k == SC_LANE, "internal: element value requested outside an element loop", FGT_ERR_UNSUPPORTED);
       D = {SC_LANE, s.p};
-      if (cached && s.p > L.phase && expensive(g.nodes[id].op)) D = {SC_CACHE, L.phase};
+      if (cached && s.p > L.phase && expensive(g.nodes[id].op) && m.guard.empty()) D = {SC_CACHE, L.phase};
     }
     if (s.k == SC_PROLANE && D.k == SC_LANE) D = s;
     std::string key = std::to_string(id) + "@" + m.key() + "#" + std::to_string((int)D.k) + ":" + std::to_string(D.p);
@@ -639,9 +646,52 @@ struct Emitter {
       case FGT_OP_RESHAPE:
       case FGT_OP_BROADCAST_IN_DIM:
       case FGT_OP_TRANSPOSE:
+      case FGT_OP_SLICE:
       case FGT_OP_STOP_GRADIENT: {
         auto ms = operand_maps(g, id, m, d);
         return val(n.args[0], ms[0], D);
+      }
+      case FGT_OP_PAD: {
+        auto ms = operand_maps(g, id, m, d);
+        const std::string xv = val(n.args[0], ms[0], D), pv = val(n.args[1], ms[1], D);
+        const std::string cond = pad_condition(g, id, m, d);
+        if (cond.empty()) return xv;
+        std::string v = fresh("t");
+        add(D, "const " + vt_t(n.dt) + " " + v + " = (" + cond + ") ? " + xv + " : " + pv + ";");
+        return v;
+      }
+      case FGT_OP_CONCATENATE: {
+        auto ms = operand_maps(g, id, m, d);
+        const std::string av = val(n.args[0], ms[0], D), bv = val(n.args[1], ms[1], D);
+        std::string v = fresh("t");
+        add(D, "const " + vt_t(n.dt) + " " + v + " = (" + concat_condition(g, id, m, d) + ") ? " + av + " : " + bv + ";");
+        return v;
+      }
+      case FGT_OP_SCATTER_ADD: {
+        // the kernel that completes the scatter: base + accumulator, one
+        // rounding to the dtype (integers wrap)
+        require(id == K.scatter_node && K.scatter_stage == 3, "internal: scatter_add read before it is complete",
+                FGT_ERR_UNSUPPORTED);
+        const std::string bv = val(n.args[0], m, D);
+        const std::string av = scatter_acc_ptr() + "[" + itext(to_linear(m, n.shape, d)) + "]";
+        std::string expr;
+        if (n.dt == FGT_F32) expr = "__double2float_rn((double)" + bv + " + " + av + ")";
+        else if (is_float(n.dt)) expr = rnd(n.dt, "fgt_f64_to_f32_odd((double)" + bv + " + " + av + ")");
+        else expr = "fgt_wrap_add<" + vt_t(n.dt) + "," + ut_t(n.dt) + ">(" + bv + ", (" + vt_t(n.dt) + ")" + av + ")";
+        std::string v = fresh("t");
+        add(D, "const " + vt_t(n.dt) + " " + v + " = " + expr + ";");
+        return v;
+      }
+      case FGT_OP_GATHER: {
+        auto ms = operand_maps(g, id, m, d);
+        const std::string gx = gather_index_name(id, m);
+        const std::string iv = val(n.args[1], ms[1], D);
+        add(D, "const fgt_i64 " + gx + " = (fgt_i64)(" + iv + ");");
+        const std::string pv = val(n.args[0], ms[0], D);
+        std::string v = fresh("t");
+        add(D, "const " + vt_t(n.dt) + " " + v + " = (" + gx + ">=0LL&&" + gx + "<" +
+                   std::to_string(g.nodes[n.args[0]].shape[n.attrs[0]]) + "LL) ? " + pv + " : (" + vt_t(n.dt) + ")0;");
+        return v;
       }
       default:
         break;
@@ -1223,6 +1273,16 @@ struct Emitter {
     return o.str();
   }
 
+  // scatter_add accumulator type and pointer text
+  std::string scatter_acc_t() const {
+    const Node& n = g.nodes[K.scatter_node];
+    if (is_float(n.dt)) return "double";
+    return n.dt == FGT_I64 ? "unsigned long long" : "int";
+  }
+  std::string scatter_acc_ptr() const {
+    return "((" + scatter_acc_t() + "*)(p.ws+" + std::to_string(K.scatter_acc) + "LL))";
+  }
+
   std::string build_elem() {
     nphase = 1;
     rowsc.assign(2, {});
@@ -1232,6 +1292,31 @@ struct Emitter {
     post.assign(1, {});
     std::vector<std::pair<RedText, std::string>> accs;
     std::vector<std::string> partial_store;
+    if (K.scatter_stage == 1) lane[0].push_back(scatter_acc_ptr() + "[e] = 0;");
+    if (K.scatter_stage == 2) {
+      // updates domain: base offset of update i = its coordinates with the
+      // scattered axis replaced by indices[i]
+      const Node& n = g.nodes[K.scatter_node];
+      const Node& base = g.nodes[n.args[0]];
+      const Node& up = g.nodes[n.args[2]];
+      const int ax = (int)n.attrs[0], ir = g.nodes[n.args[1]].rank();
+      Map mu;
+      mu.lin = true;
+      mu.l = idx_const(d.nd(), 0);
+      for (int j = 0; j < d.nd(); ++j) mu.l.c[j] = d.iw[j];
+      auto C = to_coords(mu, up.shape, d);
+      Map mi;
+      for (int k = 0; k < ir; ++k) mi.co.push_back(C[ax + k]);
+      const std::string uv = val(n.args[2], mu, Sc{SC_LANE, 0});
+      const std::string iv = val(n.args[1], mi, Sc{SC_LANE, 0});
+      auto bst = row_major_strides(base.shape);
+      std::string off = "gi_*" + std::to_string(bst[ax]) + "LL";
+      for (int k = 0; k < ax; ++k) off += "+" + itext(C[k]) + "*" + std::to_string(bst[k]) + "LL";
+      for (int k = ax + 1; k < base.rank(); ++k) off += "+" + itext(C[k - 1 + ir]) + "*" + std::to_string(bst[k]) + "LL";
+      const std::string A = scatter_acc_t();
+      lane[0].push_back("{ const fgt_i64 gi_ = (fgt_i64)(" + iv + "); if (gi_ >= 0LL && gi_ < " + std::to_string(base.shape[ax]) +
+                        "LL) atomicAdd(" + scatter_acc_ptr() + " + (" + off + "), (" + A + ")(" + uv + ")); }");
+    }
     for (auto& rd : K.reds) {
       RedText t = red_text(g, rd.node, P.opt.accumulation, CTX_FULL);
       std::string a = fresh("acc");

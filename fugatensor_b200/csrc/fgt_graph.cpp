@@ -64,6 +64,11 @@ const char* opcode_name(int op) {
     case FGT_OP_REDUCE_ALL: return "reduce_all";
     case FGT_OP_ARGMAX: return "argmax";
     case FGT_OP_ARGMIN: return "argmin";
+    case FGT_OP_SLICE: return "slice";
+    case FGT_OP_PAD: return "pad";
+    case FGT_OP_CONCATENATE: return "concatenate";
+    case FGT_OP_GATHER: return "gather";
+    case FGT_OP_SCATTER_ADD: return "scatter_add";
   }
   return "unknown";
 }
@@ -80,7 +85,7 @@ bool valid_dtype(int dt) { return dt >= FGT_BOOL && dt <= FGT_BF16; }
 bool valid_opcode(int op) {
   return (op >= FGT_OP_PARAMETER && op <= FGT_OP_CAST) || (op >= FGT_OP_ADD && op <= FGT_OP_SHIFT_RIGHT) ||
          (op >= FGT_OP_EXP && op <= FGT_OP_BITWISE_NOT) || op == FGT_OP_COMPARE || op == FGT_OP_SELECT ||
-         (op >= FGT_OP_REDUCE_SUM && op <= FGT_OP_ARGMIN);
+         (op >= FGT_OP_REDUCE_SUM && op <= FGT_OP_ARGMIN) || (op >= FGT_OP_SLICE && op <= FGT_OP_SCATTER_ADD);
 }
 
 std::string where(int id, const Node& n) {
@@ -164,6 +169,78 @@ void infer(const Graph& g, int id) {
       require(arg(1).dt == arg(2).dt && arg(1).shape == arg(2).shape, w + ": select values must match");
       same_as(arg(1));
       return;
+    // index transforms: ir/tensor_rules.py:124-237
+    case FGT_OP_SLICE: {
+      nargs(1);
+      const Node& x = arg(0);
+      const int r = x.rank();
+      require(x.dt == n.dt && n.rank() == r && (int)n.attrs.size() == 2 * r, w + ": slice needs starts and steps per axis");
+      for (int j = 0; j < r; ++j) {
+        const int64_t st = n.attrs[j], step = n.attrs[r + j], out = n.shape[j], dim = x.shape[j];
+        require(step != 0, w + ": slice step must be nonzero");
+        require(out >= 0, w + ": slice extent");
+        if (out == 0) continue;
+        const int64_t last = st + (out - 1) * step;
+        require(st >= 0 && st < dim && last >= 0 && last < dim, w + ": slice bounds out of range");
+      }
+      return;
+    }
+    case FGT_OP_PAD: {
+      nargs(2);
+      const Node& x = arg(0);
+      const int r = x.rank();
+      require(arg(1).shape.empty() && arg(1).dt == x.dt && n.dt == x.dt,
+              w + ": pad requires a 0-D scalar pad_value with the same dtype as input");
+      require(n.rank() == r && (int)n.attrs.size() == 2 * r, w + ": pad needs low and interior per axis");
+      for (int j = 0; j < r; ++j) {
+        const int64_t lo = n.attrs[j], inn = n.attrs[r + j], dim = x.shape[j];
+        require(lo >= 0 && inn >= 0, w + ": pad amounts and interior dilation must be nonnegative");
+        const int64_t inner = dim > 0 ? dim + (dim - 1) * inn : 0;
+        require(n.shape[j] >= lo + inner, w + ": pad high must be nonnegative");
+      }
+      return;
+    }
+    case FGT_OP_CONCATENATE: {
+      nargs(2);
+      const Node &a = arg(0), &b = arg(1);
+      require(n.attrs.size() == 1 && a.rank() >= 1 && n.attrs[0] >= 0 && n.attrs[0] < a.rank(),
+              w + ": concatenate axis out of range");
+      require(a.dt == b.dt && a.rank() == b.rank() && n.dt == a.dt && n.rank() == a.rank(),
+              w + ": concatenate operands must match rank and dtype");
+      const int ax = (int)n.attrs[0];
+      for (int j = 0; j < a.rank(); ++j)
+        require(j == ax ? n.shape[j] == a.shape[j] + b.shape[j] : (a.shape[j] == b.shape[j] && n.shape[j] == a.shape[j]),
+                w + ": concatenate non-axis dimensions must match");
+      return;
+    }
+    case FGT_OP_GATHER: {
+      nargs(2);
+      const Node &p = arg(0), &ix = arg(1);
+      require(p.rank() >= 1 && n.attrs.size() == 1 && n.attrs[0] >= 0 && n.attrs[0] < p.rank(),
+              w + ": gather axis out of range");
+      require(is_int(ix.dt), w + ": gather indices must have i32 or i64 dtype");
+      const int ax = (int)n.attrs[0];
+      Shape want(p.shape.begin(), p.shape.begin() + ax);
+      want.insert(want.end(), ix.shape.begin(), ix.shape.end());
+      want.insert(want.end(), p.shape.begin() + ax + 1, p.shape.end());
+      require(n.dt == p.dt && n.shape == want, w + ": gather result type mismatch");
+      return;
+    }
+    case FGT_OP_SCATTER_ADD: {
+      nargs(3);
+      const Node &b = arg(0), &ix = arg(1), &u = arg(2);
+      require(b.rank() >= 1 && n.attrs.size() == 1 && n.attrs[0] >= 0 && n.attrs[0] < b.rank(),
+              w + ": scatter_add axis out of range");
+      require(b.dt != FGT_BOOL, w + ": scatter_add base must have a numeric dtype");
+      require(is_int(ix.dt), w + ": scatter_add indices must have i32 or i64 type");
+      const int ax = (int)n.attrs[0];
+      Shape want(b.shape.begin(), b.shape.begin() + ax);
+      want.insert(want.end(), ix.shape.begin(), ix.shape.end());
+      want.insert(want.end(), b.shape.begin() + ax + 1, b.shape.end());
+      require(u.dt == b.dt && u.shape == want, w + ": scatter_add updates shape/dtype does not match base, indices and axis");
+      same_as(b);
+      return;
+    }
     default:
       break;
   }
@@ -257,7 +334,7 @@ Graph build_graph(const fgt_partition_desc* desc) {
     require(valid_dtype(s.dtype), "node " + std::to_string(i) + ": unknown dtype");
     require(s.rank >= 0 && s.rank <= FGT_MAX_RANK, "node " + std::to_string(i) + ": rank out of range");
     require(s.num_operands >= 0 && s.num_operands <= FGT_MAX_OPERANDS, "node " + std::to_string(i) + ": operand count");
-    require(s.num_attrs >= 0 && s.num_attrs <= FGT_MAX_RANK, "node " + std::to_string(i) + ": attr count");
+    require(s.num_attrs >= 0 && s.num_attrs <= FGT_MAX_ATTRS, "node " + std::to_string(i) + ": attr count");
     n.op = s.opcode;
     n.dt = s.dtype;
     for (int k = 0; k < s.rank; ++k) {

@@ -31,6 +31,7 @@ std::string Map::key() const {
   std::string s = lin ? "L" + l.key() : "C";
   if (!lin)
     for (const Idx& i : co) s += "|" + i.key();
+  if (!guard.empty()) s += "?" + guard;
   return s;
 }
 
@@ -174,19 +175,83 @@ bool idx_is_digit(const Idx& a, int digit) {
   return true;
 }
 
+// Affine helpers for the index transforms.
+static Idx idx_affine(const Idx& a, int64_t scale, int64_t shift, const Domain& d) {
+  if (a.aff) {
+    Idx r = a;
+    for (auto& c : r.c) c *= scale;
+    r.k = r.k * scale + shift;
+    return r;
+  }
+  return idx_opaque("(" + idx_text(a, d) + "*" + std::to_string(scale) + "LL+" + std::to_string(shift) + "LL)", a.dep_o,
+                    a.dep_i);
+}
+
+// A map that carries m's guard (and its digit dependence) plus `cond`.
+static Map guarded(Map x, const Map& m, const std::string& cond, bool o, bool i) {
+  x.guard = m.guard;
+  x.gdep_o = m.gdep_o;
+  x.gdep_i = m.gdep_i;
+  if (!cond.empty()) {
+    x.guard = x.guard.empty() ? cond : "(" + x.guard + ")&&(" + cond + ")";
+    x.gdep_o = x.gdep_o || o;
+    x.gdep_i = x.gdep_i || i;
+  }
+  return x;
+}
+
+std::string pad_condition(const Graph& g, int id, const Map& m, const Domain& d) {
+  const Node& n = g.nodes[id];
+  const Node& x = g.nodes[n.args[0]];
+  const int r = x.rank();
+  auto C = to_coords(m, n.shape, d);
+  std::string cond;
+  for (int j = 0; j < r; ++j) {
+    const int64_t lo = n.attrs[j], inn = n.attrs[r + j], dim = x.shape[j];
+    if (lo == 0 && inn == 0 && n.shape[j] == dim) continue;
+    const std::string t = "(" + idx_text(C[j], d) + "-" + std::to_string(lo) + "LL)";
+    std::string c = t + ">=0LL";
+    if (inn == 0) c += "&&" + t + "<" + std::to_string(dim) + "LL";
+    else c += "&&" + t + "%" + std::to_string(inn + 1) + "LL==0LL&&" + t + "/" + std::to_string(inn + 1) + "LL<" +
+              std::to_string(dim) + "LL";
+    cond += (cond.empty() ? "" : "&&") + c;
+  }
+  return cond;
+}
+
+std::string concat_condition(const Graph& g, int id, const Map& m, const Domain& d) {
+  const Node& n = g.nodes[id];
+  const int ax = (int)n.attrs[0];
+  auto C = to_coords(m, n.shape, d);
+  return idx_text(C[ax], d) + "<" + std::to_string(g.nodes[n.args[0]].shape[ax]) + "LL";
+}
+
+// The gathered index of gather node `id` read at map m, as a variable name
+// that the generator declares (fgt_i64) where the gather is evaluated.
+std::string gather_index_name(int id, const Map& m) {
+  uint64_t h = 1469598103934665603ULL;
+  for (char ch : std::to_string(id) + "@" + m.key()) {
+    h ^= (unsigned char)ch;
+    h *= 1099511628211ULL;
+  }
+  char b[32];
+  std::snprintf(b, sizeof b, "gx%016llx", (unsigned long long)h);
+  return b;
+}
+
 // Operand maps of a view / elementwise node evaluated at map m.
 std::vector<Map> operand_maps(const Graph& g, int id, const Map& m, const Domain& d) {
   const Node& n = g.nodes[id];
   std::vector<Map> r;
   switch (n.op) {
     case FGT_OP_SPLAT:
-      r.push_back(Map{});
+      r.push_back(guarded(Map{}, m, "", false, false));
       return r;
     case FGT_OP_RESHAPE: {
       Map x;
       x.lin = true;
       x.l = to_linear(m, n.shape, d);
-      r.push_back(x);
+      r.push_back(guarded(x, m, "", false, false));
       return r;
     }
     case FGT_OP_BROADCAST_IN_DIM: {
@@ -195,7 +260,7 @@ std::vector<Map> operand_maps(const Graph& g, int id, const Map& m, const Domain
       Map xm;
       for (int a = 0; a < x.rank(); ++a)
         xm.co.push_back(x.shape[a] == 1 ? idx_const(d.nd(), 0) : C[n.attrs[a]]);
-      r.push_back(xm);
+      r.push_back(guarded(xm, m, "", false, false));
       return r;
     }
     case FGT_OP_TRANSPOSE: {
@@ -204,7 +269,67 @@ std::vector<Map> operand_maps(const Graph& g, int id, const Map& m, const Domain
       Map xm;
       xm.co.assign(x.rank(), idx_const(d.nd(), 0));
       for (int i = 0; i < n.rank(); ++i) xm.co[n.attrs[i]] = C[i];
-      r.push_back(xm);
+      r.push_back(guarded(xm, m, "", false, false));
+      return r;
+    }
+    case FGT_OP_SLICE: {
+      // operand coordinate = start + step * result coordinate (always in range)
+      auto C = to_coords(m, n.shape, d);
+      const int rk = n.rank();
+      Map xm;
+      for (int j = 0; j < rk; ++j) xm.co.push_back(idx_affine(C[j], n.attrs[rk + j], n.attrs[j], d));
+      r.push_back(guarded(xm, m, "", false, false));
+      return r;
+    }
+    case FGT_OP_PAD: {
+      const Node& x = g.nodes[n.args[0]];
+      const int rk = x.rank();
+      auto C = to_coords(m, n.shape, d);
+      Map xm;
+      bool o = false, i = false;
+      for (int j = 0; j < rk; ++j) {
+        const int64_t lo = n.attrs[j], inn = n.attrs[rk + j];
+        const Idx t = idx_affine(C[j], 1, -lo, d);
+        if (inn == 0) xm.co.push_back(t);
+        else xm.co.push_back(idx_opaque("(" + idx_text(t, d) + "/" + std::to_string(inn + 1) + "LL)", idx_dep_o(t, d),
+                                        idx_dep_i(t, d)));
+        if (lo != 0 || inn != 0 || n.shape[j] != x.shape[j]) {
+          o = o || idx_dep_o(C[j], d);
+          i = i || idx_dep_i(C[j], d);
+        }
+      }
+      r.push_back(guarded(xm, m, pad_condition(g, id, m, d), o, i));
+      r.push_back(guarded(Map{}, m, "", false, false));  // the rank-0 pad value
+      return r;
+    }
+    case FGT_OP_CONCATENATE: {
+      const int ax = (int)n.attrs[0];
+      auto C = to_coords(m, n.shape, d);
+      const std::string first = concat_condition(g, id, m, d);
+      const bool o = idx_dep_o(C[ax], d), i = idx_dep_i(C[ax], d);
+      Map am, bm;
+      am.co = C;
+      bm.co = C;
+      bm.co[ax] = idx_affine(C[ax], 1, -g.nodes[n.args[0]].shape[ax], d);
+      r.push_back(guarded(am, m, first, o, i));
+      r.push_back(guarded(bm, m, "!(" + first + ")", o, i));
+      return r;
+    }
+    case FGT_OP_GATHER: {
+      // params[..., indices[i...], ...]; the gathered coordinate is a value
+      // (a variable the generator declares), and it may be out of range
+      const Node& p = g.nodes[n.args[0]];
+      const Node& ix = g.nodes[n.args[1]];
+      const int ax = (int)n.attrs[0], ir = ix.rank();
+      auto C = to_coords(m, n.shape, d);
+      Map im, pm;
+      for (int k = 0; k < ir; ++k) im.co.push_back(C[ax + k]);
+      const std::string gx = gather_index_name(id, m);
+      for (int k = 0; k < ax; ++k) pm.co.push_back(C[k]);
+      pm.co.push_back(idx_opaque(gx, true, true));
+      for (int k = ax + 1; k < p.rank(); ++k) pm.co.push_back(C[k - 1 + ir]);
+      r.push_back(guarded(pm, m, gx + ">=0LL&&" + gx + "<" + std::to_string(p.shape[ax]) + "LL", true, true));
+      r.push_back(guarded(im, m, "", false, false));
       return r;
     }
     default:
@@ -255,6 +380,14 @@ Graph shard_graph(const Graph& G, const Options& opt, std::set<int>* combine,
         if (ax(0) >= 0)
           for (int k = 0; k < n.rank(); ++k)
             if (n.attrs[k] == ax(0)) axis[i] = k;
+        break;
+      case FGT_OP_SLICE:
+      case FGT_OP_PAD:
+      case FGT_OP_CONCATENATE:
+      case FGT_OP_GATHER:
+      case FGT_OP_SCATTER_ADD:
+        for (size_t k = 0; k < n.args.size(); ++k)
+          require(ax((int)k) < 0, std::string(opcode_name(n.op)) + " of a sharded value is not supported", FGT_ERR_UNSUPPORTED);
         break;
       default:
         if (is_reduction(n.op)) {
@@ -384,6 +517,11 @@ Level Analyzer::compute(int id, const Map& m) {
   }
   if (loc[id].kind != Loc::NONE) {
     Level L = of_idx(to_linear(m, n.shape, d));
+    if (!m.guard.empty()) {
+      // a predicated element load is computed where its guard is known
+      if (m.gdep_o) L.kind |= 1;
+      if (m.gdep_i) L.kind |= 2;
+    }
     if (L.kind & 2) loads.insert(id);
     return L;
   }
@@ -399,10 +537,20 @@ Level Analyzer::compute(int id, const Map& m) {
     default:
       break;
   }
-  if (is_reduction(n.op)) throw NotFusible{};
+  if (n.op == FGT_OP_SCATTER_ADD && id == finalize_scatter) {
+    Level L = run(n.args[0], m);
+    return join(L, of_idx(to_linear(m, n.shape, d)));
+  }
+  if (is_reduction(n.op) || n.op == FGT_OP_SCATTER_ADD) throw NotFusible{};
   Level L;
   auto ms = operand_maps(g, id, m, d);
   for (size_t k = 0; k < n.args.size(); ++k) L = join(L, run(n.args[k], ms[k]));
+  // pad / concatenate select on coordinates; gather on its index value
+  if (n.op == FGT_OP_PAD || n.op == FGT_OP_CONCATENATE || n.op == FGT_OP_GATHER) {
+    const Map& gm = ms[0];
+    if (gm.gdep_o) L.kind |= 1;
+    if (gm.gdep_i) L.kind |= 2;
+  }
   return L;
 }
 
@@ -502,6 +650,113 @@ struct Planner {
     for (size_t k = 0; k < g.outputs.size(); ++k)
       if (g.outputs[k] == node) p.push_back((int)k);
     return p;
+  }
+
+  // scatter_add: three ELEM kernels. The accumulator (f64 for floating
+  // dtypes, the dtype's own width for integers, whose adds wrap) lives in the
+  // workspace; updates at out-of-range indices are dropped
+  // (tests/test_stage2_ops.py:230-238).
+  void plan_scatter(int s) {
+    const Node& n = g.nodes[s];
+    const Node& base = g.nodes[n.args[0]];
+    const Node& up = g.nodes[n.args[2]];
+    const int ax = (int)n.attrs[0], ir = g.nodes[n.args[1]].rank();
+    const int acc_bytes = is_float(n.dt) ? 8 : dtype_size(n.dt);
+    const int64_t acc = alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
+    auto make = [&](const Shape& shape, int stage) {
+      KernelDef k;
+      k.kind = KKind::ELEM;
+      for (int64_t e : shape)
+        if (e != 1) k.dom.id.push_back(e);
+      k.dom.finish();
+      k.scatter_node = s;
+      k.scatter_stage = stage;
+      k.scatter_acc = acc;
+      return k;
+    };
+    auto identity = [&](const KernelDef& k) {
+      Map m;
+      m.lin = true;
+      m.l = idx_const(k.dom.nd(), 0);
+      for (int j = 0; j < k.dom.nd(); ++j) m.l.c[j] = k.dom.iw[j];
+      return m;
+    };
+    // 1: accumulator <- 0
+    KernelDef k1 = make(base.shape, 1);
+    k1.vec = 1;
+    geometry_elem(k1);
+    plan.kernels.push_back(k1);
+    // 2: accumulator[.., indices[i..], ..] += updates[.., i.., ..]
+    if (up.n() > 0) {
+      KernelDef k2 = make(up.shape, 2);
+      Analyzer an(g, loc, k2.kind, k2.dom);
+      const Map mu = identity(k2);
+      try {
+        an.run(n.args[2], mu);
+        auto C = to_coords(mu, up.shape, k2.dom);
+        Map mi;
+        for (int k = 0; k < ir; ++k) mi.co.push_back(C[ax + k]);
+        an.run(n.args[1], mi);
+      } catch (NotFusible&) {
+        fail(FGT_ERR_UNSUPPORTED, "internal: scatter_add operands not evaluable");
+      }
+      choose_vec(k2, an.loads, {});
+      geometry_elem(k2);
+      plan.kernels.push_back(k2);
+    }
+    // 3: result <- base + accumulator
+    KernelDef k3 = make(base.shape, 3);
+    Analyzer an(g, loc, k3.kind, k3.dom);
+    an.finalize_scatter = s;
+    const Map mb = identity(k3);
+    try {
+      an.run(s, mb);
+    } catch (NotFusible&) {
+      fail(FGT_ERR_UNSUPPORTED, "internal: scatter_add base not evaluable");
+    }
+    auto ports = output_ports(s);
+    Loc L;
+    std::vector<int> outs;
+    if (!ports.empty()) {
+      L.kind = Loc::OUTPUT;
+      L.index = ports[0];
+      add_stores(k3, s, 0);
+      done_outputs.insert(s);
+      outs.push_back(s);
+    } else {
+      L.kind = Loc::TEMP;
+      L.offset = alloc(std::max<int64_t>(1, n.n()) * dtype_size(n.dt));
+      OutStore st;
+      st.node = s;
+      st.port = -1;
+      st.temp_offset = L.offset;
+      st.level = 0;
+      k3.stores.push_back(st);
+      outs.push_back(s);
+    }
+    choose_vec(k3, an.loads, outs);
+    geometry_elem(k3);
+    plan.kernels.push_back(k3);
+    loc[s] = L;
+  }
+
+  // Unmaterialised scatter_adds reachable from pending outputs.
+  std::vector<int> needed_scatters() {
+    std::vector<char> seen(g.nodes.size(), 0);
+    std::vector<int> stack;
+    for (int o : g.outputs)
+      if (!done_outputs.count(o)) stack.push_back(o);
+    std::set<int> sc;
+    while (!stack.empty()) {
+      int id = stack.back();
+      stack.pop_back();
+      if (seen[id]) continue;
+      seen[id] = 1;
+      if (loc[id].kind != Loc::NONE) continue;
+      if (g.nodes[id].op == FGT_OP_SCATTER_ADD) sc.insert(id);
+      for (int a : g.nodes[id].args) stack.push_back(a);
+    }
+    return std::vector<int>(sc.begin(), sc.end());
   }
 
   // Unmaterialised reductions reachable from pending outputs, in topo order.
@@ -887,6 +1142,12 @@ struct Planner {
       for (int o : g.outputs) pending = pending || !done_outputs.count(o);
       if (!pending) break;
       auto R = needed_reductions();
+      auto S = needed_scatters();
+      // the lowest node first: everything it reads is materialised or fusible
+      if (!S.empty() && (R.empty() || S.front() < R.front())) {
+        plan_scatter(S.front());
+        continue;
+      }
       if (R.empty()) {
         plan_elem_outputs();
         break;

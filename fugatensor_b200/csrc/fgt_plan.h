@@ -49,6 +49,12 @@ struct Map {
   bool lin = false;          // true: `l` is the value's row-major linear index
   Idx l;
   std::vector<Idx> co;       // false: one coordinate per value dimension
+  // Condition (C text over digits and gather indices) under which this
+  // value is actually used: set below pad / concatenate / gather, where a
+  // coordinate may fall outside its operand. Loads under a guard are element
+  // loads predicated on it, never vector loads.
+  std::string guard;
+  bool gdep_o = false, gdep_i = false;  // digits the guard depends on
   std::string key() const;
 };
 
@@ -109,6 +115,11 @@ struct KernelDef {
   int64_t send_offset = -1, recv_offset = -1, record_bytes = 0;
   std::string source;
   std::string signature;          // human-readable kernel summary
+  // scatter_add (ELEM kernels over the base or the updates): stage 1 zeroes
+  // the accumulator, 2 adds the in-range updates atomically, 3 combines base
+  // and accumulator into the result
+  int scatter_node = -1, scatter_stage = 0;
+  int64_t scatter_acc = -1;       // workspace offset of the accumulator
   int row_phases = 0;             // ROW: dependency levels holding row reductions (block barriers per row)
   int regs = -1, spill_bytes = -1;  // from the sm_100a compile (-1: unknown)
 };
@@ -143,6 +154,11 @@ bool idx_is_digit(const Idx& a, int digit);
 Idx to_linear(const Map& m, const Shape& shape, const Domain& d);
 std::vector<Idx> to_coords(const Map& m, const Shape& shape, const Domain& d);
 std::vector<Map> operand_maps(const Graph& g, int id, const Map& m, const Domain& d);
+// Conditions of the index transforms at map m (C text): pad / concatenate:
+// the value comes from the (first) operand; gather: the index is in range.
+std::string pad_condition(const Graph& g, int id, const Map& m, const Domain& d);
+std::string concat_condition(const Graph& g, int id, const Map& m, const Domain& d);
+std::string gather_index_name(int id, const Map& m);
 
 // Thrown by the analysis when a value cannot be evaluated in a kernel.
 struct NotFusible {};
@@ -158,6 +174,7 @@ struct Analyzer {
   const Graph& g;
   const std::vector<Loc>& loc;
   KKind kind;
+  int finalize_scatter = -1;      // the scatter_add node this kernel completes (read as base + accumulator)
   const Domain& d;
   std::map<int, const RedDef*> group;  // reductions computed (or finalised) here
   std::map<std::string, Level> memo;

@@ -269,6 +269,9 @@ def _build(g, op, argv, attrs):
         return g.stop_gradient(argv[0])
     if op in ir.REDUCTIONS or op in ("argmax", "argmin"):
         return getattr(g, op)(argv[0], attrs[0])
+    if op in ("slice", "pad", "concatenate", "gather", "scatter_add"):
+        from .tensor import _index_op
+        return _index_op(g, op, argv, attrs)
     return getattr(g, op)(*argv)
 
 

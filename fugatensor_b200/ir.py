@@ -27,6 +27,7 @@ INT_DTYPES = frozenset({"i32", "i64"})
 WIDTH = {"bool": 1, "i32": 4, "i64": 8, "f32": 4, "f16": 2, "bf16": 2}
 
 MAX_RANK = 8
+MAX_ATTRS = 24
 
 OP = {
     "parameter": 0, "constant": 1, "splat": 2, "reshape": 3, "broadcast_in_dim": 4, "transpose": 5,
@@ -38,6 +39,7 @@ OP = {
     "compare": 50, "select": 51,
     "reduce_sum": 60, "reduce_max": 61, "reduce_min": 62, "reduce_prod": 63, "reduce_any": 64,
     "reduce_all": 65, "argmax": 66, "argmin": 67,
+    "slice": 70, "pad": 71, "concatenate": 72, "gather": 73, "scatter_add": 74,
 }
 PREDICATES = {"eq": 0, "ne": 1, "lt": 2, "le": 3, "gt": 4, "ge": 5}
 BINARY = ("add", "mul", "div", "maximum", "minimum", "pow", "floordiv", "mod", "bitwise_and",
@@ -293,6 +295,89 @@ class Graph:
         shape = tuple(s for a, s in enumerate(x.shape) if a != axis)
         return self._add(op, "i64", shape, (x,), (axis,))
 
+    # -- index transforms (typing: ir/tensor_rules.py:124-237) -------------
+    def slice(self, x: Value, starts, stops, steps) -> Value:
+        """Strided slice with normalised bounds (ops.py:481-508 produces them)."""
+        starts, stops, steps = tuple(starts), tuple(stops), tuple(steps)
+        if not (len(starts) == len(stops) == len(steps) == x.rank):
+            raise ValueError("slice starts, stops and steps must match operand rank")
+        shape = []
+        for dim, st, sp, step in zip(x.shape, starts, stops, steps):
+            if step == 0:
+                raise ValueError("slice step must be nonzero")
+            if step > 0:
+                if not 0 <= st <= sp <= dim:
+                    raise ValueError("slice forward bounds out of range")
+                shape.append(0 if sp == st else (sp - st + step - 1) // step)
+            elif st == sp:
+                if not 0 <= st <= dim:
+                    raise ValueError("slice empty bounds out of range")
+                shape.append(0)
+            else:
+                if not (0 <= st < dim and -1 <= sp < st):
+                    raise ValueError("slice reverse bounds out of range")
+                shape.append((st - sp + (-step) - 1) // (-step))
+        if tuple(shape) == x.shape and all(st == 0 and step == 1 for st, step in zip(starts, steps)):
+            return x
+        return self._add("slice", x.dtype, tuple(shape), (x,), starts + steps)
+
+    def pad(self, x: Value, pad_value: Value, low, high, interior) -> Value:
+        low, high, interior = tuple(low), tuple(high), tuple(interior)
+        if pad_value.shape != () or pad_value.dtype != x.dtype:
+            raise TypeError("pad requires a 0-D scalar pad_value with the same dtype as input")
+        if not (len(low) == len(high) == len(interior) == x.rank):
+            raise ValueError("pad attributes must match operand rank")
+        if any(v < 0 for v in low + high + interior):
+            raise ValueError("pad amounts and interior dilation must be nonnegative integers")
+        shape = tuple(l + (d + (d - 1) * i if d > 0 else 0) + h for d, l, h, i in zip(x.shape, low, high, interior))
+        return self._add("pad", x.dtype, shape, (x, pad_value), low + interior)
+
+    def concatenate(self, xs, axis) -> Value:
+        xs = list(xs)
+        if not xs:
+            raise TypeError("concatenate requires at least one operand")
+        first = xs[0]
+        if first.rank < 1 or not 0 <= axis < first.rank:
+            raise ValueError("concatenate axis out of range")
+        for v in xs:
+            if v.dtype != first.dtype or v.rank != first.rank:
+                raise TypeError("concatenate operands must match rank and dtype")
+            if any(a != axis and s != first.shape[a] for a, s in enumerate(v.shape)):
+                raise ValueError("concatenate non-axis dimensions must match")
+        xs = [v for v in xs if v.shape[axis] > 0] or xs[:1]
+        if len(xs) == 1:
+            return xs[0]
+        # n-ary joins nest as binary ones (left to right)
+        acc = xs[0]
+        for v in xs[1:]:
+            shape = tuple(s + v.shape[a] if a == axis else s for a, s in enumerate(acc.shape))
+            acc = self._add("concatenate", acc.dtype, shape, (acc, v), (axis,))
+        return acc
+
+    def gather(self, params: Value, indices: Value, axis) -> Value:
+        if params.rank < 1:
+            raise ValueError("gather params must be a concrete tensor of rank at least one")
+        if indices.dtype not in INT_DTYPES:
+            raise TypeError("gather indices must have i32 or i64 dtype")
+        if not 0 <= axis < params.rank:
+            raise ValueError("gather axis out of range")
+        shape = params.shape[:axis] + indices.shape + params.shape[axis + 1:]
+        return self._add("gather", params.dtype, shape, (params, indices), (axis,))
+
+    def scatter_add(self, base: Value, indices: Value, updates: Value, axis) -> Value:
+        if base.rank < 1:
+            raise ValueError("scatter_add base must be a concrete tensor of rank at least one")
+        if base.dtype == "bool":
+            raise TypeError("scatter_add base must have a numeric dtype")
+        if indices.dtype not in INT_DTYPES:
+            raise TypeError("scatter_add indices must have concrete i32 or i64 type")
+        if not 0 <= axis < base.rank:
+            raise ValueError("scatter_add axis out of range")
+        want = base.shape[:axis] + indices.shape + base.shape[axis + 1:]
+        if updates.shape != want or updates.dtype != base.dtype:
+            raise TypeError("scatter_add updates shape/dtype does not match base, indices and axis")
+        return self._add("scatter_add", base.dtype, base.shape, (base, indices, updates), (axis,))
+
     # -- descriptor -------------------------------------------------------
     def descriptor(self, outputs):
         return Descriptor(self, [o.id if isinstance(o, Value) else int(o) for o in outputs])
@@ -313,7 +398,7 @@ class CNode(ctypes.Structure):
     _fields_ = [("opcode", ctypes.c_int32), ("dtype", ctypes.c_int32), ("rank", ctypes.c_int32),
                 ("num_operands", ctypes.c_int32), ("shape", ctypes.c_int64 * MAX_RANK),
                 ("operands", ctypes.c_int32 * 3), ("num_attrs", ctypes.c_int32),
-                ("attrs", ctypes.c_int64 * MAX_RANK), ("predicate", ctypes.c_int32),
+                ("attrs", ctypes.c_int64 * MAX_ATTRS), ("predicate", ctypes.c_int32),
                 ("reserved", ctypes.c_int32), ("constant_bits", ctypes.c_uint64)]
 
 
@@ -323,7 +408,7 @@ class CPartition(ctypes.Structure):
                 ("outputs", ctypes.POINTER(ctypes.c_int32))]
 
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class Descriptor:

@@ -316,6 +316,30 @@ class Tensor:
         from .ops import sqrt
         return sqrt(self)
 
+    def __getitem__(self, key):
+        from .ops import getitem
+        return getitem(self, key)
+
+    def split(self, split_size_or_sections, axis=0):
+        from .ops import split
+        return split(self, split_size_or_sections, axis)
+
+    def chunk(self, chunks, axis=0):
+        from .ops import chunk
+        return chunk(self, chunks, axis)
+
+    def flatten(self, start_dim=0, end_dim=-1):
+        from .ops import flatten
+        return flatten(self, start_dim, end_dim)
+
+    def squeeze(self, axis=None):
+        from .ops import squeeze
+        return squeeze(self, axis)
+
+    def unsqueeze(self, axis):
+        from .ops import unsqueeze
+        return unsqueeze(self, axis)
+
 
 def _infer(op, args, attrs):
     """Result type of a primitive, by the same rules as the IR builder."""
@@ -341,9 +365,24 @@ def _infer(op, args, attrs):
         v = getattr(g, op)(vals[0], attrs[0])
     elif op in ("argmax", "argmin"):
         v = getattr(g, op)(vals[0], attrs[0])
+    elif op in ("slice", "pad", "concatenate", "gather", "scatter_add"):
+        v = _index_op(g, op, vals, attrs)
     else:
         v = getattr(g, op)(*vals)
     return v.dtype, v.shape
+
+
+def _index_op(g, op, vals, attrs):
+    """IR builder call of an index transform (shared by typing and tracing)."""
+    if op == "slice":
+        return g.slice(vals[0], *attrs)
+    if op == "pad":
+        return g.pad(vals[0], vals[1], *attrs)
+    if op == "concatenate":
+        return g.concatenate(list(vals), attrs[0])
+    if op == "gather":
+        return g.gather(vals[0], vals[1], attrs[0])
+    return g.scatter_add(vals[0], vals[1], vals[2], attrs[0])
 
 
 def _prim(op, args, attrs=()):

@@ -34,9 +34,10 @@
 extern "C" {
 #endif
 
-#define FGT_ABI_VERSION 2
+#define FGT_ABI_VERSION 3
 #define FGT_MAX_RANK 8
 #define FGT_MAX_OPERANDS 3
+#define FGT_MAX_ATTRS 24
 
 typedef int32_t fgt_status;
 enum {
@@ -81,7 +82,17 @@ typedef enum fgt_opcode {
   /* reductions: attrs = sorted reduced axes (argmax/argmin: attrs[0] = axis) */
   FGT_OP_REDUCE_SUM = 60, FGT_OP_REDUCE_MAX = 61, FGT_OP_REDUCE_MIN = 62,
   FGT_OP_REDUCE_PROD = 63, FGT_OP_REDUCE_ANY = 64, FGT_OP_REDUCE_ALL = 65,
-  FGT_OP_ARGMAX = 66, FGT_OP_ARGMIN = 67
+  FGT_OP_ARGMAX = 66, FGT_OP_ARGMIN = 67,
+  /* index transforms (src/fugatensor/lowering.py:103-111, ir/tensor_rules.py:124-237) */
+  FGT_OP_SLICE = 70,          /* attrs = starts[rank], steps[rank]; stops follow from  */
+                              /* the result shape                                      */
+  FGT_OP_PAD = 71,            /* (x, pad value: rank 0, same dtype); attrs = low[rank], */
+                              /* interior[rank]; high follows from the result shape    */
+  FGT_OP_CONCATENATE = 72,    /* two operands joined along attrs[0] (longer lists nest) */
+  FGT_OP_GATHER = 73,         /* (params, indices i32/i64); attrs[0] = axis; indices    */
+                              /* outside [0, extent) read 0                            */
+  FGT_OP_SCATTER_ADD = 74     /* (base, indices, updates); attrs[0] = axis; result =    */
+                              /* base plus updates at indices (outside: dropped)       */
 } fgt_opcode;
 
 typedef enum fgt_predicate {
@@ -98,7 +109,7 @@ typedef struct fgt_node {
   int64_t shape[FGT_MAX_RANK];
   int32_t operands[FGT_MAX_OPERANDS];
   int32_t num_attrs;
-  int64_t attrs[FGT_MAX_RANK];
+  int64_t attrs[FGT_MAX_ATTRS];
   int32_t predicate;
   int32_t reserved;
   uint64_t constant_bits;

@@ -581,6 +581,107 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
           memcpy((char*)o->v + j * vsize(o->dt), (char*)s->v + j * vsize(o->dt), vsize(o->dt));
         }
         break;
+      /* index transforms (src/fugatensor/ir/tensor_rules.py:124-237; out-of-range
+       * gather indices read 0 and out-of-range scatter_add indices are dropped,
+       * tests/test_stage2_ops.py:190-191,230-260) */
+      case FGT_OP_SLICE: {
+        const int r = a->rank;
+        strides(a->shape, r, as);
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, r, cc);
+          int64_t off = 0;
+          for (int k = 0; k < r; ++k) off += (nd->attrs[k] + cc[k] * nd->attrs[r + k]) * as[k];
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)a->v + off * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      }
+      case FGT_OP_PAD: {
+        const int r = a->rank;
+        strides(a->shape, r, as);
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, r, cc);
+          int in = 1;
+          int64_t off = 0;
+          for (int k = 0; k < r && in; ++k) {
+            const int64_t t = cc[k] - nd->attrs[k], step = nd->attrs[r + k] + 1;
+            if (t < 0 || t % step || t / step >= a->shape[k]) in = 0;
+            else off += (t / step) * as[k];
+          }
+          const Buf* src = in ? a : b;
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)src->v + (in ? off : 0) * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      }
+      case FGT_OP_CONCATENATE: {
+        const int ax = (int)nd->attrs[0], r = o->rank;
+        int64_t bs[FGT_MAX_RANK];
+        strides(a->shape, r, as);
+        strides(b->shape, r, bs);
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, r, cc);
+          const int first = cc[ax] < a->shape[ax];
+          if (!first) cc[ax] -= a->shape[ax];
+          int64_t off = 0;
+          for (int k = 0; k < r; ++k) off += cc[k] * (first ? as[k] : bs[k]);
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)(first ? a : b)->v + off * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      }
+      case FGT_OP_GATHER: {
+        const int ax = (int)nd->attrs[0], ir = b->rank, pr = a->rank;
+        strides(a->shape, pr, as);
+        int64_t is_[FGT_MAX_RANK];
+        strides(b->shape, ir, is_);
+        for (int64_t j = 0; j < o->n; ++j) {
+          unravel(j, o->shape, o->rank, cc);
+          int64_t ioff = 0;
+          for (int k = 0; k < ir; ++k) ioff += cc[ax + k] * is_[k];
+          const int64_t idx = geti(b, ioff);
+          if (idx < 0 || idx >= a->shape[ax]) {
+            memset((char*)o->v + j * vsize(o->dt), 0, vsize(o->dt));
+            continue;
+          }
+          int64_t off = idx * as[ax];
+          for (int k = 0; k < ax; ++k) off += cc[k] * as[k];
+          for (int k = ax + 1; k < pr; ++k) off += cc[k - 1 + ir] * as[k];
+          memcpy((char*)o->v + j * vsize(o->dt), (char*)a->v + off * vsize(o->dt), vsize(o->dt));
+        }
+        break;
+      }
+      case FGT_OP_SCATTER_ADD: {
+        /* base + updates in update order; LITERAL rounds every add to the
+         * dtype, ACCURATE sums in long double and rounds once per element */
+        const int ax = (int)nd->attrs[0], ir = b->rank, br = a->rank;
+        Buf u = *c;
+        strides(a->shape, br, as);
+        int64_t is_[FGT_MAX_RANK];
+        strides(b->shape, ir, is_);
+        long double* accf = NULL;
+        if (is_float(o->dt) && mode == MODE_ACCURATE) {
+          accf = (long double*)malloc(sizeof(long double) * (size_t)(o->n ? o->n : 1));
+          for (int64_t j = 0; j < o->n; ++j) accf[j] = ((float*)a->v)[j];
+        } else {
+          memcpy(o->v, a->v, (size_t)o->n * vsize(o->dt));
+        }
+        for (int64_t j = 0; j < u.n; ++j) {
+          unravel(j, u.shape, u.rank, cc);
+          int64_t ioff = 0;
+          for (int k = 0; k < ir; ++k) ioff += cc[ax + k] * is_[k];
+          const int64_t idx = geti(b, ioff);
+          if (idx < 0 || idx >= a->shape[ax]) continue;
+          int64_t off = idx * as[ax];
+          for (int k = 0; k < ax; ++k) off += cc[k] * as[k];
+          for (int k = ax + 1; k < br; ++k) off += cc[k - 1 + ir] * as[k];
+          if (accf) accf[off] += ((float*)u.v)[j];
+          else if (is_float(o->dt)) ((float*)o->v)[off] = rnd_f(((float*)o->v)[off] + ((float*)u.v)[j], o->dt);
+          else put_int(o, off, wrap((int64_t)((uint64_t)geti(o, off) + (uint64_t)geti(&u, j)), o->dt));
+        }
+        if (accf) {
+          for (int64_t j = 0; j < o->n; ++j) ((float*)o->v)[j] = rnd_dt(accf[j], o->dt);
+          free(accf);
+        }
+        break;
+      }
       default:
         if (op >= FGT_OP_REDUCE_SUM && op <= FGT_OP_ARGMIN) {
           rc = eval_reduce(nd, a, o, mode);

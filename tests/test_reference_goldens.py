@@ -334,3 +334,115 @@ def test_argmax_rows_of_identity_values(backend):
     big = T([[-math.inf] * 3000])
     (d,) = run(backend, big.argmax())
     assert int(d) == 0
+
+
+# ------------------------------------------------------ index transforms ---
+def _grid():
+    return T([[float(r * 5 + c) for c in range(5)] for r in range(4)])
+
+
+def test_slicing_and_tensor_indexing(backend):
+    """tests/test_stage2_ops.py:180-191: strided / reversed slices, None, Ellipsis, empty slices,
+    and an integer-tensor row index whose -1 entry reads a zero row."""
+    x = _grid()
+    a, b, c = x[::-1, 1:5:2], x[-1, None, ::2], x[..., 0]
+    got = run(backend, a, b, c)
+    assert got[0].tolist() == [[16.0, 18.0], [11.0, 13.0], [6.0, 8.0], [1.0, 3.0]]
+    assert got[1].tolist() == [[15.0, 17.0, 19.0]]
+    assert got[2].tolist() == [0.0, 5.0, 10.0, 15.0]
+    assert x[2:1].shape == (0, 5) and x[1:3:-1].shape == (0, 5)
+    tidx = T([3, 0, 3, -1], "int64")
+    (g,) = run(backend, x[tidx, 1:4])
+    assert g.tolist() == [[16.0, 17.0, 18.0], [1.0, 2.0, 3.0], [16.0, 17.0, 18.0], [0.0, 0.0, 0.0]]
+
+
+def test_pad_interior_and_concatenate(backend):
+    """tests/test_stage2_ops.py:193-212: interior pad with an empty edge; cat with an empty
+    operand; stack; split and chunk of the concatenation."""
+    small = T([[1.0, 2.0], [3.0, 4.0]])
+    padded = ft.pad(small, ((1, 0), (0, 1)), constant_value=-1.0, interior=(1, 1))
+    assert padded.shape == (4, 4)
+    a = T([[1.0, 2.0]])
+    b = T([[3.0, 4.0], [5.0, 6.0]])
+    empty = ft.tensor(np.zeros((0, 2), np.float32))
+    cat = ft.cat([a, empty, b], axis=0)
+    stk = ft.stack([a.squeeze(0), a.squeeze(0)], axis=1)
+    p0, p1, p2 = cat.split([1, 0, 2], axis=0)
+    ch0, ch1 = cat.chunk(2, axis=0)
+    got = run(backend, padded, cat, stk, p0, p2, ch0, ch1)
+    assert got[0].tolist() == [[-1.0, -1.0, -1.0, -1.0], [1.0, -1.0, 2.0, -1.0], [-1.0, -1.0, -1.0, -1.0],
+                               [3.0, -1.0, 4.0, -1.0]]
+    assert got[1].tolist() == [[1.0, 2.0], [3.0, 4.0], [5.0, 6.0]]
+    assert got[2].tolist() == [[1.0, 1.0], [2.0, 2.0]]
+    assert got[3].tolist() == [[1.0, 2.0]] and p1.shape == (0, 2) and got[4].tolist() == [[3.0, 4.0], [5.0, 6.0]]
+    assert ch0.shape == (2, 2) and ch1.shape == (1, 2)
+    assert got[5].tolist() == [[1.0, 2.0], [3.0, 4.0]] and got[6].tolist() == [[5.0, 6.0]]
+
+
+def test_one_hot_and_triangles(backend):
+    """tests/test_stage2_ops.py:219-224: one_hot with an out-of-range class gives a zero row."""
+    oh = ft.one_hot(T([2, 0, -1], "int32"), 4, dtype=ft.fp32)
+    (got,) = run(backend, oh)
+    assert got.tolist() == [[0.0, 0.0, 1.0, 0.0], [1.0, 0.0, 0.0, 0.0], [0.0, 0.0, 0.0, 0.0]]
+
+
+@pytest.mark.parametrize("dtype", FLOATS)
+def test_scatter_add_duplicates_and_out_of_range(backend, dtype):
+    """tests/test_stage2_ops.py:230-238: duplicate indices accumulate, -1 and 4 are dropped."""
+    base = ft.tensor(np.zeros((4, 2), np.float32), dtype=getattr(ft, dtype))
+    idx = T([1, 3, 1, -1, 4, 1], "int32")
+    upd = T([[1.0, 2.0], [3.0, 4.0], [5.0, 6.0], [10.0, 10.0], [20.0, 20.0], [0.5, -1.0]], dtype)
+    (got,) = run(backend, ft.scatter_add(base, idx, upd, axis=0))
+    close(got, [[0.0, 0.0], [6.5, 7.0], [0.0, 0.0], [3.0, 4.0]], 1e-5 if dtype == "fp32" else 1e-2)
+
+
+def test_scatter_add_axis1_and_empty_updates(backend):
+    """tests/test_stage2_ops.py:240-260: scatter along axis 1 with repeats (then abs); empty
+    updates keep the base."""
+    for scale in (1.0, 2.0, -3.0):
+        b = T([[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]])
+        i = T([2, 0, 2], "int64")
+        u = T([[scale, scale, scale], [-scale, scale, 0.0]])
+        (got,) = run(backend, ft.scatter_add(b, i, u, axis=1).abs())
+        close(got, [[abs(1.0 + scale), 2.0, abs(3.0 + 2.0 * scale)], [abs(4.0 + scale), 5.0, abs(6.0 - scale)]], 1e-6)
+    keep = T([[1.0, 2.0], [3.0, 4.0]])
+    e_idx = ft.tensor(np.zeros((0,), np.int32), dtype=ft.int32)
+    e_upd = ft.tensor(np.zeros((0, 2), np.float32))
+    (got,) = run(backend, ft.scatter_add(keep, e_idx, e_upd, axis=0))
+    assert got.tolist() == [[1.0, 2.0], [3.0, 4.0]]
+
+
+def test_index_transform_gradients(backend):
+    """tests/test_stage2_ops.py:291-322: gradients through a reversed strided slice, a pad
+    whose pad value is differentiated, gather and scatter_add, against central differences."""
+    w0 = [1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0, 8.0]
+
+    def geom(wf, pv):
+        rows = [[pv, pv, pv], [wf[3], wf[1], pv], [pv, pv, pv], [wf[7], wf[5], pv]]
+        res = [[1.0, 1.0], [1.0, 1.0]]
+        for ii in (1, 0, 1):
+            res[ii][0] += rows[ii][0]
+            res[ii][1] += rows[ii][1]
+        return res[0][0] * 1 + res[0][1] * 2 + res[1][0] * 3 + res[1][1] * 4
+
+    def cdiff(f, xs, eps=1e-3):
+        out = []
+        for k in range(len(xs)):
+            hi, lo = list(xs), list(xs)
+            hi[k] += eps
+            lo[k] -= eps
+            out.append((f(hi) - f(lo)) / (2 * eps))
+        return out
+
+    w = T([w0[:4], w0[4:]])
+    pv = ft.tensor(0.5)
+    idx = T([1, 0, 1], "int32")
+    sl = w[:, ::-2]
+    pd = ft.pad(sl, ((1, 0), (0, 1)), constant_value=pv, interior=(1, 0))
+    gth = ft.gather(pd, idx, axis=0)
+    sc2 = ft.scatter_add(ft.tensor(np.ones((2, 2), np.float32)), idx, gth[:, :2], axis=0)
+    loss = (sc2 * T([[1.0, 2.0], [3.0, 4.0]])).sum()
+    gw, gpv = ft.grad(loss, (w, pv))
+    got_w, got_pv = run(backend, gw, gpv)
+    close(got_w, cdiff(lambda wf: geom(wf, 0.5), w0), 1e-3)
+    close([float(got_pv)], cdiff(lambda p: geom(w0, p[0]), [0.5]), 1e-3)
