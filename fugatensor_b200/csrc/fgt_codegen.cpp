@@ -401,6 +401,7 @@ struct Emitter {
     U = elem ? K.unroll : 1;
     fin_reds = K.reds;
     for (auto& rd : fin_reds) an.group[rd.node] = &rd;
+    if (K.scatter_stage == 3) an.finalize_scatter = K.scatter_node;
   }
 
   std::string fresh(const char* p) { return std::string(p) + std::to_string(uid++); }
@@ -631,7 +632,8 @@ struct Emitter {
     const Node& n = g.nodes[id];
     auto rv = red_var.find(id);
     if (rv != red_var.end() && an.group.count(id)) return rv->second;
-    if (P.loc[id].kind != Loc::NONE && !an.group.count(id)) return load(id, m, D);
+    const bool completes = id == K.scatter_node && K.scatter_stage == 3;
+    if (P.loc[id].kind != Loc::NONE && !an.group.count(id) && !completes) return load(id, m, D);
     switch (n.op) {
       case FGT_OP_CONSTANT:
         return literal(n.dt, n.cbits);

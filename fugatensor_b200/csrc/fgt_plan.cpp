@@ -515,6 +515,12 @@ Level Analyzer::compute(int id, const Map& m) {
     red_phase[id] = op.phase;
     return Level{1, op.phase + 1};
   }
+  // the kernel that completes a scatter_add computes it (base + accumulator)
+  // even once its result has a location
+  if (n.op == FGT_OP_SCATTER_ADD && id == finalize_scatter) {
+    Level L = run(n.args[0], m);
+    return join(L, of_idx(to_linear(m, n.shape, d)));
+  }
   if (loc[id].kind != Loc::NONE) {
     Level L = of_idx(to_linear(m, n.shape, d));
     if (!m.guard.empty()) {
@@ -536,10 +542,6 @@ Level Analyzer::compute(int id, const Map& m) {
       throw NotFusible{};
     default:
       break;
-  }
-  if (n.op == FGT_OP_SCATTER_ADD && id == finalize_scatter) {
-    Level L = run(n.args[0], m);
-    return join(L, of_idx(to_linear(m, n.shape, d)));
   }
   if (is_reduction(n.op) || n.op == FGT_OP_SCATTER_ADD) throw NotFusible{};
   Level L;
