@@ -261,6 +261,29 @@ def run_fgt(args):
                     del L
                 del tt
                 torch.cuda.empty_cache()
+        # index-transform partitions (synthetic; no BASELINE config names them)
+        for name in W.INDEX_WORKLOADS:
+            tt = W.index_inputs(name, device)
+            t = {k: ft.Tensor(engine, W.INDEX_DTYPES[name][k], tuple(v.shape), data=v) for k, v in tt.items()}
+            spec, desc, leaves, roots = engine.compile(*W.index_build(name, t))
+            L = Launcher(spec, [l._data for l in leaves], device)
+            for _ in range(3):
+                L(stream.cuda_stream)
+            times = []
+            for _ in range(args.table_iters):
+                flush_l2(flush)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                L(stream.cuda_stream)
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            ms = statistics.median(times)
+            nb = W.index_bytes(name)
+            partitions[f"index/{name}/f32"] = {"ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
+                                               "frac": round(nb / ms / 1e6 / peak, 4), "kernels": spec.kernel_count}
+            del tt, t, L
+            torch.cuda.empty_cache()
 
     clk.__exit__(None, None, None)
 

@@ -150,3 +150,49 @@ def algorithmic_bytes(cfg, variant, rows, cols, dtype="f32"):
     if cfg == "c5":
         return n * 4 + rows * 4 + cols * 2 + n * 2 + rows * 4
     raise KeyError(cfg)
+
+
+# ------------------------------------------------------- index transforms ---
+# Synthetic index-transform partitions (no BASELINE config names them): an
+# embedding-style row gather, a row scatter_add with repeated indices, and a
+# pad / reversed-slice / concatenate row rewrite. Shapes exceed L2.
+INDEX_WORKLOADS = ("gather_rows", "scatter_add_rows", "pad_concat")
+
+
+def index_inputs(name, device, seed=6):
+    """Device inputs (torch) of an index-transform workload."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    if name == "gather_rows":
+        return {"T": torch.randn((262144, 512), device=device, generator=g),
+                "I": torch.randint(0, 262144, (131072,), device=device, generator=g)}
+    if name == "scatter_add_rows":
+        return {"B": torch.randn((65536, 512), device=device, generator=g),
+                "I": torch.randint(0, 65536, (131072,), device=device, generator=g, dtype=torch.int32),
+                "U": torch.randn((131072, 512), device=device, generator=g)}
+    if name == "pad_concat":
+        return {"X": torch.randn((16384, 8192), device=device, generator=g)}
+    raise KeyError(name)
+
+
+INDEX_DTYPES = {"gather_rows": {"T": "f32", "I": "i64"}, "scatter_add_rows": {"B": "f32", "I": "i32", "U": "f32"},
+                "pad_concat": {"X": "f32"}}
+
+
+def index_build(name, t):
+    import fugatensor_b200 as ft
+    if name == "gather_rows":
+        return [ft.gather(t["T"], t["I"], axis=0)]
+    if name == "scatter_add_rows":
+        return [ft.scatter_add(t["B"], t["I"], t["U"], axis=0)]
+    X = t["X"]
+    return [ft.cat([ft.pad(X[:, 1:], ((0, 0), (0, 1))), X[:, ::-1]], axis=1)]
+
+
+def index_bytes(name):
+    """Algorithmic HBM bytes: rows read or written once each, indices once (scratch excluded)."""
+    if name == "gather_rows":
+        return 131072 * 512 * 4 * 2 + 131072 * 8
+    if name == "scatter_add_rows":
+        return 65536 * 512 * 4 * 2 + 131072 * 512 * 4 + 131072 * 4
+    return 16384 * 8192 * 4 + 16384 * 16384 * 4
