@@ -160,8 +160,13 @@ std::string binary_expr(int op, int dt, const std::string& a, const std::string&
       if (!f) return "fgt_wrap_mul<" + T + "," + U + ">(" + a + "," + b + ")";
       // x * (+-1) of a value exact in its dtype is exact (it is how the
       // reference spells negation and subtraction), so it needs no rounding.
+      // As a negation it folds into the consumer (an add of -x is a subtract):
+      // the same value for every non-NaN x (a NaN keeps its payload, sign aside).
       static const std::string one = "__uint_as_float(0x3f800000u)", neg = "__uint_as_float(0xbf800000u)";
-      if (a == one || a == neg || b == one || b == neg) return "__fmul_rn(" + a + "," + b + ")";
+      if (b == one) return a;
+      if (a == one) return b;
+      if (b == neg) return "(-" + a + ")";
+      if (a == neg) return "(-" + b + ")";
       return rnd(dt, "__fmul_rn(" + a + "," + b + ")");
     }
     case FGT_OP_DIV: return rnd(dt, "__fdiv_rn(" + a + "," + b + ")");
