@@ -13,6 +13,7 @@
 // contraction (src/fugatensor/_ask/gpu.py:189), f16/bf16 computed in f32 and
 // rounded once per operation, exp/log/tanh/erf through CUDA's f32 math
 // library (the reference links libdevice, src/fugatensor/_ask/cuda.py:215-229).
+#include <cstdio>
 #include <cstring>
 #include <functional>
 #include <sstream>
@@ -169,7 +170,20 @@ std::string binary_expr(int op, int dt, const std::string& a, const std::string&
       if (a == neg) return "(-" + b + ")";
       return rnd(dt, "__fmul_rn(" + a + "," + b + ")");
     }
-    case FGT_OP_DIV: return rnd(dt, "__fdiv_rn(" + a + "," + b + ")");
+    case FGT_OP_DIV: {
+      // x / 2^k is x * 2^-k exactly (both are one rounding of the same real)
+      unsigned bits = 0;
+      if (std::sscanf(b.c_str(), "__uint_as_float(0x%8xu)", &bits) == 1 && (bits & 0x7fffffu) == 0) {
+        const unsigned e = (bits >> 23) & 0xffu;
+        if (e >= 1 && e <= 253) {
+          const unsigned r = (bits & 0x80000000u) | ((254u - e) << 23);
+          char lit[48];
+          std::snprintf(lit, sizeof lit, "__uint_as_float(0x%08xu)", r);
+          return rnd(dt, "__fmul_rn(" + a + "," + lit + ")");
+        }
+      }
+      return rnd(dt, "__fdiv_rn(" + a + "," + b + ")");
+    }
     case FGT_OP_MAXIMUM:
       if (f) return "fgt_fmax(" + a + "," + b + ")";
       if (dt == FGT_BOOL) return "(" + a + "||" + b + ")";
@@ -356,6 +370,7 @@ struct Emitter {
   std::vector<std::string> rowpf, rowpf_first, rowpf_next;  // row-scope loads, one row ahead
   std::map<std::string, std::pair<std::string, Sc>> unrounded;  // bf16 temp -> (f32 expression, scope)
   std::map<std::string, std::string> texpr;  // temp -> its defining expression
+  std::map<std::string, std::string> cse;    // (scope, type, expression) -> temp
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
@@ -714,7 +729,10 @@ struct Emitter {
       // per-element division is then the corrected reciprocal product, which
       // equals the IEEE quotient (fgt_div_by).
       const Level la = an.run(n.args[0], ms[0]), lb = an.run(n.args[1], ms[1]);
-      if ((lb.kind & 2) == 0 && (la.kind & 2) != 0) {
+      unsigned dbits = 0;
+      const bool pow2 = std::sscanf(a[1].c_str(), "__uint_as_float(0x%8xu)", &dbits) == 1 && (dbits & 0x7fffffu) == 0 &&
+                        ((dbits >> 23) & 0xffu) >= 1 && ((dbits >> 23) & 0xffu) <= 253;
+      if (!pow2 && (lb.kind & 2) == 0 && (la.kind & 2) != 0) {
         const Sc db = lb.kind == 0 ? Sc{SC_PRO, 0} : Sc{SC_ROW, lb.phase};
         const std::string rk = "rcp|" + a[1] + "#" + std::to_string((int)db.k) + ":" + std::to_string(db.p);
         auto it = memo.find(rk);
@@ -748,8 +766,15 @@ struct Emitter {
     else if (is_binary(n.op)) expr = binary_expr(n.op, n.dt, a[0], a[1]);
     else if (is_unary(n.op)) expr = unary_expr(n.op, n.dt, a[0]);
     else fail(FGT_ERR_UNSUPPORTED, std::string("generator cannot place ") + opcode_name(n.op));
+    // Identical pure expressions in one scope share one temporary (graph
+    // nodes that differ only in shape, e.g. [R] and [R, 1] row statistics,
+    // produce the same text).
+    const std::string ck = std::to_string((int)D.k) + ":" + std::to_string(D.p) + "|" + vt_t(n.dt) + "|" + expr;
+    auto hit = cse.find(ck);
+    if (hit != cse.end()) return hit->second;
     std::string v = fresh("t");
     add(D, "const " + vt_t(n.dt) + " " + v + " = " + expr + ";");
+    cse[ck] = v;
     texpr[v] = expr;
     // A bf16 value is the rounding of an f32 expression; a store of it may
     // round pairs at once instead (store_stmt_elem).
