@@ -1,0 +1,83 @@
+"""GPU parity on the shapes the benchmark configs do not reach: rows too long
+for registers (streamed rows), rows that do not divide into thread chunks,
+middle-axis and rank-3 reductions, axis-0 arg-reductions, boolean and
+wrapping integer reductions, empty results, and bf16 through index transforms."""
+import numpy as np
+import pytest
+
+import fugatensor_b200 as ft
+import fugatensor_b200.nn.functional as F
+import oracle as O
+from tests._util import assert_matches
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(outs, arrays):
+    eng = outs[0].engine
+    desc, leaves, roots = eng.trace(*outs)
+    ref = O.evaluate(desc, [arrays[id(l)] for l in leaves])
+    ft.evaluate(*outs)
+    for o, r in zip(outs, ref):
+        got = o.numpy()
+        assert got.shape == r.shape
+        if o.dtype.ir in ("i32", "i64", "bool"):
+            assert np.array_equal(got, r), o._expr[0] if o._expr else ""
+        elif o.dtype.ir == "bf16":
+            assert_matches(O.bf16_bits_to_f32(got), O.bf16_bits_to_f32(r), "bf16")
+        else:
+            assert_matches(got, r, o.dtype.ir)
+
+
+@pytest.mark.parametrize("rows,cols", [(3, 1 << 20), (2, 600001), (5, 8191), (17, 5000), (1, 12345)])
+def test_long_and_ragged_rows(rows, cols):
+    rng = np.random.default_rng(cols)
+    x = (rng.standard_normal((rows, cols)) * 3).astype(np.float32)
+    d = rng.standard_normal((rows, cols)).astype(np.float32)
+    X, D = ft.tensor(x), ft.tensor(d)
+    y = F.softmax(X, axis=-1)
+    outs = [y, ft.grad(y, X, seed=D), ft.argmax(X, axis=1), ft.amin(X, axis=1), F.log_softmax(X, axis=-1)]
+    _check(outs, {id(X): x, id(D): d})
+
+
+@pytest.mark.parametrize("shape,axes", [((6, 300, 40), (1,)), ((6, 300, 40), (0, 2)), ((4096, 3), (0,)),
+                                        ((3, 4096), (0,)), ((2, 3, 5, 7), (1, 3)), ((1, 1, 257), (2,))])
+def test_reductions_over_other_axes(shape, axes):
+    rng = np.random.default_rng(len(shape) * 10 + axes[0])
+    x = rng.standard_normal(shape).astype(np.float32)
+    X = ft.tensor(x)
+    outs = [ft.sum(X, axis=axes), ft.amax(X, axis=axes), ft.mean(X, axis=axes, keepdims=True), ft.argmax(X, axis=axes[0]),
+            ft.prod(X * 0.5 + 1.0, axis=axes)]
+    _check(outs, {id(X): x})
+
+
+def test_boolean_and_wrapping_integer_reductions():
+    rng = np.random.default_rng(3)
+    a = rng.integers(-2**31, 2**31 - 1, (64, 3000), dtype=np.int64).astype(np.int32)
+    b = rng.integers(-2**62, 2**62, (64, 3000), dtype=np.int64)
+    A, B = ft.tensor(a, dtype=ft.int32), ft.tensor(b, dtype=ft.int64)
+    pos = A > 0
+    outs = [ft.sum(A, axis=1), ft.sum(B, axis=1), ft.sum(B), ft.any(pos, axis=1), ft.all(pos | (A < 100), axis=1),
+            ft.amax(A, axis=0), ft.argmin(B, axis=0), ft.prod(A, axis=1)]
+    _check(outs, {id(A): a, id(B): b})
+
+
+def test_empty_results_and_empty_operands():
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((6, 10)).astype(np.float32)
+    X = ft.tensor(x)
+    empty_rows = X[4:2]
+    assert empty_rows.shape == (0, 10)
+    outs = [empty_rows * 2.0, ft.sum(empty_rows, axis=0), ft.cat([X[:, :0], X[:, 3:5]], axis=1), X[:, 7:3].sum(axis=1)]
+    _check(outs, {id(X): x})
+
+
+def test_bf16_through_index_transforms():
+    rng = np.random.default_rng(8)
+    x = O.f32_to_bf16_bits(rng.standard_normal((300, 1024)).astype(np.float32))
+    idx = rng.integers(-2, 300, 200).astype(np.int32)
+    X, I = ft.tensor(x, dtype=ft.bf16), ft.tensor(idx, dtype=ft.int32)
+    outs = [X[I, ::2], ft.pad(X[::-1, 3:], ((1, 2), (0, 5)), constant_value=1.5),
+            ft.cat([X, X * 2.0], axis=0), F.softmax(ft.gather(X, I, axis=0), axis=-1),
+            ft.scatter_add(X[:50], I % 50, X[:200], axis=0)]
+    _check(outs, {id(X): x, id(I): idx})
