@@ -948,9 +948,9 @@ struct Emitter {
   }
 
   std::string build_row() {
-    // every chunk of the row is in range when the row is a whole number of
-    // thread-chunks; the bound check is then left out
-    const std::string CHK = d.NI % ((int64_t)K.tpr * K.vec) == 0 ? "if (true)" : "if (e0 < NI)";
+    // every chunk of the row is in range when the (nonempty) row is a whole
+    // number of thread-chunks; the bound check is then left out
+    const std::string CHK = d.NI > 0 && d.NI % ((int64_t)K.tpr * K.vec) == 0 ? "if (true)" : "if (e0 < NI)";
     // Phases: one element loop per dependency level of the row reductions.
     std::vector<const RedDef*> rows, cols;
     for (auto& rd : K.reds) (rd.role == ROLE_ROW ? rows : cols).push_back(&rd);

@@ -193,3 +193,15 @@ def test_encode_float_rne_subnormals_overflow():
     assert ir.round_float(65504, "f16") == 65504
     with pytest.raises(ValueError):
         ir.encode_float(65520, "f16")
+
+
+def test_empty_rows_keep_the_bound_check():
+    """A row reduction over empty rows ([R, 0]) must keep the per-chunk bound check:
+    every chunk is out of range, so the kernel reads nothing and writes identities."""
+    import torch
+    eng = ft.Engine("cuda:0", tune=False)
+    x = ft.Tensor(eng, ft.fp32, (6, 10), data=torch.empty(0))
+    s = x[:, 7:3].sum(axis=1)
+    spec, *_ = eng.compile(s)
+    src = spec.kernel_source(0)
+    assert "if (e0 < NI)" in src and "if (true)" not in src

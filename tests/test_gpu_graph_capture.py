@@ -22,7 +22,7 @@ def test_captured_launch_replays_with_new_inputs(cfg):
     rows, cols = 256, 2048
     shapes = [(rows, cols), (rows, cols)] if cfg == "softmax_vjp" else [(rows, cols)]
     host = [rng.standard_normal(s).astype(np.float32) for s in shapes]
-    leaves = [ft.tensor(h) for h in host]
+    leaves = [eng.tensor(h) for h in host]
     if cfg == "softmax_vjp":
         y = F.softmax(leaves[0], axis=-1)
         outs = [y, ft.grad(y, leaves[0], seed=leaves[1])]
