@@ -392,6 +392,10 @@ def run_fgt(args):
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline(args.cpu_threads, seconds=args.cpu_seconds)
+        # the reference's own CPU benchmarks run on one thread
+        # (docs/assets/torch-benchmark/fp32/metadata.json): report that figure beside
+        one = cpu_baseline(1, seconds=max(2.0, args.cpu_seconds / 3))
+        cpu["single_thread"] = {"value": one["value"], "unit": one["unit"], "sample": one["sample"]}
 
     if world > 1:
         dist.destroy_process_group()
