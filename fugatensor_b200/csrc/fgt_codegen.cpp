@@ -398,9 +398,12 @@ struct Emitter {
   int64_t stage_bytes = 0;         // bytes of one stage (all staged operands)
   // Shared-memory address (bytes from the dynamic base) of a thread's piece.
   std::string piece_off(const RowSite& rs, const std::string& stg) {
+    // a thread's own piece within this CTA (in a cluster the CTA holds
+    // nt of the row's tpr threads: index by the CTA-local thread)
+    const bool cl = K.cluster > 1;
     return "(" + std::to_string(rs.smem_off) + "u + (unsigned)((((" + stg + ") * " + std::to_string(K.rows_per_cta) +
-           " + grp) * " + std::to_string(K.nch) + " + c) * " + std::to_string(K.tpr) + " + lane) * " +
-           std::to_string(rs.bytes) + "u)";
+           " + grp) * " + std::to_string(K.nch) + " + c) * " + std::to_string(cl ? K.nt : K.tpr) + " + " +
+           (cl ? "tid" : "lane") + ") * " + std::to_string(rs.bytes) + "u)";
   }
   std::string site_load(const RowSite& rs, const std::string& arr, const char* rvar) {
     if (rs.uniform) return arr + "[c] = " + rs.ptr + "[" + itext(rs.addr, "e0", rvar) + "];";
@@ -563,7 +566,7 @@ struct Emitter {
           rs.bytes = K.vec * dtype_size(n.dt);
           // cp.async moves 4, 8 or 16 bytes; a stage (one row of every staged
           // operand) must fit the ring budget.
-          const int64_t piece = (int64_t)K.rows_per_cta * K.nch * K.tpr * rs.bytes;
+          const int64_t piece = (int64_t)K.rows_per_cta * K.nch * (K.tpr / K.cluster) * rs.bytes;
           rs.staged = P.opt.row_staging && (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) &&
                       stage_bytes + piece <= (int64_t)P.opt.ring_kb * 1024;
           if (rs.staged) stage_bytes += piece;
@@ -897,6 +900,7 @@ struct Emitter {
         }
       }
       out.push_back("}");
+      cluster_exchange(out, accs, tag);
       if (trailing_sync) out.push_back("__syncthreads();");
       return;
     }
@@ -911,6 +915,44 @@ struct Emitter {
       out.push_back("}");
     }
     out.push_back("__syncthreads();");
+  }
+
+  // Row split over a cluster: every CTA holds its part of each reduction (the
+  // same value in all its threads); thread 0 publishes it in a two-deep ring
+  // (cx_ counts exchanges), one cluster barrier makes the parts visible, and
+  // every thread combines them in rank order, so all CTAs agree bit for bit.
+  // The next exchange's barrier orders these reads before the ring slot is
+  // written again.
+  void cluster_exchange(std::vector<std::string>& out, const std::vector<std::pair<RedText, std::string>>& accs,
+                        const std::string& tag) {
+    if (K.cluster <= 1) return;
+    const std::string CL = std::to_string(K.cluster);
+    auto xt = [](const std::string& t) { return t == "bool" ? std::string("int") : t; };
+    for (auto& [t, a] : accs) {
+      kdecl.push_back("__shared__ " + xt(t.acc_t) + " smc_" + a + tag + "[2];");
+      if (t.arg) kdecl.push_back("__shared__ fgt_i64 smci_" + a + tag + "[2];");
+    }
+    out.push_back("if (tid == 0) {");
+    for (auto& [t, a] : accs) {
+      out.push_back("  smc_" + a + tag + "[cx_ & 1] = (" + xt(t.acc_t) + ")" + a + ";");
+      if (t.arg) out.push_back("  smci_" + a + tag + "[cx_ & 1] = " + a + "i;");
+    }
+    out.push_back("}");
+    out.push_back("fgt_cluster_sync();");
+    for (auto& [t, a] : accs) {
+      out.push_back(a + " = (" + t.acc_t + ")fgt_dsmem_ld(&smc_" + a + tag + "[cx_ & 1], 0u);");
+      if (t.arg) out.push_back(a + "i = fgt_dsmem_ld(&smci_" + a + tag + "[cx_ & 1], 0u);");
+      out.push_back("for (unsigned q_ = 1; q_ < " + CL + "u; ++q_) {");
+      if (t.arg)
+        out.push_back("  { const " + t.acc_t + " ov = (" + t.acc_t + ")fgt_dsmem_ld(&smc_" + a + tag + "[cx_ & 1], q_); " +
+                      "const fgt_i64 oi = fgt_dsmem_ld(&smci_" + a + tag + "[cx_ & 1], q_); " + arg_stmt(t, a, a + "i", "ov", "oi") +
+                      " }");
+      else
+        out.push_back("  { const " + t.acc_t + " ov = (" + t.acc_t + ")fgt_dsmem_ld(&smc_" + a + tag + "[cx_ & 1], q_); " +
+                      comb_stmt(t, a, "ov") + " }");
+      out.push_back("}");
+    }
+    out.push_back("++cx_;");
   }
 
   std::string arg_index(const RedDef& rd) {
@@ -1098,7 +1140,9 @@ struct Emitter {
       } else {
         lane[p].push_back(comb_stmt(t, a + "[c][v]", v));
       }
-      std::string slot = "((fgt_i64)blockIdx.x * " + std::to_string(K.rows_per_cta) + " + grp)";
+      std::string slot = "(" + std::string(K.cluster > 1 ? "(fgt_i64)(blockIdx.x / " + std::to_string(K.cluster) + ")"
+                                                          : "(fgt_i64)blockIdx.x") +
+                         " * " + std::to_string(K.rows_per_cta) + " + grp)";
       std::string pv = "((" + t.part_t + "*)(p.ws+" + std::to_string(rd->part_val) + "LL))";
       std::string body = pv + "[" + slot + "*" + std::to_string(d.NI) + "LL + e] = (" + t.part_t + ")" + a + "[c][v];";
       if (t.arg) body += " ((fgt_i64*)(p.ws+" + std::to_string(rd->part_idx) + "LL))[" + slot + "*" + std::to_string(d.NI) +
@@ -1125,8 +1169,16 @@ struct Emitter {
     const std::string NT = std::to_string(K.nt), TPR = std::to_string(K.tpr), VEC = std::to_string(K.vec),
                       NCH = std::to_string(K.nch), RPC = std::to_string(K.rows_per_cta);
     o << args_struct();
-    o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
-    o << "  const int tid = threadIdx.x; const int lane = tid % " << TPR << "; const int grp = tid / " << TPR << ";\n";
+    if (K.cluster > 1) {
+      // one row over a cluster: the row's thread index spans the cluster's CTAs
+      o << "extern \"C\" __global__ void __cluster_dims__(" << K.cluster << ", 1, 1) __launch_bounds__(" << NT << ") " << K.name
+        << "(const FgtArgs p) {\n";
+      o << "  const int tid = threadIdx.x; const unsigned crank = fgt_cluster_rank(); const int lane = (int)crank * " << NT
+        << " + tid; const int grp = 0;\n";
+    } else {
+      o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
+      o << "  const int tid = threadIdx.x; const int lane = tid % " << TPR << "; const int grp = tid / " << TPR << ";\n";
+    }
     o << "  (void)lane; (void)grp;\n";
     o << "  const fgt_i64 NR = " << d.NR << "LL, NI = " << d.NI << "LL; (void)NI;\n";
     put(o, kdecl, "  ");
@@ -1154,10 +1206,12 @@ struct Emitter {
       int64_t off = 0;
       for (auto* rs : staged_sites) {
         rs->smem_off = off;
-        off += (int64_t)stages * K.rows_per_cta * K.nch * K.tpr * rs->bytes;
+        off += (int64_t)stages * K.rows_per_cta * K.nch * (K.tpr / K.cluster) * rs->bytes;
       }
     }
-    const std::string stride = "(fgt_i64)gridDim.x * " + RPC;
+    const std::string stride = K.cluster > 1 ? "(fgt_i64)(gridDim.x / " + std::to_string(K.cluster) + ") * " + RPC
+                                             : "(fgt_i64)gridDim.x * " + RPC;
+    const std::string CB = K.cluster > 1 ? "(fgt_i64)(blockIdx.x / " + std::to_string(K.cluster) + ")" : "(fgt_i64)blockIdx.x";
     auto chunk_loop = [&](std::ostringstream& os, const std::string& ind, const std::function<void(const std::string&)>& body) {
       os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
       os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
@@ -1197,7 +1251,7 @@ struct Emitter {
     // stage (i+k) % S holds row i+k for k = 1..S (S cp.async groups pending).
     const std::string S = std::to_string(stages);
     if (!row_sites.empty()) {
-      o << "  { const fgt_i64 r0_ = (fgt_i64)blockIdx.x * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
+      o << "  { const fgt_i64 r0_ = " << CB << " * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
       reg_loads(o, "      ", "r0_", false);
       o << "    }\n";
       if (stages) {
@@ -1215,12 +1269,13 @@ struct Emitter {
       if (stages) o << "  int stg = " << (stages > 1 ? 1 : 0) << ";\n";
     }
     if (!rowpf_first.empty()) {
-      o << "  { const fgt_i64 r = (fgt_i64)blockIdx.x * " << RPC << " + grp; const bool rv = r < NR; " << digits_o() << "\n";
+      o << "  { const fgt_i64 r = " << CB << " * " << RPC << " + grp; const bool rv = r < NR; " << digits_o() << "\n";
       put(o, rowpf_first, "    ");
       o << "  }\n";
     }
     if (parity_rows) o << "  int it_ = 0;\n";
-    o << "  for (fgt_i64 rb = (fgt_i64)blockIdx.x * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
+    if (K.cluster > 1 && xw) o << "  int cx_ = 0;\n";
+    o << "  for (fgt_i64 rb = " << CB << " * " << RPC << "; rb < NR; rb += " << stride << ") {\n";
     o << "    const fgt_i64 r = rb + grp; const bool rv = r < NR; " << digits_o() << "\n";
     if (!rowpf.empty()) {
       put(o, rowpf, "    ");
@@ -1293,6 +1348,9 @@ struct Emitter {
     if (parity_rows) o << "    ++it_;\n";
     o << "  }\n";
     if (stages) o << "  fgt_cp_wait<0>();\n";
+    // no CTA of a cluster leaves while a peer may still read its shared
+    // memory (the last exchange has no later barrier of its own)
+    if (K.cluster > 1) o << "  fgt_cluster_sync();\n";
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";

@@ -171,6 +171,35 @@ template <int N> FGT_DEV fgt_u32 fgt_min_bf16x2_row(fgt_u32 acc, const fgt_u16 (
   }
   return acc;
 }
+// ---- thread-block clusters: a row split over the CTAs of a cluster combines
+// its reductions through distributed shared memory (DSMEM).
+FGT_DEV unsigned fgt_cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of every CTA of the cluster: writes before it are visible to
+// DSMEM reads after it.
+FGT_DEV void fgt_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// Value of `local`'s shared-memory location in CTA `rank` of the cluster.
+template <class T> FGT_DEV T fgt_dsmem_ld(const T* local, unsigned rank) {
+  static_assert(sizeof(T) == 4 || sizeof(T) == 8, "32- or 64-bit values");
+  const unsigned la = (unsigned)__cvta_generic_to_shared(local);
+  unsigned ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  union { T v; unsigned u[sizeof(T) / 4]; } w;
+  if (sizeof(T) == 4) {
+    asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(w.u[0]) : "r"(ra) : "memory");
+  } else {
+    unsigned long long b;
+    asm volatile("ld.shared::cluster.b64 %0, [%1];" : "=l"(b) : "r"(ra) : "memory");
+    w.u[0] = (unsigned)b;
+    w.u[sizeof(T) / 4 - 1] = (unsigned)(b >> 32);
+  }
+  return w.v;
+}
 template <class T> FGT_DEV T fgt_imax(T a, T b) { return a > b ? a : b; }
 template <class T> FGT_DEV T fgt_imin(T a, T b) { return a < b ? a : b; }
 

@@ -813,6 +813,13 @@ struct Planner {
       k.nt = (int)nt;
       k.tpr = (int)nt;
       k.rows_per_cta = 1;
+      // A cluster of CTAs shares the row: each CTA holds nt / cluster threads
+      // with the same per-thread state, so more rows fit on an SM.
+      const int cl = opt.row_cluster;
+      if (cl > 1 && nt % cl == 0 && nt / cl >= 64) {
+        k.cluster = cl;
+        k.nt = (int)(nt / cl);
+      }
     } else {
       int64_t tpr = 1;
       while (tpr < 32 && tpr * 2 <= nvec) tpr *= 2;
@@ -1195,6 +1202,7 @@ struct Planner {
     mix(opt.row_elems);
     mix(opt.row_staging);
     mix(opt.ring_kb);
+    mix(opt.row_cluster);
     char tag[16];
     std::snprintf(tag, sizeof tag, "%08x", (unsigned)(h ^ (h >> 32)));
     for (size_t i = 0; i < plan.kernels.size(); ++i) {
@@ -1279,7 +1287,8 @@ std::string plan_json(const Plan& plan) {
   for (size_t i = 0; i < plan.kernels.size(); ++i) {
     const KernelDef& k = plan.kernels[i];
     j << (i ? "," : "") << "{\"name\":\"" << k.name << "\",\"rows\":" << k.dom.NR << ",\"row_elements\":" << k.dom.NI
-      << ",\"threads\":" << k.nt << ",\"threads_per_row\":" << k.tpr << ",\"vector\":" << k.vec
+      << ",\"threads\":" << k.nt << ",\"threads_per_row\":" << k.tpr << ",\"cluster\":" << k.cluster
+      << ",\"vector\":" << k.vec
       << ",\"chunks\":" << k.nch << ",\"smem_bytes\":" << k.smem_bytes << ",\"streaming\":" << (k.streaming ? "true" : "false")
       << ",\"reductions\":" << k.reds.size() << ",\"row_phases\":" << k.row_phases << ",\"registers\":" << k.regs
       << ",\"spill_bytes\":" << k.spill_bytes << "}";

@@ -106,6 +106,7 @@ struct KernelDef {
   int fin_stage = 0;              // FIN: 0 = unsharded, 1 = CTA partials -> rank record, 2 = ranks -> outputs
   // geometry (chosen by the planner)
   int nt = 256, tpr = 256, vec = 1, nch = 1, unroll = 1;
+  int cluster = 1;                // ROW: CTAs of a thread-block cluster sharing one row (tpr = nt * cluster)
   bool streaming = false;
   int64_t rows_per_cta = 1;
   int64_t max_ctas = 0;           // partial slots reserved (grid upper bound)
@@ -133,6 +134,7 @@ struct Options {
   int row_staging = 1;            // next row arrives via cp.async into shared memory (FGT_ROW_STAGING=0: registers)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
   int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)
+  int row_cluster = 1;            // CTAs per row in block-per-row kernels (thread-block cluster; FGT_ROW_CLUSTER)
 };
 
 struct Plan {

@@ -280,8 +280,12 @@ LoadedModule& module_for(fgt_spec* s) {
     if (smem > 0)
       cu_check(drv().FuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, smem), "cuFuncSetAttribute");
     int occ = 1;
-    cu_check(drv().OccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, s->plan.kernels[i].nt, (size_t)smem),
-             "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    const KernelDef& kd = s->plan.kernels[i];
+    if (drv().OccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, kd.nt, (size_t)smem) != CUDA_SUCCESS || occ < 1) {
+      // estimate from the compile report (cluster kernels may not answer the query)
+      occ = kd.regs > 0 ? std::max(1, 65536 / (kd.regs * kd.nt)) : 1;
+      if (smem > 0) occ = std::max(1, std::min<int>(occ, (int)((227 * 1024) / (smem + 1024))));
+    }
     lm.mods.push_back(m);
     lm.fn.push_back(f);
     lm.occupancy.push_back(std::max(1, occ));
@@ -310,9 +314,11 @@ int64_t grid_for(const KernelDef& k, const LoadedModule& lm, size_t idx) {
   const int64_t resident = (int64_t)lm.sms * lm.occupancy[idx];
   switch (k.kind) {
     case KKind::ROW: {
+      // a cluster of k.cluster CTAs per row group; the grid is a whole number of clusters
       int64_t groups = (k.dom.NR + k.rows_per_cta - 1) / k.rows_per_cta;
-      int64_t g = std::min(groups, resident);
-      if (k.max_ctas > 0) g = std::min(g, k.max_ctas);
+      int64_t g = std::min(groups * k.cluster, resident);
+      if (k.max_ctas > 0) g = std::min(g, k.max_ctas * k.cluster);
+      g = std::max<int64_t>(k.cluster, g / k.cluster * k.cluster);
       return g;
     }
     case KKind::ELEM: {
@@ -371,7 +377,7 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
     if (k.producer >= 0) nparts = parts[k.producer];
     if (empty_kernel(k)) continue;
     int64_t grid = grid_for(k, lm, i);
-    parts[i] = k.kind == KKind::ROW ? grid * k.rows_per_cta : grid;
+    parts[i] = k.kind == KKind::ROW ? grid / k.cluster * k.rows_per_cta : grid;
     ArgBlock a = make_args(p, inputs, outputs, ws, nparts);
     void* params[] = {a.bytes.data()};
     cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, 1, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
@@ -445,6 +451,9 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       require(options->ring_kb >= 0 && options->ring_kb <= 200, "ring_kb must be in [0, 200]");
       if (options->row_elems > 0) opt.row_elems = options->row_elems;
       if (options->ring_kb > 0) opt.ring_kb = options->ring_kb;
+      require(options->row_cluster >= 0 && options->row_cluster <= 8 && (options->row_cluster & (options->row_cluster - 1)) == 0,
+              "row_cluster must be 0 or a power of two up to 8");
+      if (options->row_cluster > 0) opt.row_cluster = options->row_cluster;
     }
     // FGT_ROW_STAGING=0 keeps streamed row operands in registers
     // (double-buffered) instead of the shared-memory ring.
@@ -455,6 +464,10 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       row_elems_forced = true;
     }
     if (const char* rk = std::getenv("FGT_RING_KB")) opt.ring_kb = std::max(4, std::min(200, std::atoi(rk)));
+    if (const char* rc = std::getenv("FGT_ROW_CLUSTER")) {
+      const int v = std::atoi(rc);
+      if (v == 1 || v == 2 || v == 4) opt.row_cluster = v;
+    }
     int sms = current_sm_count();
     if (sms > 0) opt.num_sms = sms;
     auto spec = std::make_unique<fgt_spec>();

@@ -12,7 +12,10 @@ inputs of the partition's own types and shapes (CUDA events, L2 flushed
 between launches), and keeps the fastest. The choice is stored in
 ``tuning.json`` in the kernel cache directory, keyed by the partition's
 structure, the GPU, and the library build, so later processes skip the
-measurement. All geometries compute the same results; only speed differs.
+measurement. Every geometry computes the partition's results within its
+tolerances; floating-point sums may differ in the last bits between
+geometries (a row's summation order follows how its elements are spread over
+threads), and the persisted choice keeps one geometry per partition.
 """
 from __future__ import annotations
 
@@ -24,8 +27,10 @@ from pathlib import Path
 
 from . import _fgt, ir
 
-# (elements per thread per row operand, shared-memory ring KB); (0, 0) is the library default.
-CANDIDATES = ((0, 0), (16, 32), (16, 24), (32, 96), (32, 32), (32, 24))
+# (elements per thread per row operand, shared-memory ring KB, CTAs per row); (0, 0, 0) is the
+# library default. Cluster candidates split each row over two CTAs of a thread-block cluster.
+CANDIDATES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0),
+              (16, 32, 2), (32, 32, 2), (32, 64, 2))
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 _lock = threading.Lock()
 
@@ -114,21 +119,22 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     path = _db_path(cache_dir)
     hit = _load(path).get(key)
     if hit is not None:
-        e, r = hit["geometry"]
-        if (e, r) == (0, 0):
+        geom = tuple(hit["geometry"]) + (0,) * (3 - len(hit["geometry"]))
+        if geom == (0, 0, 0):
             return default
-        return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r)
+        e, r, c = geom
+        return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r, row_cluster=c)
     specs, seen = [], {}
-    for e, r in CANDIDATES:
-        s = default if (e, r) == (0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
-                                                       row_elems=e, ring_kb=r)
+    for e, r, c in CANDIDATES:
+        s = default if (e, r, c) == (0, 0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
+                                                             row_elems=e, ring_kb=r, row_cluster=c)
         src = tuple(s.kernel_source(i) for i in range(s.kernel_count))
         if src in seen:
             continue
         seen[src] = True
-        specs.append(((e, r), s))
+        specs.append(((e, r, c), s))
     if len(specs) == 1:
-        _store(path, key, {"geometry": [0, 0], "ms": None})
+        _store(path, key, {"geometry": [0, 0, 0], "ms": None})
         return default
     gen = torch.Generator(device=dev).manual_seed(0)
     with torch.cuda.device(dev):
@@ -138,5 +144,5 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
         del inputs, flush
     ms, geom, best = min(timed, key=lambda t: t[0])
     _store(path, key, {"geometry": list(geom), "ms": round(ms, 5),
-                       "candidates": {f"{g[0]}x{g[1]}": round(t, 5) for t, g, _ in timed}})
+                       "candidates": {"x".join(map(str, g)): round(t, 5) for t, g, _ in timed}})
     return best

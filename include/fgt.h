@@ -143,7 +143,8 @@ typedef struct fgt_spec_options {
   const char* cache_dir;      /* compiled-kernel disk cache (NULL: FGT_CACHE_DIR env)  */
   int32_t ring_kb;            /* row kernels: shared-memory row ring budget per CTA in */
                               /* KB (0: the library's choice, 96)                      */
-  int32_t reserved;
+  int32_t row_cluster;        /* block-per-row kernels: CTAs of a thread-block cluster */
+                              /* sharing each row (0/1: none; 2, 4, 8)                 */
 } fgt_spec_options;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
