@@ -1290,20 +1290,17 @@ struct Emitter {
       o << "    }\n";
     }
     put(o, rowdecl, "    ");
-    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind,
-                          const std::vector<std::string>& vpre = {}, const std::vector<std::string>& vpost = {}) {
+    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind) {
       if (cached) o << ind << "  #pragma unroll\n";
       else o << ind << "  #pragma unroll 1\n";
       o << ind << "  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << ind << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
       o << ind << "    " << CHK << " {\n";
       put(o, chunkpre[p], ind + "      ");
-      put(o, vpre, ind + "      ");
       o << ind << "      #pragma unroll\n" << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
       put(o, body, ind + "        ");
       o << ind << "      }\n";
-      put(o, vpost, ind + "      ");
       put(o, chunkpost[p], ind + "      ");
       o << ind << "    }\n" << ind << "  }\n";
     };
