@@ -1,0 +1,40 @@
+"""Seeded random partitions (tests/fuzz_graphs.py): every one plans and compiles
+for sm_100a on the CPU; on a B200 every output matches the oracle (bit-exact for
+integer and index outputs, the f32 tolerance otherwise)."""
+import numpy as np
+import pytest
+
+import oracle as O
+from fugatensor_b200 import _fgt
+from tests import fuzz_graphs
+from tests._util import assert_matches
+
+SEEDS = range(60)
+
+
+def test_fuzz_partitions_plan_and_compile():
+    for seed in SEEDS:
+        g, outs, arrays = fuzz_graphs.build(seed)
+        desc = g.descriptor(outs)
+        spec = _fgt.Spec(desc)
+        assert spec.kernel_count >= 1, seed
+        O.evaluate(desc, arrays)  # the oracle accepts the same descriptor
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", SEEDS)
+def test_fuzz_partitions_match_oracle(seed):
+    import torch
+    g, outs, arrays = fuzz_graphs.build(seed)
+    desc = g.descriptor(outs)
+    ref = O.evaluate(desc, arrays)
+    spec = _fgt.Spec(desc)
+    dev = torch.device("cuda", 0)
+    res = _fgt.run(spec, *[torch.from_numpy(a).to(dev) for a in arrays])
+    torch.cuda.synchronize()
+    for k, (o, r, (dt, _)) in enumerate(zip(res, ref, spec.output_types)):
+        got = o.cpu().numpy()
+        if dt in ("i32", "i64", "bool"):
+            assert np.array_equal(got, r), (seed, k)
+        else:
+            assert_matches(got, r, dt, what=f"seed {seed} output {k}")
