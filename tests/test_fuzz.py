@@ -1,6 +1,8 @@
 """Seeded random partitions (tests/fuzz_graphs.py): every one plans and compiles
 for sm_100a on the CPU; on a B200 every output matches the oracle (bit-exact for
 integer and index outputs, the f32 tolerance otherwise)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -9,7 +11,7 @@ from fugatensor_b200 import _fgt
 from tests import fuzz_graphs
 from tests._util import assert_matches
 
-SEEDS = range(60)
+SEEDS = range(int(os.environ.get("FGT_FUZZ_SEEDS", "60")))  # more seeds for a deeper sweep
 
 
 def test_fuzz_partitions_plan_and_compile():
