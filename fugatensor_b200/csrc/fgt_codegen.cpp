@@ -625,7 +625,11 @@ struct Emitter {
       if (cached && s.p > L.phase && expensive(g.nodes[id].op) && m.guard.empty()) D = {SC_CACHE, L.phase};
     }
     if (s.k == SC_PROLANE && D.k == SC_LANE) D = s;
-    std::string key = std::to_string(id) + "@" + m.key() + "#" + std::to_string((int)D.k) + ":" + std::to_string(D.p);
+    // a prologue value read from the row loop goes through its persisted
+    // register copy, keyed apart from the prologue-local temporary
+    const bool persisted = D.k == SC_PROLANE && s.k != SC_PROLANE;
+    std::string key = std::to_string(id) + "@" + m.key() + "#" + std::to_string((int)D.k) + ":" +
+                      std::to_string(D.p) + (persisted ? "+cv" : "");
     auto it = memo.find(key);
     if (it != memo.end()) return it->second;
     std::string r;
@@ -636,7 +640,7 @@ struct Emitter {
       rowdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
       lane[D.p].push_back(cname + "[c][v] = " + v + ";");
       r = cname + "[c][v]";
-    } else if (D.k == SC_PROLANE && s.k != SC_PROLANE) {
+    } else if (persisted) {
       std::string v = val(id, m, Sc{SC_PROLANE, 0});
       std::string cname = fresh("cv");
       kdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
@@ -992,7 +996,9 @@ struct Emitter {
   std::string build_row() {
     // every chunk of the row is in range when the (nonempty) row is a whole
     // number of thread-chunks; the bound check is then left out
-    const std::string CHK = d.NI > 0 && d.NI % ((int64_t)K.tpr * K.vec) == 0 ? "if (true)" : "if (e0 < NI)";
+    // (with column tiles: a whole number of tiles)
+    const int64_t span = K.col_tiles > 1 ? K.tile_elems : (int64_t)K.tpr * K.vec;
+    const std::string CHK = d.NI > 0 && d.NI % span == 0 ? "if (true)" : "if (e0 < NI)";
     // Phases: one element loop per dependency level of the row reductions.
     std::vector<const RedDef*> rows, cols;
     for (auto& rd : K.reds) (rd.role == ROLE_ROW ? rows : cols).push_back(&rd);
@@ -1168,6 +1174,9 @@ struct Emitter {
     std::ostringstream o;
     const std::string NT = std::to_string(K.nt), TPR = std::to_string(K.tpr), VEC = std::to_string(K.vec),
                       NCH = std::to_string(K.nch), RPC = std::to_string(K.rows_per_cta);
+    // element offset of chunk c of this thread; column tiles add the tile's base
+    const std::string E0 = (K.col_tiles > 1 ? "(fgt_i64)blockIdx.y * " + std::to_string(K.tile_elems) + "LL + " : std::string()) +
+                           "((fgt_i64)c * " + TPR + " + lane) * " + VEC;
     o << args_struct();
     if (K.cluster > 1) {
       // one row over a cluster: the row's thread index spans the cluster's CTAs
@@ -1184,7 +1193,7 @@ struct Emitter {
     put(o, kdecl, "  ");
     if (cached && !prolane.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
-      o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << "    const fgt_i64 e0 = " << E0 << ";\n";
       o << "    " << CHK << " {\n";
       put(o, prosites, "      ");
       o << "      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
@@ -1214,7 +1223,7 @@ struct Emitter {
     const std::string CB = K.cluster > 1 ? "(fgt_i64)(blockIdx.x / " + std::to_string(K.cluster) + ")" : "(fgt_i64)blockIdx.x";
     auto chunk_loop = [&](std::ostringstream& os, const std::string& ind, const std::function<void(const std::string&)>& body) {
       os << ind << "#pragma unroll\n" << ind << "for (int c = 0; c < " << NCH << "; ++c) {\n";
-      os << ind << "  const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      os << ind << "  const fgt_i64 e0 = " << E0 << ";\n";
       os << ind << "  " << CHK << " {\n";
       body(ind + "    ");
       os << ind << "  }\n" << ind << "}\n";
@@ -1294,7 +1303,7 @@ struct Emitter {
       if (cached) o << ind << "  #pragma unroll\n";
       else o << ind << "  #pragma unroll 1\n";
       o << ind << "  for (int c = 0; c < " << NCH << "; ++c) {\n";
-      o << ind << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << ind << "    const fgt_i64 e0 = " << E0 << ";\n";
       o << ind << "    " << CHK << " {\n";
       put(o, chunkpre[p], ind + "      ");
       o << ind << "      #pragma unroll\n" << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
@@ -1350,7 +1359,7 @@ struct Emitter {
     if (K.cluster > 1) o << "  fgt_cluster_sync();\n";
     if (!colfin.empty()) {
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
-      o << "    const fgt_i64 e0 = ((fgt_i64)c * " << TPR << " + lane) * " << VEC << ";\n";
+      o << "    const fgt_i64 e0 = " << E0 << ";\n";
       o << "    " << CHK << " {\n      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << "        const fgt_i64 e = e0 + v;\n";
       put(o, colfin, "        ");
@@ -1410,12 +1419,13 @@ struct Emitter {
       kdecl.push_back(t.acc_t + " " + a + " = " + t.ident + ";");
       if (t.arg) kdecl.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
       std::string v = val(g.nodes[rd.node].args[0], rd.opmap, Sc{SC_LANE, 0});
-      // Two-level accumulation: the VEC lanes of a chunk reduce in the value
-      // type with a 32-bit lane index, then the chunk folds into the thread
-      // accumulator (f64 sums, 64-bit indices) once per chunk.
+      // Two-level accumulation: the VEC lanes of a chunk reduce with a 32-bit
+      // lane index, then the chunk folds into the thread accumulator (64-bit
+      // indices) once per chunk. Sums and products keep the accumulator's type
+      // in the lanes too (f64 for f32), so a whole-tensor sum rounds once.
       const std::string la = a + "l";
-      const std::string lt = t.arg ? t.acc_t : (t.acc_t == "double" ? std::string("float") : t.acc_t);
-      const std::string lident = (t.acc_t == "double") ? (t.op == FGT_OP_REDUCE_SUM ? "0.0f" : "1.0f") : t.ident;
+      const std::string lt = t.acc_t;
+      const std::string lident = t.ident;
       const std::string ix = arg_index(rd);
       if (t.arg && ix == "(0LL+1LL*e)") {
         chunkpre[0].push_back(lt + " " + la + " = " + t.ident + "; int " + la + "i = 0x7fffffff;");
@@ -1430,7 +1440,7 @@ struct Emitter {
       } else {
         chunkpre[0].push_back(lt + " " + la + " = " + lident + ";");
         lane[0].push_back(comb_stmt(t, la, v));
-        chunkpost[0].push_back(comb_stmt(t, a, t.acc_t == "double" ? "(double)" + la : la));
+        chunkpost[0].push_back(comb_stmt(t, a, la));
       }
       accs.push_back({t, a});
       std::string ps = "((" + t.part_t + "*)(p.ws+" + std::to_string(rd.part_val) + "LL))[blockIdx.x] = (" + t.part_t + ")" + a + ";";

@@ -810,6 +810,8 @@ struct Planner {
     if (nvec >= 256) {
       int64_t nt = 128;
       while (nt * 2 <= 1024 && nt * 2 * per_thread_chunks <= nvec) nt *= 2;
+      // a row just past nt x 16 chunks takes more threads rather than streaming
+      while (nt < 1024 && (nvec + nt - 1) / nt > 16) nt *= 2;
       k.nt = (int)nt;
       k.tpr = (int)nt;
       k.rows_per_cta = 1;
@@ -830,6 +832,22 @@ struct Planner {
     k.nch = (int)((nvec + k.tpr - 1) / k.tpr);
     k.streaming = k.nch > 16;
     if (k.streaming) k.nch = (int)((nvec + k.tpr - 1) / k.tpr);
+  }
+
+  // Column reductions over rows longer than the register-resident limit: the
+  // row splits into column tiles (blockIdx.y), each register-resident with
+  // per-thread column accumulators; a CTA walks its rows for one tile, and
+  // its partials fill that tile's part of its slots.
+  void geometry_tiles(KernelDef& k) {
+    const int64_t per_thread_chunks = std::max<int64_t>(1, (opt.row_elems + k.vec - 1) / k.vec);
+    k.nt = k.tpr = 256;
+    k.rows_per_cta = 1;
+    k.cluster = 1;
+    k.nch = (int)std::min<int64_t>(16, per_thread_chunks);
+    k.tile_elems = (int64_t)k.nt * k.nch * k.vec;
+    k.col_tiles = (k.dom.NI + k.tile_elems - 1) / k.tile_elems;
+    k.streaming = false;
+    if (k.col_tiles > 65535) fail(FGT_ERR_UNSUPPORTED, "column reductions over rows of more than 2^28 elements");
   }
 
   void geometry_elem(KernelDef& k) {
@@ -880,7 +898,11 @@ struct Planner {
     }
   }
 
-  void plan_group(int r0) {
+  // drop: reductions of this role stay out of the group (later groups take them)
+  void plan_group(int r0, int drop = -1) {
+    const std::set<int> saved_done = done_outputs;
+    const std::vector<Loc> saved_loc = loc;
+    const int64_t saved_ws = ws;
     Sig s0 = signature(g, r0);
     KernelDef k;
     k.kind = s0.form == 2 ? KKind::ELEM : KKind::ROW;
@@ -919,6 +941,7 @@ struct Planner {
         } else {
           continue;
         }
+        if (rd.role == drop) continue;
       }
       if (combine.count(r)) {
         if (rd.role == ROLE_ROW) {
@@ -1044,10 +1067,26 @@ struct Planner {
     choose_vec(k, an.loads, eo);
     if (k.kind == KKind::ROW) geometry_row(k);
     else geometry_elem(k);
-    // Column reductions need register accumulators per element: not in
-    // streaming rows.
-    if (k.kind == KKind::ROW && k.streaming && has_col)
-      fail(FGT_ERR_UNSUPPORTED, "column reductions over rows longer than the register-resident limit");
+    // Column reductions need register accumulators per element, so not in
+    // streaming rows: a group that also holds row reductions is planned again
+    // without the role r0 does not have, and a column-only group splits its
+    // rows into register-resident column tiles.
+    if (k.kind == KKind::ROW && k.streaming && has_col) {
+      int r0_role = ROLE_COL;
+      bool has_row = false;
+      for (auto& rd : reds) {
+        if (rd.node == r0) r0_role = rd.role;
+        has_row = has_row || rd.role == ROLE_ROW;
+      }
+      if (has_row) {
+        done_outputs = saved_done;
+        loc = saved_loc;
+        ws = saved_ws;
+        plan_group(r0, r0_role == ROLE_COL ? ROLE_ROW : ROLE_COL);
+        return;
+      }
+      geometry_tiles(k);
+    }
     k.reds = reds;
     const int kidx = (int)plan.kernels.size();
     plan.kernels.push_back(k);
@@ -1058,7 +1097,8 @@ struct Planner {
     KernelDef& prod = plan.kernels[kidx];
     // Partial buffers: one slot per (CTA x row group) of the producer; the
     // launch never uses more CTAs than can be resident at once.
-    const int64_t resident = (int64_t)opt.num_sms * std::max(1, 2048 / prod.nt);
+    const int64_t resident =
+        std::max<int64_t>(1, (int64_t)opt.num_sms * std::max(1, 2048 / prod.nt) / std::max<int64_t>(1, prod.col_tiles));
     const int64_t units = prod.kind == KKind::ROW ? (prod.dom.NR + prod.rows_per_cta - 1) / prod.rows_per_cta
                                                   : (prod.dom.NI / std::max(1, prod.vec) + prod.nt - 1) / prod.nt;
     prod.max_ctas = std::max<int64_t>(1, std::min(resident, units));
@@ -1290,6 +1330,7 @@ std::string plan_json(const Plan& plan) {
       << ",\"threads\":" << k.nt << ",\"threads_per_row\":" << k.tpr << ",\"cluster\":" << k.cluster
       << ",\"vector\":" << k.vec
       << ",\"chunks\":" << k.nch << ",\"smem_bytes\":" << k.smem_bytes << ",\"streaming\":" << (k.streaming ? "true" : "false")
+      << ",\"col_tiles\":" << k.col_tiles
       << ",\"reductions\":" << k.reds.size() << ",\"row_phases\":" << k.row_phases << ",\"registers\":" << k.regs
       << ",\"spill_bytes\":" << k.spill_bytes << "}";
   }

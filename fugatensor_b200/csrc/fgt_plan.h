@@ -107,6 +107,8 @@ struct KernelDef {
   // geometry (chosen by the planner)
   int nt = 256, tpr = 256, vec = 1, nch = 1, unroll = 1;
   int cluster = 1;                // ROW: CTAs of a thread-block cluster sharing one row (tpr = nt * cluster)
+  int64_t col_tiles = 1;          // ROW, column reductions only: the row splits into tiles of tile_elems (blockIdx.y)
+  int64_t tile_elems = 0;
   bool streaming = false;
   int64_t rows_per_cta = 1;
   int64_t max_ctas = 0;           // partial slots reserved (grid upper bound)

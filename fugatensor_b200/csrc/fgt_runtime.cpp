@@ -316,7 +316,8 @@ int64_t grid_for(const KernelDef& k, const LoadedModule& lm, size_t idx) {
     case KKind::ROW: {
       // a cluster of k.cluster CTAs per row group; the grid is a whole number of clusters
       int64_t groups = (k.dom.NR + k.rows_per_cta - 1) / k.rows_per_cta;
-      int64_t g = std::min(groups * k.cluster, resident);
+      // column tiles (gridDim.y) share the resident CTAs
+      int64_t g = std::min(groups * k.cluster, std::max<int64_t>(1, resident / std::max<int64_t>(1, k.col_tiles)));
       if (k.max_ctas > 0) g = std::min(g, k.max_ctas * k.cluster);
       g = std::max<int64_t>(k.cluster, g / k.cluster * k.cluster);
       return g;
@@ -380,7 +381,8 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
     parts[i] = k.kind == KKind::ROW ? grid / k.cluster * k.rows_per_cta : grid;
     ArgBlock a = make_args(p, inputs, outputs, ws, nparts);
     void* params[] = {a.bytes.data()};
-    cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, 1, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
+    const unsigned gy = k.kind == KKind::ROW ? (unsigned)std::max<int64_t>(1, k.col_tiles) : 1u;
+    cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, gy, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
                                 nullptr),
              "cuLaunchKernel");
     for (int c : p.collectives) {
@@ -477,6 +479,12 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       generate_sources(*plan);
       cubins->clear();
       for (auto& k : plan->kernels) {
+        // FGT_DUMP_DIR: write each kernel's generated source before compiling it (debugging)
+        if (const char* dump = std::getenv("FGT_DUMP_DIR")) {
+          mkdirs(dump);
+          std::ofstream f(std::string(dump) + "/" + k.name + ".cu");
+          f << k.source;
+        }
         Compiled c = compile_cubin(k.name, std::string(fgt_device_library_source) + "\n" + k.source, dir);
         k.regs = c.regs;
         k.spill_bytes = c.spill_bytes;

@@ -205,3 +205,30 @@ def test_empty_rows_keep_the_bound_check():
     spec, *_ = eng.compile(s)
     src = spec.kernel_source(0)
     assert "if (e0 < NI)" in src and "if (true)" not in src
+
+
+def test_column_reductions_over_long_rows_plan_as_tiles():
+    """Rows past the register-resident limit: a column-only group splits the row
+    into column tiles; a group with row reductions too keeps the seed's role and
+    leaves the other role to a later group."""
+    from fugatensor_b200 import _fgt
+    g = ir.Graph()
+    x = g.parameter("f32", (8, 100001))
+    s = _fgt.Spec(g.descriptor([g.reduce_sum(x, (0,)), g.argmax(x, 0)]))
+    ks = s.execution_plan["cuda_lowering"]["kernels"]
+    row = [k for k in ks if k["name"].startswith("fgt_row")]
+    assert len(row) == 1 and row[0]["col_tiles"] == 25 and not row[0]["streaming"]
+    assert "blockIdx.y * 4096LL" in s.kernel_source(0) and "if (e0 < NI)" in s.kernel_source(0)
+    for first_row in (True, False):
+        g = ir.Graph()
+        x = g.parameter("f32", (64, 100000))
+        rs, cs = g.reduce_sum(x, (1,)), g.reduce_sum(g.mul(x, x), (0,))
+        s = _fgt.Spec(g.descriptor([rs, cs] if first_row else [cs, rs]))
+        row = [k for k in s.execution_plan["cuda_lowering"]["kernels"] if k["name"].startswith("fgt_row")]
+        assert sorted((k["streaming"], k["col_tiles"]) for k in row) == [(False, 25), (True, 1)]
+    # a row just past 256 threads x 16 chunks takes more threads instead of streaming
+    g = ir.Graph()
+    x = g.parameter("f32", (64, 129, 33))
+    s = _fgt.Spec(g.descriptor([g.reduce_sum(x, (0,))]))
+    k0 = s.execution_plan["cuda_lowering"]["kernels"][0]
+    assert k0["threads_per_row"] == 512 and not k0["streaming"] and k0["col_tiles"] == 1

@@ -81,3 +81,30 @@ def test_bf16_through_index_transforms():
             ft.cat([X, X * 2.0], axis=0), F.softmax(ft.gather(X, I, axis=0), axis=-1),
             ft.scatter_add(X[:50], I % 50, X[:200], axis=0)]
     _check(outs, {id(X): x, id(I): idx})
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 100001), (3, 1 << 18), (33, 70000)])
+def test_column_reductions_over_long_rows(rows, cols):
+    """Column reductions over rows past the register-resident limit run as column
+    tiles; groups that also hold row reductions split into a streamed row kernel
+    and a tiled column kernel."""
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    d = rng.standard_normal((rows, cols)).astype(np.float32)
+    X, D = ft.tensor(x), ft.tensor(d)
+    outs = [ft.sum(X * D, axis=0), ft.argmax(X, axis=0), ft.amin(X, axis=0), X + D,
+            ft.sum(X, axis=1), ft.sum(X * X, axis=0)]
+    _check(outs, {id(X): x, id(D): d})
+
+
+def test_layer_norm_vjp_over_long_rows():
+    rng = np.random.default_rng(12)
+    rows, cols = 16, 80000
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    dy = rng.standard_normal((rows, cols)).astype(np.float32)
+    w = (rng.standard_normal(cols) * 0.1 + 1).astype(np.float32)
+    b = (rng.standard_normal(cols) * 0.1).astype(np.float32)
+    X, DY, W, B = ft.tensor(x), ft.tensor(dy), ft.tensor(w), ft.tensor(b)
+    y = F.layer_norm(X, (cols,), W, B)
+    dx, dw, db = ft.grad(y, [X, W, B], seed=DY)
+    _check([y, dx, dw, db], {id(X): x, id(DY): dy, id(W): w, id(B): b})
