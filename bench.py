@@ -236,7 +236,7 @@ def run_fgt(args):
     if not args.skip_table and world == 1:
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
         for c, vs in W.VARIANTS.items():
-            for dt in (("f32", "bf16") if c == "c2" else ("f32",)):
+            for dt in W.LABELS[c]:
                 r, h = W.FULL[c]
                 tt = device_inputs(c, r, h, dt, device)
                 for v in vs:
@@ -293,7 +293,7 @@ def run_fgt(args):
         from fugatensor_b200 import sharded
         group = sharded.ShardGroup(world, rank)
         peak_, _ = measured_peak()
-        for c, v, dt in (("c4", "global_reductions", "f32"), ("c3", "layernorm_vjp", "f32")):
+        for c, v, dt in (("c4", "global_reductions", "f32"), ("c3", "layernorm_vjp", "bf16")):
             r, h = W.FULL[c]
             tt = device_inputs(c, r // world, h, dt, device, seed=rank)
             dts = W.input_dtypes(c, dt)

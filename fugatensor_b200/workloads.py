@@ -40,7 +40,7 @@ def f32_to_bf16_bits(x):
     return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
 
 
-def make_inputs(cfg, rows, cols, dtype="f32"):
+def make_inputs(cfg, rows, cols, dtype=None):
     """Seeded host inputs (numpy; bf16 as uint16 bits) for a workload."""
     if cfg == "c1":
         rng = np.random.default_rng(0)
@@ -82,7 +82,14 @@ INPUT_DTYPES = {
 }
 
 
-def input_dtypes(cfg, dtype="f32"):
+# the dtype labels each workload runs at (c3 is bf16 throughout; c5 mixes i32 and f16)
+LABELS = {"c1": ("f32",), "c2": ("f32", "bf16"), "c3": ("bf16",), "c4": ("f32",), "c5": ("mixed",)}
+
+
+def input_dtypes(cfg, dtype=None):
+    dtype = dtype or LABELS[cfg][0]
+    if dtype not in LABELS[cfg]:
+        raise ValueError(f"workload {cfg} runs at {LABELS[cfg]}, not {dtype}")
     d = dict(INPUT_DTYPES[cfg])
     if cfg == "c2" and dtype == "bf16":
         d = {"X": "bf16", "dY": "bf16"}

@@ -46,7 +46,7 @@ def assert_matches(got, ref, dtype, rtol=None, what=""):
                                   f"(got {g[fin][worst]:.6e}), bound {bound[worst]:.3e}")
 
 
-def trace_workload(engine, cfg, variant, rows, cols, dtype="f32"):
+def trace_workload(engine, cfg, variant, rows, cols, dtype=None):
     inp = W.make_inputs(cfg, rows, cols, dtype)
     dts = W.input_dtypes(cfg, dtype)
     tensors = {k: engine.tensor(v, dtype=dts[k]) for k, v in inp.items()}

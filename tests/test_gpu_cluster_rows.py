@@ -18,8 +18,8 @@ from tests._util import assert_matches, oracle_outputs, trace_workload
 pytestmark = pytest.mark.gpu
 
 CASES = [("c2", "softmax_fwd", "f32"), ("c2", "softmax_vjp", "f32"), ("c2", "softmax_vjp", "bf16"),
-         ("c3", "layernorm_vjp", "f32"), ("c3", "rmsnorm_vjp", "f32"), ("c3", "layernorm_fwd", "f32"),
-         ("c5", "broadcast_select", "f32")]
+         ("c3", "layernorm_vjp", "bf16"), ("c3", "rmsnorm_vjp", "bf16"), ("c3", "layernorm_fwd", "bf16"),
+         ("c5", "broadcast_select", "mixed")]
 
 
 def _run_spec(spec, arrays):

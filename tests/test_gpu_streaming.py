@@ -15,7 +15,7 @@ def _bits(a):
     return a.view(np.uint8)
 
 
-def _both(cfg, variants, rows, cols, dtype="f32"):
+def _both(cfg, variants, rows, cols, dtype=None):
     inp = W.make_inputs(cfg, rows, cols, dtype)
     dts = W.input_dtypes(cfg, dtype)
     eng = ft.Engine("cuda:0")
@@ -33,9 +33,9 @@ def _both(cfg, variants, rows, cols, dtype="f32"):
 @pytest.mark.parametrize("cfg,variants,rows,cols,dtype", [
     ("c2", ("softmax_fwd", "softmax_vjp"), 1024, 8192, "f32"),
     ("c2", ("softmax_fwd", "softmax_vjp"), 512, 8192, "bf16"),
-    ("c3", ("layernorm_fwd",), 256, 8192, "f32"),
+    ("c3", ("layernorm_fwd",), 256, 8192, "bf16"),
     ("c1", ("chain_rowsum",), 2048, 4096, "f32"),
-    ("c5", ("broadcast_select",), 1024, 8192, "f32"),
+    ("c5", ("broadcast_select",), 1024, 8192, "mixed"),
 ])
 def test_streamed_rows_match_device_evaluate(monkeypatch, cfg, variants, rows, cols, dtype, chunk_bytes):
     monkeypatch.setattr(streaming, "CHUNK_BYTES", chunk_bytes)

@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 CASES = []
 for cfg, variants in W.VARIANTS.items():
     for var in variants:
-        dtypes = ("f32", "bf16") if cfg == "c2" else ("f32",)
+        dtypes = W.LABELS[cfg]
         for dt in dtypes:
             for rows, cols in ((3, 5), (7, 33), (64, 1000), (40, 8192), (256, 256)):
                 CASES.append((cfg, var, dt, rows, cols))
