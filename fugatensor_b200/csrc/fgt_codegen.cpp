@@ -374,6 +374,7 @@ struct Emitter {
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
+  std::set<std::string> f32_sum_accs;       // f32 sum accumulators (arrays) whose two lanes may add as a pair
   const Domain& d;
   std::set<int64_t>* temps_loaded;
   std::vector<RedDef> fin_reds;
@@ -428,6 +429,7 @@ struct Emitter {
   }
 
   std::string fresh(const char* p) { return std::string(p) + std::to_string(uid++); }
+  bool pairs() const { return P.opt.lane_pairs && K.vec % 2 == 0; }
 
   void add(Sc s, const std::string& st) {
     switch (s.k) {
@@ -1092,6 +1094,7 @@ struct Emitter {
         rowsc[p].push_back(t.acc_t + " " + a + "_s[4] = {" + t.ident + ", " + t.ident + ", " + t.ident + ", " + t.ident +
                            "};");
         lane[p].push_back(comb_stmt(t, a + "_s[(c * " + std::to_string(K.vec) + " + v) & 3]", v));
+        if (t.acc_t == "float" && t.op == FGT_OP_REDUCE_SUM && !t.storage) f32_sum_accs.insert(a + "_s");
         post[p].push_back(comb_stmt(t, a + "_s[0]", a + "_s[1]"));
         post[p].push_back(comb_stmt(t, a + "_s[2]", a + "_s[3]"));
         post[p].push_back(comb_stmt(t, a + "_s[0]", a + "_s[2]"));
@@ -1145,6 +1148,7 @@ struct Emitter {
         lane[p].push_back("{ const fgt_i64 ix = " + ix + "; " + scan_stmt(t, a + "[c][v]", a + "i[c][v]", v, "ix") + " }");
       } else {
         lane[p].push_back(comb_stmt(t, a + "[c][v]", v));
+        if (t.acc_t == "float" && t.op == FGT_OP_REDUCE_SUM && !t.storage) f32_sum_accs.insert(a);
       }
       std::string slot = "(" + std::string(K.cluster > 1 ? "(fgt_i64)(blockIdx.x / " + std::to_string(K.cluster) + ")"
                                                           : "(fgt_i64)blockIdx.x") +
@@ -1306,9 +1310,15 @@ struct Emitter {
       o << ind << "    const fgt_i64 e0 = " << E0 << ";\n";
       o << ind << "    " << CHK << " {\n";
       put(o, chunkpre[p], ind + "      ");
-      o << ind << "      #pragma unroll\n" << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
-      o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
-      put(o, body, ind + "        ");
+      o << ind << "      #pragma unroll\n";
+      if (pairs()) {
+        o << ind << "      " << pair_header(VEC);
+        put(o, pair_body(body), ind + "        ");
+      } else {
+        o << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
+        o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+        put(o, body, ind + "        ");
+      }
       o << ind << "      }\n";
       put(o, chunkpost[p], ind + "      ");
       o << ind << "    }\n" << ind << "  }\n";
@@ -1472,9 +1482,15 @@ struct Emitter {
     o << "    #pragma unroll\n    for (int u = 0; u < " << UU << "; ++u) {\n";
     o << "      const fgt_i64 ch = base + u * stride;\n      if (ch < NCK) {\n        const fgt_i64 e0 = ch * " << VEC << ";\n";
     put(o, chunkpre[0], "        ");
-    o << "        #pragma unroll\n        for (int v = 0; v < " << VEC << "; ++v) {\n";
-    o << "          const fgt_i64 e = e0 + v; " << digits_i() << "\n";
-    put(o, lane[0], "          ");
+    o << "        #pragma unroll\n";
+    if (pairs()) {
+      o << "        " << pair_header(VEC);
+      put(o, pair_body(lane[0]), "          ");
+    } else {
+      o << "        for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << "          const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+      put(o, lane[0], "          ");
+    }
     o << "        }\n";
     put(o, chunkpost[0], "        ");
     o << "      }\n    }\n  }\n";
@@ -1620,6 +1636,177 @@ struct Emitter {
       out.push_back(s);
     }
     return out;
+  }
+
+  // ---- lane pairs: element loops step v by 2 and run each statement for
+  // lane v (slot a) and lane v + 1 (slot b). Slot b's statement is slot a's
+  // with the names the body declares, the element index e and the index
+  // digits i<k> renamed, and v read as (v + 1). f32 adds, multiplies, tracked
+  // divisions by a row constant and pairable accumulations issue as one
+  // f32x2 instruction for both slots (sm_100 FADD2 / FMUL2 / FFMA2: IEEE
+  // round-to-nearest per lane, subnormals kept); every other statement runs
+  // slot a, then slot b, so each accumulator sees its elements in order.
+  struct Tok {
+    std::string s;
+    bool ident;
+  };
+  static std::vector<Tok> tokens(const std::string& x) {
+    std::vector<Tok> out;
+    size_t i = 0;
+    while (i < x.size()) {
+      const char ch = x[i];
+      if (std::isalpha((unsigned char)ch) || ch == '_') {
+        size_t j = i + 1;
+        while (j < x.size() && (std::isalnum((unsigned char)x[j]) || x[j] == '_')) ++j;
+        out.push_back({x.substr(i, j - i), true});
+        i = j;
+      } else if (std::isdigit((unsigned char)ch)) {
+        size_t j = i + 1;
+        while (j < x.size() && (std::isalnum((unsigned char)x[j]) || x[j] == '_' || x[j] == '.')) ++j;
+        out.push_back({x.substr(i, j - i), false});
+        i = j;
+      } else {
+        out.push_back({std::string(1, ch), false});
+        ++i;
+      }
+    }
+    return out;
+  }
+  // top-level comma split of a call's argument text
+  static std::vector<std::string> split_args(const std::string& a) {
+    std::vector<std::string> out;
+    int depth = 0;
+    size_t st = 0;
+    for (size_t i = 0; i < a.size(); ++i) {
+      const char ch = a[i];
+      if (ch == '(' || ch == '[') ++depth;
+      else if (ch == ')' || ch == ']') --depth;
+      else if (ch == ',' && depth == 0) {
+        out.push_back(a.substr(st, i - st));
+        st = i + 1;
+      }
+    }
+    out.push_back(a.substr(st));
+    return out;
+  }
+  // `F(args)` -> args when x is exactly one call of F
+  static bool call_of(const std::string& x, const std::string& f, std::string* args) {
+    if (x.size() < f.size() + 2 || x.compare(0, f.size() + 1, f + "(") != 0 || x.back() != ')') return false;
+    int depth = 0;
+    for (size_t i = f.size(); i < x.size(); ++i) {
+      if (x[i] == '(') ++depth;
+      else if (x[i] == ')' && --depth == 0 && i + 1 != x.size()) return false;
+    }
+    *args = x.substr(f.size() + 1, x.size() - f.size() - 2);
+    return true;
+  }
+  std::vector<std::string> pair_body(const std::vector<std::string>& body) const {
+    std::set<std::string> renamed = {"e"};
+    for (size_t k = 0; k < d.id.size(); ++k) renamed.insert("i" + std::to_string(k));
+    for (const std::string& st : body) {
+      auto T = tokens(st);
+      for (size_t i = 1; i + 1 < T.size(); ++i) {
+        if (!T[i].ident) continue;
+        size_t n = i + 1;  // next non-space token: '=' but not '=='
+        while (n < T.size() && T[n].s == " ") ++n;
+        if (n >= T.size() || T[n].s != "=" || (n + 1 < T.size() && T[n + 1].s == "=")) continue;
+        size_t j = i;  // previous non-space token
+        while (j > 0 && T[j - 1].s == " ") --j;
+        if (j > 0 && T[j - 1].ident && T[j - 1].s != "else" && T[j - 1].s != "return") renamed.insert(T[i].s);
+      }
+    }
+    auto slot_b = [&](const std::string& st) {
+      std::string out;
+      for (auto& t : tokens(st)) {
+        if (t.ident && t.s == "v") out += "(v + 1)";
+        else if (t.ident && renamed.count(t.s)) out += t.s + "_b";
+        else out += t.s;
+      }
+      return out;
+    };
+    auto trim = [](std::string x) {
+      while (!x.empty() && x.front() == ' ') x.erase(x.begin());
+      while (!x.empty() && x.back() == ' ') x.pop_back();
+      return x;
+    };
+    std::vector<std::string> out;
+    for (const std::string& sa : body) {
+      const std::string sb = slot_b(sa);
+      const std::string a = trim(sa), b = trim(sb);
+      bool done = false;
+      // const float N = [round](F(x,y)); / const float N = fgt_div_q(x,D,Y);
+      static const std::string cf = "const float ";
+      const size_t eq = a.find(" = ");
+      if (a.compare(0, cf.size(), cf) == 0 && eq != std::string::npos && a.back() == ';' &&
+          a.find(';') == a.size() - 1) {
+        const std::string na = a.substr(cf.size(), eq - cf.size());
+        const std::string nb = b.substr(cf.size(), b.find(" = ") - cf.size());
+        std::string ea = a.substr(eq + 3, a.size() - eq - 4), eb = b.substr(b.find(" = ") + 3);
+        eb.pop_back();
+        std::string wrap, inner_a = ea, inner_b = eb, args;
+        for (const char* w : {"fgt_rnd_bf16", "fgt_rnd_f16"}) {
+          std::string ia, ib;
+          if (call_of(ea, w, &ia) && call_of(eb, w, &ib)) {
+            wrap = w;
+            inner_a = ia;
+            inner_b = ib;
+          }
+        }
+        const std::string pv = na + "_p2";
+        for (const char* f : {"__fadd_rn", "__fmul_rn"}) {
+          std::string aa, ab;
+          if (!call_of(inner_a, f, &aa) || !call_of(inner_b, f, &ab)) continue;
+          auto xa = split_args(aa), xb = split_args(ab);
+          if (xa.size() != 2 || xb.size() != 2) break;
+          const std::string f2 = std::string(f) == "__fadd_rn" ? "__fadd2_rn" : "__fmul2_rn";
+          auto rw = [&](const std::string& x) { return wrap.empty() ? x : wrap + "(" + x + ")"; };
+          out.push_back("const float2 " + pv + " = " + f2 + "(make_float2(" + xa[0] + ", " + xb[0] + "), make_float2(" +
+                        xa[1] + ", " + xb[1] + ")); const float " + na + " = " + rw(pv + ".x") + "; const float " + nb +
+                        " = " + rw(pv + ".y") + ";");
+          done = true;
+          break;
+        }
+        std::string da, db;
+        if (!done && wrap.empty() && call_of(ea, "fgt_div_q", &da) && call_of(eb, "fgt_div_q", &db)) {
+          auto xa = split_args(da), xb = split_args(db);
+          if (xa.size() == 3 && xb.size() == 3 && xa[1] == xb[1] && xa[2] == xb[2]) {
+            out.push_back("const float2 " + pv + " = fgt_div_q2(make_float2(" + xa[0] + ", " + xb[0] + "), " + xa[1] + ", " +
+                          xa[2] + "); const float " + na + " = " + pv + ".x; const float " + nb + " = " + pv + ".y;");
+            done = true;
+          }
+        }
+      }
+      // L = L + X; over a registered f32 sum accumulator with distinct slots
+      if (!done && eq != std::string::npos && a.back() == ';' && a.find(';') == a.size() - 1) {
+        const std::string la = a.substr(0, eq), lb = b.substr(0, b.find(" = "));
+        const std::string base = la.substr(0, la.find('['));
+        const std::string ra = a.substr(eq + 3, a.size() - eq - 4);
+        std::string rb = b.substr(b.find(" = ") + 3);
+        rb.pop_back();
+        if (f32_sum_accs.count(base) && la != lb && ra.compare(0, la.size() + 3, la + " + ") == 0 &&
+            rb.compare(0, lb.size() + 3, lb + " + ") == 0) {
+          const std::string xa = ra.substr(la.size() + 3), xb = rb.substr(lb.size() + 3);
+          out.push_back("{ const float2 s_ = __fadd2_rn(make_float2(" + la + ", " + lb + "), make_float2(" + xa + ", " + xb +
+                        ")); " + la + " = s_.x; " + lb + " = s_.y; }");
+          done = true;
+        }
+      }
+      if (!done) {
+        out.push_back(sa);
+        out.push_back(sb);
+      }
+    }
+    return out;
+  }
+  // loop header over lane pairs (slot b's element index and digits included)
+  std::string pair_header(const std::string& vec) {
+    std::string dg = digits_i(), db;
+    for (auto& t : tokens(dg)) db += (t.ident && (t.s == "e" || (t.s.size() > 1 && t.s[0] == 'i' &&
+                                                                   std::isdigit((unsigned char)t.s[1]))))
+                                        ? t.s + "_b"
+                                        : t.s;
+    return "for (int v = 0; v < " + vec + "; v += 2) {\n" + "const fgt_i64 e = e0 + v; " + dg + "\n" +
+           "const fgt_i64 e_b = e0 + v + 1; " + db + " (void)e_b;\n";
   }
 
   std::string build() {

@@ -144,6 +144,15 @@ FGT_DEV float fgt_div_q(float x, float d, float y) {
   const float r = __fmaf_rn(-q, d, x);
   return __fmaf_rn(r, y, q);
 }
+// fgt_div_q on two lanes at once (packed f32x2 multiply and FMAs; the same
+// IEEE operations per lane): x - q*d is formed as fma(q, -d, x), the same
+// exact value rounded once.
+FGT_DEV float2 fgt_div_q2(float2 x, float d, float y) {
+  const float2 yy = make_float2(y, y);
+  const float2 q = __fmul2_rn(x, yy);
+  const float2 r = __ffma2_rn(q, make_float2(-d, -d), x);
+  return __ffma2_rn(r, yy, q);
+}
 FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
   mx = fgt_fmax(mx, fabsf(q));
   mn = fminf(mn, fabsf(q));

@@ -1241,6 +1241,7 @@ struct Planner {
     if (rank_offsets) mix(opt.rank);
     mix(opt.row_elems);
     mix(opt.row_staging);
+    mix(opt.lane_pairs);
     mix(opt.ring_kb);
     mix(opt.row_cluster);
     char tag[16];

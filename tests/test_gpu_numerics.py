@@ -153,3 +153,56 @@ def test_bf16_row_max_min_packed_ieee():
     for got, want in zip((mx.numpy(), mn.numpy()), ref):
         nan = np.isnan(got) & np.isnan(want)
         assert not ((_bits(got) != _bits(want)) & ~nan).any(), (got[:8], want[:8])
+
+
+def _run_spec(desc, arrays, pairs):
+    import os
+    import torch
+    from fugatensor_b200 import _fgt
+    old = os.environ.get("FGT_LANE_PAIRS")
+    os.environ["FGT_LANE_PAIRS"] = "1" if pairs else "0"
+    try:
+        spec = _fgt.Spec(desc)
+    finally:
+        if old is None:
+            del os.environ["FGT_LANE_PAIRS"]
+        else:
+            os.environ["FGT_LANE_PAIRS"] = old
+    src = "".join(spec.kernel_source(i) for i in range(spec.kernel_count))
+    assert ("v += 2" in src) == pairs
+    dev = torch.device("cuda", 0)
+    outs = _fgt.run(spec, *[torch.from_numpy(a).to(dev) for a in arrays])
+    torch.cuda.synchronize()
+    return [o.cpu().numpy() for o in outs]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_lane_pairs_change_no_bit(dtype):
+    """Element loops run two lanes per f32x2 instruction (adds, multiplies, tracked
+    divisions, row and column sums). Every output equals the one-lane kernel's bit
+    for bit, and the elementwise results equal IEEE f32 (subnormals included)."""
+    from fugatensor_b200 import ir
+    rng = np.random.default_rng(11)
+    rows, cols = 64, 4096
+    a = _random_floats(rng, rows * cols, 1, 254).reshape(rows, cols)
+    b = _random_floats(rng, rows * cols, 1, 254).reshape(rows, cols)
+    a[0], b[0] = _random_floats(rng, cols, 0, 3), _random_floats(rng, cols, 0, 3)          # subnormal sums
+    a[1], b[1] = _random_floats(rng, cols, 1, 40), _random_floats(rng, cols, 60, 110)      # subnormal products
+    a[2, :6] = [0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45]
+    g = ir.Graph()
+    x, y = g.parameter(dtype, (rows, cols)), g.parameter(dtype, (rows, cols))
+    s, p = g.add(x, y), g.mul(x, y)
+    t = g.tanh(g.mul(x, g.filled(1e-30, dtype, (rows, cols))))
+    rs = g.reduce_sum(g.mul(t, t), (1,))
+    q = g.div(t, g.broadcast_in_dim(g.add(rs, g.filled(1.0, dtype, (rows,))), (rows, cols), (0,)))
+    cs = g.reduce_sum(g.add(q, t), (0,))
+    desc = g.descriptor([s, p, q, cs, rs])
+    arrays = [a, b] if dtype == "f32" else [O.f32_to_bf16_bits(a), O.f32_to_bf16_bits(b)]
+    paired, single = _run_spec(desc, arrays, True), _run_spec(desc, arrays, False)
+    for k, (u, w) in enumerate(zip(paired, single)):
+        assert np.array_equal(u.view(np.uint8), w.view(np.uint8)), f"output {k} differs between lane pairs and one lane"
+    if dtype == "f32":
+        with np.errstate(all="ignore"):
+            for got, ref in ((paired[0], a + b), (paired[1], a * b)):
+                both_nan = np.isnan(got) & np.isnan(ref)
+                assert not ((_bits(got) != _bits(ref)) & ~both_nan).any()
