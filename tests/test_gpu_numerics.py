@@ -171,9 +171,11 @@ def _run_spec(desc, arrays, pairs):
     src = "".join(spec.kernel_source(i) for i in range(spec.kernel_count))
     assert ("v += 2" in src) == pairs
     dev = torch.device("cuda", 0)
-    outs = _fgt.run(spec, *[torch.from_numpy(a).to(dev) for a in arrays])
+    ins = [torch.from_numpy(a.view(np.int16)).view(torch.bfloat16) if a.dtype == np.uint16 else torch.from_numpy(a)
+           for a in arrays]
+    outs = _fgt.run(spec, *[t.to(dev) for t in ins])
     torch.cuda.synchronize()
-    return [o.cpu().numpy() for o in outs]
+    return [(o.view(torch.int16) if o.dtype == torch.bfloat16 else o).cpu().numpy() for o in outs]
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
