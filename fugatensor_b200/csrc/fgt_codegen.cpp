@@ -392,6 +392,7 @@ struct Emitter {
     bool uniform;
     int bytes = 0;         // one thread's piece per chunk (VEC elements)
     bool staged = false;   // copied through the shared-memory stage ring
+    bool packed = false;   // 16-bit values two per 32-bit word ([NCH][VEC / 2] words)
     int64_t smem_off = 0;  // region of this operand in the ring
   };
   std::vector<RowSite> row_sites;
@@ -408,6 +409,7 @@ struct Emitter {
   }
   std::string site_load(const RowSite& rs, const std::string& arr, const char* rvar) {
     if (rs.uniform) return arr + "[c] = " + rs.ptr + "[" + itext(rs.addr, "e0", rvar) + "];";
+    if (rs.packed) return "fgt_vload(" + arr + "[c], (const fgt_u32*)(" + rs.ptr + " + " + itext(rs.addr, "e", rvar) + " + e0));";
     return "fgt_vload(" + arr + "[c], " + rs.ptr + " + " + itext(rs.addr, "e", rvar) + " + e0);";
   }
   std::vector<std::vector<std::string>> rowsc, lane, chunkpre, chunkpost, post;
@@ -430,6 +432,9 @@ struct Emitter {
 
   std::string fresh(const char* p) { return std::string(p) + std::to_string(uid++); }
   bool pairs() const { return P.opt.lane_pairs && K.vec % 2 == 0; }
+  // 16-bit operands held two per 32-bit register (element v of a chunk is
+  // half v % 2 of word v / 2): half the registers of one value per register
+  bool pack16(int dt) const { return P.opt.lane_pairs && K.vec % 2 == 0 && dtype_size(dt) == 2; }
 
   void add(Sc s, const std::string& st) {
     switch (s.k) {
@@ -558,13 +563,16 @@ struct Emitter {
       else {
         s = fresh("s");
         memo[key] = s;
-        const std::string vec = std::to_string(K.vec);
+        const bool pk = pack16(n.dt);
+        const std::string vec = std::to_string(pk ? K.vec / 2 : K.vec), SS = pk ? std::string("fgt_u32") : ST;
+        const std::string src = pk ? "(const fgt_u32*)(" + ptr + " + " + base + " + e0)" : ptr + " + " + base + " + e0";
         if (prol) {
-          prosites.push_back(ST + " " + s + "[" + vec + "]; fgt_vload_keep(" + s + ", " + ptr + " + " + base + " + e0);");
+          prosites.push_back(SS + " " + s + "[" + vec + "]; fgt_vload_keep(" + s + ", " + src + ");");
         } else if (cached) {
           Idx b = A;
           for (int k = 0; k < (int)d.id.size(); ++k) b.c[d.no() + k] = 0;
-          RowSite rs{s, ST, ptr, b, false};
+          RowSite rs{s, SS, ptr, b, false};
+          rs.packed = pk;
           rs.bytes = K.vec * dtype_size(n.dt);
           // cp.async moves 4, 8 or 16 bytes; a stage (one row of every staged
           // operand) must fit the ring budget.
@@ -574,16 +582,15 @@ struct Emitter {
           if (rs.staged) stage_bytes += piece;
           row_sites.push_back(rs);
         } else if (elem) {
-          eload.push_back("fgt_vload(" + s + "[u], " + ptr + " + " + base + " + e0);");
-          rowdecl.push_back(ST + " " + s + "[" + std::to_string(U) + "][" + vec + "];");
+          eload.push_back("fgt_vload(" + s + "[u], " + src + ");");
+          rowdecl.push_back(SS + " " + s + "[" + std::to_string(U) + "][" + vec + "];");
         } else {
-          chunkpre[D.p].push_back(ST + " " + s + "[" + vec + "]; fgt_vload(" + s + ", " + ptr + " + " + base + " + e0);");
+          chunkpre[D.p].push_back(SS + " " + s + "[" + vec + "]; fgt_vload(" + s + ", " + src + ");");
         }
       }
-      if (prol) return ld_conv(n.dt, s + "[v]");
-      if (cached) return ld_conv(n.dt, s + "[c][v]");
-      if (elem) return ld_conv(n.dt, s + "[u][v]");
-      return ld_conv(n.dt, s + "[v]");
+      const std::string arr = prol ? s : cached ? s + "[c]" : elem ? s + "[u]" : s;
+      if (pack16(n.dt)) return ld_conv(n.dt, "fgt_h16(" + arr + ", v)");
+      return ld_conv(n.dt, arr + "[v]");
     }
     if (uniform(A)) {
       std::string at = itext(A, "e0");
@@ -1061,13 +1068,14 @@ struct Emitter {
       {
         auto te = texpr.find(v);
         const std::string& ex = te == texpr.end() ? v : te->second;
-        static const std::string pre = "fgt_bf16_to_f32(", suf = "[c][v])";
+        const bool pk = pack16(FGT_BF16);
+        const std::string pre = pk ? "fgt_bf16_to_f32(fgt_h16(" : "fgt_bf16_to_f32(", suf = pk ? "[c], v))" : "[c][v])";
         if ((t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN) && t.fl && !t.storage && cached && K.vec % 2 == 0 &&
             ex.size() > pre.size() + suf.size() && ex.compare(0, pre.size(), pre) == 0 &&
             ex.compare(ex.size() - suf.size(), suf.size(), suf) == 0) {
           const std::string site = ex.substr(pre.size(), ex.size() - pre.size() - suf.size());
           for (auto& rs : row_sites)
-            if (rs.name == site && rs.st == "fgt_u16" && !rs.uniform) pk_site = site;
+            if (rs.name == site && rs.st == (pk ? "fgt_u32" : "fgt_u16") && !rs.uniform) pk_site = site;
         }
       }
       resets[p].push_back(a + " = " + t.ident + ";");
@@ -1251,7 +1259,8 @@ struct Emitter {
       });
     };
     for (auto& rs : row_sites) {
-      std::string dims = rs.uniform ? "[" + NCH + "]" : "[" + NCH + "][" + VEC + "]";
+      const std::string W = rs.packed ? std::to_string(K.vec / 2) : VEC;
+      std::string dims = rs.uniform ? "[" + NCH + "]" : "[" + NCH + "][" + W + "]";
       o << "  " << rs.st << " " << rs.name << dims << ";";
       if (!rs.staged) o << " " << rs.st << " " << rs.name << "_n" << dims << ";";
       o << "\n";
@@ -1350,7 +1359,7 @@ struct Emitter {
     put(o, rowend, "    ");
     for (auto* rs : reg_sites) {
       if (rs->uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) " << rs->name << "[c] = " << rs->name << "_n[c];\n";
-      else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << VEC << "; ++v) " << rs->name << "[c][v] = " << rs->name << "_n[c][v];\n";
+      else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << (rs->packed ? std::to_string(K.vec / 2) : VEC) << "; ++v) " << rs->name << "[c][v] = " << rs->name << "_n[c][v];\n";
     }
     if (stages) {
       // row i+1 -> registers; its stage refills with row i+1+S
@@ -1729,6 +1738,27 @@ struct Emitter {
       while (!x.empty() && x.back() == ' ') x.pop_back();
       return x;
     };
+    // negations N = (-X): an add of N pairs as a subtraction of X, written
+    // fma(X, -1, A) (X * -1 is exact, so this is A - X rounded once)
+    std::map<std::string, std::string> negs;
+    for (const std::string& st : body) {
+      const std::string a = trim(st);
+      static const std::string cf = "const float ";
+      const size_t eq = a.find(" = (-");
+      if (a.compare(0, cf.size(), cf) != 0 || eq == std::string::npos || a.size() < eq + 7 ||
+          a.compare(a.size() - 2, 2, ");") != 0)
+        continue;
+      const std::string n = a.substr(cf.size(), eq - cf.size()), x = a.substr(eq + 5, a.size() - eq - 7);
+      auto T = tokens(x);
+      if (T.size() == 1 && T[0].ident) negs[n] = x;
+    }
+    // "make_float2(A, B)" with the negated operands of both slots, when both are negations
+    auto neg_pair = [&](const std::string& a, const std::string& b, std::string* out) {
+      auto ia = negs.find(trim(a));
+      if (ia == negs.end()) return false;
+      *out = "make_float2(" + ia->second + ", " + slot_b(ia->second) + ")";
+      return trim(b) == slot_b(trim(a));
+    };
     std::vector<std::string> out;
     for (const std::string& sa : body) {
       const std::string sb = slot_b(sa);
@@ -1758,11 +1788,18 @@ struct Emitter {
           if (!call_of(inner_a, f, &aa) || !call_of(inner_b, f, &ab)) continue;
           auto xa = split_args(aa), xb = split_args(ab);
           if (xa.size() != 2 || xb.size() != 2) break;
-          const std::string f2 = std::string(f) == "__fadd_rn" ? "__fadd2_rn" : "__fmul2_rn";
+          const bool add = std::string(f) == "__fadd_rn";
           auto rw = [&](const std::string& x) { return wrap.empty() ? x : wrap + "(" + x + ")"; };
-          out.push_back("const float2 " + pv + " = " + f2 + "(make_float2(" + xa[0] + ", " + xb[0] + "), make_float2(" +
-                        xa[1] + ", " + xb[1] + ")); const float " + na + " = " + rw(pv + ".x") + "; const float " + nb +
-                        " = " + rw(pv + ".y") + ";");
+          std::string expr, nx;
+          if (add && neg_pair(xa[1], xb[1], &nx))
+            expr = "__ffma2_rn(" + nx + ", make_float2(-1.0f, -1.0f), make_float2(" + xa[0] + ", " + xb[0] + "))";
+          else if (add && neg_pair(xa[0], xb[0], &nx))
+            expr = "__ffma2_rn(" + nx + ", make_float2(-1.0f, -1.0f), make_float2(" + xa[1] + ", " + xb[1] + "))";
+          else
+            expr = std::string(add ? "__fadd2_rn" : "__fmul2_rn") + "(make_float2(" + xa[0] + ", " + xb[0] +
+                   "), make_float2(" + xa[1] + ", " + xb[1] + "))";
+          out.push_back("const float2 " + pv + " = " + expr + "; const float " + na + " = " + rw(pv + ".x") +
+                        "; const float " + nb + " = " + rw(pv + ".y") + ";");
           done = true;
           break;
         }
@@ -1786,8 +1823,11 @@ struct Emitter {
         if (f32_sum_accs.count(base) && la != lb && ra.compare(0, la.size() + 3, la + " + ") == 0 &&
             rb.compare(0, lb.size() + 3, lb + " + ") == 0) {
           const std::string xa = ra.substr(la.size() + 3), xb = rb.substr(lb.size() + 3);
-          out.push_back("{ const float2 s_ = __fadd2_rn(make_float2(" + la + ", " + lb + "), make_float2(" + xa + ", " + xb +
-                        ")); " + la + " = s_.x; " + lb + " = s_.y; }");
+          std::string nx;
+          const std::string sum = neg_pair(xa, xb, &nx)
+                                      ? "__ffma2_rn(" + nx + ", make_float2(-1.0f, -1.0f), make_float2(" + la + ", " + lb + "))"
+                                      : "__fadd2_rn(make_float2(" + la + ", " + lb + "), make_float2(" + xa + ", " + xb + "))";
+          out.push_back("{ const float2 s_ = " + sum + "; " + la + " = s_.x; " + lb + " = s_.y; }");
           done = true;
         }
       }

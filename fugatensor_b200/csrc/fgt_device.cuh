@@ -162,6 +162,20 @@ FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // Max / min of a packed accumulator with a register row piece of N bf16
 // values, two values per instruction (max.NaN / min.NaN on bf16x2: NaN wins,
 // exact otherwise). The halves are folded into the f32 accumulator later.
+// 16-bit element v of a packed row piece (two values per 32-bit word, the
+// lower index in the low half)
+template <int N> FGT_DEV fgt_u16 fgt_h16(const fgt_u32 (&w)[N], int v) { return (fgt_u16)(w[v >> 1] >> ((v & 1) * 16)); }
+// packed pieces are already bf16x2 words
+template <int N> FGT_DEV fgt_u32 fgt_max_bf16x2_row(fgt_u32 acc, const fgt_u32 (&w)[N]) {
+#pragma unroll
+  for (int k = 0; k < N; ++k) asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(acc) : "r"(acc), "r"(w[k]));
+  return acc;
+}
+template <int N> FGT_DEV fgt_u32 fgt_min_bf16x2_row(fgt_u32 acc, const fgt_u32 (&w)[N]) {
+#pragma unroll
+  for (int k = 0; k < N; ++k) asm("min.NaN.bf16x2 %0, %1, %2;" : "=r"(acc) : "r"(acc), "r"(w[k]));
+  return acc;
+}
 template <int N> FGT_DEV fgt_u32 fgt_max_bf16x2_row(fgt_u32 acc, const fgt_u16 (&h)[N]) {
   static_assert(N % 2 == 0, "pairs");
 #pragma unroll
