@@ -372,6 +372,7 @@ struct Emitter {
   std::map<std::string, std::string> texpr;  // temp -> its defining expression
   std::map<std::string, std::string> cse;    // (scope, type, expression) -> temp
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
+  std::set<int> exp_phases;                 // phases with element exps by fgt_exp_q (range noted)
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
   std::set<std::string> f32_sum_accs;       // f32 sum accumulators (arrays) whose two lanes may add as a pair
@@ -774,6 +775,15 @@ struct Emitter {
           expr = rnd(n.dt, "fgt_div_by(" + a[0] + "," + a[1] + "," + rcp + ")");
         }
       }
+    }
+    if (expr.empty() && n.op == FGT_OP_EXP && is_float(n.dt) && D.k == SC_LANE && row && cached && P.opt.own_exp) {
+      // e^x by fgt_exp_q with a note of |x|: the phase is redone with expf by
+      // any thread whose arguments left |x| <= 86 (or held a NaN / inf)
+      const std::string x = fresh("xe");
+      add(D, "const float " + x + " = @EXPQ@(" + a[0] + ");");
+      add(D, "@ENOTE@(" + a[0] + ");");
+      exp_phases.insert(D.p);
+      expr = rnd(n.dt, x);
     }
     if (!expr.empty()) {
     } else if (n.op == FGT_OP_CAST) expr = cast_expr(odt, n.dt, a[0]);
@@ -1340,15 +1350,21 @@ struct Emitter {
       // accumulators and redoes the phase with IEEE division. Redoing is
       // safe: the phase's other effects (cached values, element stores) are
       // overwritten with the same values.
-      const bool track = div_phases.count(p) && !col_phases.count(p) && cached;
-      const std::string dx = "dgx" + std::to_string(p), dn = "dgn" + std::to_string(p);
-      if (track) o << "    float " << dx << " = 0.0f, " << dn << " = __int_as_float(0x7f800000);\n";
+      // Exps of such a phase by fgt_exp_q note max |x| the same way, and the
+      // redo computes them with expf.
+      const bool track = (div_phases.count(p) || exp_phases.count(p)) && !col_phases.count(p) && cached;
+      const std::string dx = "dgx" + std::to_string(p), dn = "dgn" + std::to_string(p), de = "dge" + std::to_string(p);
+      if (track)
+        o << "    float " << dx << " = 0.0f, " << dn << " = __int_as_float(0x7f800000), " << de << " = 0.0f;\n";
       o << "    if (rv) {\n";
-      phase_loop(p, div_form(lane[p], track ? "fgt_div_q" : "fgt_div_by", track ? "fgt_div_note(" + dx + ", " + dn + ", " : ""),
+      phase_loop(p,
+                 track ? div_form(lane[p], "fgt_div_q", "fgt_div_note(" + dx + ", " + dn + ", ", "fgt_exp_q",
+                                  "fgt_exp_note(" + de + ", ")
+                       : div_form(lane[p], "fgt_div_by", ""),
                  "    ");
       o << "    }\n";
       if (track) {
-        o << "    if (rv && !fgt_div_ok(" << dx << ", " << dn << ")) {\n";
+        o << "    if (rv && !(fgt_div_ok(" << dx << ", " << dn << ") && fgt_exp_ok(" << de << "))) {\n";
         put(o, resets[p], "      ");
         phase_loop(p, div_form(lane[p], "fgt_div_ieee", ""), "    ");
         o << "    }\n";
@@ -1633,7 +1649,8 @@ struct Emitter {
   // `fn`, and the @NOTE@(q) statements become `note` + "q);" (dropped when
   // note is empty).
   static std::vector<std::string> div_form(const std::vector<std::string>& v, const std::string& fn,
-                                           const std::string& note) {
+                                           const std::string& note, const std::string& efn = "expf",
+                                           const std::string& enote = "") {
     std::vector<std::string> out;
     for (const std::string& s0 : v) {
       std::string s = s0;
@@ -1641,7 +1658,12 @@ struct Emitter {
         if (!note.empty()) out.push_back(note + s.substr(7));
         continue;
       }
+      if (s.compare(0, 8, "@ENOTE@(") == 0) {
+        if (!enote.empty()) out.push_back(enote + s.substr(8));
+        continue;
+      }
       for (size_t at; (at = s.find("@DIVQ@")) != std::string::npos;) s.replace(at, 6, fn);
+      for (size_t at; (at = s.find("@EXPQ@")) != std::string::npos;) s.replace(at, 6, efn);
       out.push_back(s);
     }
     return out;
@@ -1804,6 +1826,12 @@ struct Emitter {
           break;
         }
         std::string da, db;
+        if (!done && wrap.empty() && call_of(ea, "fgt_exp_q", &da) && call_of(eb, "fgt_exp_q", &db) &&
+            split_args(da).size() == 1) {
+          out.push_back("const float2 " + pv + " = fgt_exp_q2(make_float2(" + da + ", " + db + ")); const float " + na + " = " +
+                        pv + ".x; const float " + nb + " = " + pv + ".y;");
+          done = true;
+        }
         if (!done && wrap.empty() && call_of(ea, "fgt_div_q", &da) && call_of(eb, "fgt_div_q", &db)) {
           auto xa = split_args(da), xb = split_args(db);
           if (xa.size() == 3 && xb.size() == 3 && xa[1] == xb[1] && xa[2] == xb[2]) {
@@ -1856,8 +1884,9 @@ struct Emitter {
     std::ostringstream out;
     for (std::string line; std::getline(in, line);) {
       const size_t k = line.find_first_not_of(' ');
-      if (k != std::string::npos && line.compare(k, 7, "@NOTE@(") == 0) continue;
+      if (k != std::string::npos && (line.compare(k, 7, "@NOTE@(") == 0 || line.compare(k, 8, "@ENOTE@(") == 0)) continue;
       for (size_t at; (at = line.find("@DIVQ@")) != std::string::npos;) line.replace(at, 6, "fgt_div_by");
+      for (size_t at; (at = line.find("@EXPQ@")) != std::string::npos;) line.replace(at, 6, "expf");
       out << line << "\n";
     }
     return out.str();

@@ -153,6 +153,35 @@ FGT_DEV float2 fgt_div_q2(float2 x, float d, float y) {
   const float2 r = __ffma2_rn(q, make_float2(-d, -d), x);
   return __ffma2_rn(r, yy, q);
 }
+// e^x for |x| <= 86 (phases note max |x| and redo with expf past it, or for
+// a NaN / inf argument). x log2(e) = n + f with n the nearest integer (the
+// product rounded at unit precision by adding 1.5 * 2^23) and f from the
+// two-constant product x * (L2E + L2E_LO) - n (Cody & Waite's splitting, the
+// error of f below 2^-24); 2^f in [2^-1/2, 2^1/2] by ex2.approx, and 2^n added
+// to its exponent field: the low bits of t are n (t = 1.5 * 2^23 + n), so
+// (bits(t) << 23) is n << 23 modulo 2^32 and the result stays normal.
+// Error within about 2 ulp of e^x (the approximation of 2^f dominates).
+FGT_DEV float fgt_ex2_approx(float f) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(f));
+  return r;
+}
+FGT_DEV float fgt_exp_q(float x) {
+  const float t = __fmaf_rn(x, __int_as_float(0x3fb8aa3b), __int_as_float(0x4b400000));
+  const float nn = __fsub_rn(__int_as_float(0x4b400000), t);  // -n, exact
+  const float f = __fmaf_rn(x, __int_as_float(0x32a57060), __fmaf_rn(x, __int_as_float(0x3fb8aa3b), nn));
+  return __int_as_float(__float_as_int(fgt_ex2_approx(f)) + (__float_as_int(t) << 23));
+}
+FGT_DEV float2 fgt_exp_q2(float2 x) {
+  const float2 t = __ffma2_rn(x, make_float2(__int_as_float(0x3fb8aa3b), __int_as_float(0x3fb8aa3b)), make_float2(__int_as_float(0x4b400000), __int_as_float(0x4b400000)));
+  const float2 nn = __ffma2_rn(t, make_float2(-1.0f, -1.0f), make_float2(__int_as_float(0x4b400000), __int_as_float(0x4b400000)));
+  const float2 f1 = __ffma2_rn(x, make_float2(__int_as_float(0x3fb8aa3b), __int_as_float(0x3fb8aa3b)), nn);
+  const float2 f = __ffma2_rn(x, make_float2(__int_as_float(0x32a57060), __int_as_float(0x32a57060)), f1);
+  return make_float2(__int_as_float(__float_as_int(fgt_ex2_approx(f.x)) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(fgt_ex2_approx(f.y)) + (__float_as_int(t.y) << 23)));
+}
+FGT_DEV void fgt_exp_note(float& mx, float x) { mx = fgt_fmax(mx, fabsf(x)); }
+FGT_DEV bool fgt_exp_ok(float mx) { return mx <= 86.0f; }
 FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
   mx = fgt_fmax(mx, fabsf(q));
   mn = fminf(mn, fabsf(q));

@@ -1242,6 +1242,7 @@ struct Planner {
     mix(opt.row_elems);
     mix(opt.row_staging);
     mix(opt.lane_pairs);
+    mix(opt.own_exp);
     mix(opt.ring_kb);
     mix(opt.row_cluster);
     char tag[16];

@@ -208,3 +208,33 @@ def test_lane_pairs_change_no_bit(dtype):
             for got, ref in ((paired[0], a + b), (paired[1], a * b)):
                 both_nan = np.isnan(got) & np.isnan(ref)
                 assert not ((_bits(got) != _bits(ref)) & ~both_nan).any()
+
+
+def test_row_phase_exp_within_two_ulp():
+    """exp inside a redoable row phase runs as fgt_exp_q (2^f by ex2.approx,
+    2^n in the exponent field) and falls back to expf for the rows whose
+    arguments leave |x| <= 86 or hold NaN / inf: every normal result is within
+    2 ulp of e^x and the special values match."""
+    from fugatensor_b200 import ir
+    rng = np.random.default_rng(21)
+    rows, cols = 96, 4096
+    x = rng.uniform(-86, 86, (rows, cols)).astype(np.float32)
+    x[1] = rng.uniform(-1e-3, 1e-3, cols)
+    x[2] = np.linspace(-1, 1, cols, dtype=np.float32)
+    x[3, :8] = [np.nan, np.inf, -np.inf, 88.5, 89.0, -87.5, -100.0, -200.0]
+    x[4, :2] = [86.5, -86.5]
+    g = ir.Graph()
+    xv = g.parameter("f32", (rows, cols))
+    e = g.exp(xv)
+    desc = g.descriptor([e, g.reduce_sum(e, (1,))])
+    got = _run_spec(desc, [x], True)[0].astype(np.float64)
+    with np.errstate(all="ignore"):
+        ref = np.exp(x.astype(np.float64))
+    ref32 = ref.astype(np.float32)
+    normal = np.isfinite(ref32) & (np.abs(ref32) >= np.finfo(np.float32).tiny)
+    ulp = np.abs(got[normal] - ref[normal]) / np.spacing(ref32[normal]).astype(np.float64)
+    assert ulp.max() <= 2.0, f"max {ulp.max():.2f} ulp"
+    assert np.array_equal(np.isnan(got), np.isnan(ref32))
+    assert np.array_equal(np.isinf(got), np.isinf(ref32))
+    tiny = np.isfinite(ref32) & ~normal  # zero and subnormal results
+    assert np.all(np.abs(got[tiny] - ref[tiny]) <= 2 * 2.0 ** -149)
