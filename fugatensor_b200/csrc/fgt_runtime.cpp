@@ -456,6 +456,8 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       require(options->row_cluster >= 0 && options->row_cluster <= 8 && (options->row_cluster & (options->row_cluster - 1)) == 0,
               "row_cluster must be 0 or a power of two up to 8");
       if (options->row_cluster > 0) opt.row_cluster = options->row_cluster;
+      require(options->occupancy_step == 0 || options->occupancy_step == 1, "occupancy_step must be 0 or 1");
+      opt.occupancy_step = options->occupancy_step;
     }
     // FGT_ROW_STAGING=0 keeps streamed row operands in registers
     // (double-buffered) instead of the shared-memory ring.
@@ -488,6 +490,30 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
           f << k.source;
         }
         Compiled c = compile_cubin(k.name, std::string(fgt_device_library_source) + "\n" + k.source, dir);
+        // Occupancy step: registers are allocated per thread in steps of 8,
+        // so a block-per-row kernel a little above a CTA-count boundary (say
+        // 79 registers at 256 threads: 3 CTAs per SM) is compiled again bounded
+        // to one more CTA per SM (64 registers: 4) when that bound is within
+        // 70% of its registers and the ring still fits; kept with at most 256
+        // bytes of spills (the option is a tuning candidate: the tuner times
+        // it against the unbounded kernel).
+        if (o.occupancy_step && k.kind == KKind::ROW && c.regs > 0 && c.spill_bytes == 0) {
+          const int64_t per = ((c.regs + 7) / 8) * 8 * (int64_t)k.nt;
+          const int64_t ctas = 65536 / per, max_ctas = 2048 / k.nt;
+          const int64_t target = ctas + 1, cap = (65536 / (target * k.nt)) / 8 * 8;
+          const std::string lb = "__launch_bounds__(" + std::to_string(k.nt) + ")";
+          const size_t at = k.source.find(lb);
+          if (ctas >= 1 && target <= max_ctas && cap >= 32 && cap * 10 >= (int64_t)c.regs * 7 &&
+              k.smem_bytes * target <= 227 * 1024 && at != std::string::npos) {
+            std::string src = k.source;
+            src.replace(at, lb.size(), "__launch_bounds__(" + std::to_string(k.nt) + ", " + std::to_string(target) + ")");
+            Compiled b = compile_cubin(k.name, std::string(fgt_device_library_source) + "\n" + src, dir);
+            if (b.spill_bytes >= 0 && b.spill_bytes <= 256 && b.regs > 0 && b.regs <= cap) {
+              k.source = src;
+              c = std::move(b);
+            }
+          }
+        }
         k.regs = c.regs;
         k.spill_bytes = c.spill_bytes;
         cubins->push_back(std::move(c.cubin));

@@ -80,11 +80,11 @@ def _chunk_count(R, row_bytes, chunk_bytes):
 class RowStream:
     """Chunk specs of one partition (cached per engine)."""
 
-    def __init__(self, desc, rows, split, chunks, accumulation, geometry=(0, 0, 0)):
+    def __init__(self, desc, rows, split, chunks, accumulation, geometry=(0, 0, 0, 0)):
         self.rows, self.split, self.chunks = rows, split, chunks
-        e, r, c = tuple(geometry) + (0,) * (3 - len(geometry))
+        e, r, c, o = tuple(geometry) + (0,) * (4 - len(geometry))
         mk = lambda k: _fgt.Spec(desc, accumulation=accumulation, world=chunks, rank=k, shard_inputs=split,
-                                 row_elems=e, ring_kb=r, row_cluster=c)
+                                 row_elems=e, ring_kb=r, row_cluster=c, occupancy_step=o)
         first, second = mk(0), mk(1)
         names = lambda s: [k["name"] for k in s.execution_plan["cuda_lowering"]["kernels"]]
         if names(first) == names(second):
@@ -109,7 +109,7 @@ def plan(engine, desc, leaves, roots):
             # partition, so streamed results equal evaluate()'s bit for bit
             # (the geometry fixes each row's summation order). Partitions too
             # large to measure on the device keep the default geometry.
-            geometry = (0, 0, 0)
+            geometry = (0, 0, 0, 0)
             if _moved_bytes(desc) <= WHOLE_LIMIT:
                 geometry = engine._spec(desc).geometry
             rs = RowStream(desc, R, split, chunks, engine.accumulation, geometry) if chunks else None

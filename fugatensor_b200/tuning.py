@@ -27,11 +27,15 @@ from pathlib import Path
 
 from . import _fgt, ir
 
-# (elements per thread per row operand, shared-memory ring KB, CTAs per row); (0, 0, 0) is the
-# library default. Rows split over a cluster (third field 2) measured slower on every benchmark
-# partition (half-size CTAs give no more warps per SM, and each phase adds a cluster barrier), so
-# they are not candidates; the option stays available through the spec options.
-CANDIDATES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
+# (elements per thread per row operand, shared-memory ring KB, CTAs per row, occupancy step);
+# (0, 0, 0, 0) is the library default. Rows split over a cluster (third field 2) measured slower on
+# every benchmark partition (half-size CTAs give no more warps per SM, and each phase adds a
+# cluster barrier), so they are not candidates; the option stays available through the spec
+# options. The occupancy step (fourth field 1) bounds a kernel's registers to fit one more CTA per
+# SM when it is close (the bf16 softmax forward: 79 -> 64 registers, 3 -> 4 CTAs); candidates it
+# leaves unchanged compile to the same source and are timed once.
+_GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
+CANDIDATES = tuple(g + (o,) for o in (0, 1) for g in _GEOMETRIES)
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 _lock = threading.Lock()
 
@@ -120,22 +124,23 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     path = _db_path(cache_dir)
     hit = _load(path).get(key)
     if hit is not None:
-        geom = tuple(hit["geometry"]) + (0,) * (3 - len(hit["geometry"]))
-        if geom == (0, 0, 0):
+        geom = tuple(hit["geometry"]) + (0,) * (4 - len(hit["geometry"]))
+        if geom == (0, 0, 0, 0):
             return default
-        e, r, c = geom
-        return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r, row_cluster=c)
+        e, r, c, o = geom
+        return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r, row_cluster=c,
+                         occupancy_step=o)
     specs, seen = [], {}
-    for e, r, c in CANDIDATES:
-        s = default if (e, r, c) == (0, 0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
-                                                             row_elems=e, ring_kb=r, row_cluster=c)
+    for e, r, c, o in CANDIDATES:
+        s = default if (e, r, c, o) == (0, 0, 0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
+                                                                   row_elems=e, ring_kb=r, row_cluster=c, occupancy_step=o)
         src = tuple(s.kernel_source(i) for i in range(s.kernel_count))
         if src in seen:
             continue
         seen[src] = True
-        specs.append(((e, r, c), s))
+        specs.append(((e, r, c, o), s))
     if len(specs) == 1:
-        _store(path, key, {"geometry": [0, 0, 0], "ms": None})
+        _store(path, key, {"geometry": [0, 0, 0, 0], "ms": None})
         return default
     gen = torch.Generator(device=dev).manual_seed(0)
     with torch.cuda.device(dev):

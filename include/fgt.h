@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FGT_ABI_VERSION 3
+#define FGT_ABI_VERSION 4
 #define FGT_MAX_RANK 8
 #define FGT_MAX_OPERANDS 3
 #define FGT_MAX_ATTRS 24
@@ -145,6 +145,10 @@ typedef struct fgt_spec_options {
                               /* KB (0: the library's choice, 96)                      */
   int32_t row_cluster;        /* block-per-row kernels: CTAs of a thread-block cluster */
                               /* sharing each row (0/1: none; 2, 4, 8)                 */
+  int32_t occupancy_step;     /* block-per-row kernels: 1 = a kernel whose registers   */
+                              /* are within reach of one more resident CTA per SM is   */
+                              /* compiled bounded to that many (kept when it spills at */
+                              /* most 256 bytes); 0 = the compiler's register choice   */
 } fgt_spec_options;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
