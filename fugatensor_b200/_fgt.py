@@ -48,7 +48,7 @@ lib = ctypes.CDLL(str(LIB_PATH))
 class SpecOptions(ctypes.Structure):
     _fields_ = [("accumulation", ctypes.c_int32), ("shard_world", ctypes.c_int32), ("shard_rank", ctypes.c_int32),
                 ("row_elems", ctypes.c_int32), ("shard_inputs", ctypes.c_uint64), ("cache_dir", ctypes.c_char_p),
-                ("ring_kb", ctypes.c_int32), ("row_cluster", ctypes.c_int32), ("occupancy_step", ctypes.c_int32)]
+                ("ring_kb", ctypes.c_int32), ("row_cluster", ctypes.c_int32), ("row_flags", ctypes.c_int32)]
 
 
 class SpecInfo(ctypes.Structure):
@@ -100,9 +100,9 @@ class Spec:
     """A planned, compiled partition (owns an fgt_spec*)."""
 
     def __init__(self, descriptor: ir.Descriptor, *, accumulation="wide", world=1, rank=0, shard_inputs=(),
-                 cache_dir=None, row_elems=0, ring_kb=0, row_cluster=0, occupancy_step=0):
+                 cache_dir=None, row_elems=0, ring_kb=0, row_cluster=0, row_flags=0):
         self.descriptor = descriptor
-        self.geometry = (row_elems, ring_kb, row_cluster, occupancy_step)
+        self.geometry = (row_elems, ring_kb, row_cluster, row_flags)
         opts = SpecOptions()
         opts.accumulation = ACCUMULATION[accumulation]
         opts.shard_world = world
@@ -110,7 +110,7 @@ class Spec:
         opts.row_elems = row_elems
         opts.ring_kb = ring_kb
         opts.row_cluster = row_cluster
-        opts.occupancy_step = occupancy_step
+        opts.row_flags = row_flags
         mask = 0
         for i in shard_inputs:
             mask |= 1 << i

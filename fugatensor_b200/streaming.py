@@ -84,7 +84,7 @@ class RowStream:
         self.rows, self.split, self.chunks = rows, split, chunks
         e, r, c, o = tuple(geometry) + (0,) * (4 - len(geometry))
         mk = lambda k: _fgt.Spec(desc, accumulation=accumulation, world=chunks, rank=k, shard_inputs=split,
-                                 row_elems=e, ring_kb=r, row_cluster=c, occupancy_step=o)
+                                 row_elems=e, ring_kb=r, row_cluster=c, row_flags=o)
         first, second = mk(0), mk(1)
         names = lambda s: [k["name"] for k in s.execution_plan["cuda_lowering"]["kernels"]]
         if names(first) == names(second):

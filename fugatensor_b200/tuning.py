@@ -27,15 +27,16 @@ from pathlib import Path
 
 from . import _fgt, ir
 
-# (elements per thread per row operand, shared-memory ring KB, CTAs per row, occupancy step);
+# (elements per thread per row operand, shared-memory ring KB, CTAs per row, row flags);
 # (0, 0, 0, 0) is the library default. Rows split over a cluster (third field 2) measured slower on
 # every benchmark partition (half-size CTAs give no more warps per SM, and each phase adds a
 # cluster barrier), so they are not candidates; the option stays available through the spec
-# options. The occupancy step (fourth field 1) bounds a kernel's registers to fit one more CTA per
-# SM when it is close (the bf16 softmax forward: 79 -> 64 registers, 3 -> 4 CTAs); candidates it
-# leaves unchanged compile to the same source and are timed once.
+# options. Row flags (fgt_row_flag): 1 bounds a kernel's registers to fit one more CTA per SM
+# when it is close; 2 computes exp with CUDA's expf instead of the library's exp, whose extra
+# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers).
+# Candidates a flag leaves unchanged compile to the same source and are timed once.
 _GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
-CANDIDATES = tuple(g + (o,) for o in (0, 1) for g in _GEOMETRIES)
+CANDIDATES = tuple(g + (f,) for f in (0, 1, 2) for g in _GEOMETRIES)
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 _lock = threading.Lock()
 
@@ -129,11 +130,11 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
             return default
         e, r, c, o = geom
         return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r, row_cluster=c,
-                         occupancy_step=o)
+                         row_flags=o)
     specs, seen = [], {}
     for e, r, c, o in CANDIDATES:
         s = default if (e, r, c, o) == (0, 0, 0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
-                                                                   row_elems=e, ring_kb=r, row_cluster=c, occupancy_step=o)
+                                                                   row_elems=e, ring_kb=r, row_cluster=c, row_flags=o)
         src = tuple(s.kernel_source(i) for i in range(s.kernel_count))
         if src in seen:
             continue

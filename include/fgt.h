@@ -145,11 +145,17 @@ typedef struct fgt_spec_options {
                               /* KB (0: the library's choice, 96)                      */
   int32_t row_cluster;        /* block-per-row kernels: CTAs of a thread-block cluster */
                               /* sharing each row (0/1: none; 2, 4, 8)                 */
-  int32_t occupancy_step;     /* block-per-row kernels: 1 = a kernel whose registers   */
-                              /* are within reach of one more resident CTA per SM is   */
-                              /* compiled bounded to that many (kept when it spills at */
-                              /* most 256 bytes); 0 = the compiler's register choice   */
+  int32_t row_flags;          /* block-per-row kernels, fgt_row_flag bits (0: none)    */
 } fgt_spec_options;
+
+typedef enum fgt_row_flag {
+  /* a kernel whose registers are within reach of one more resident CTA per SM
+   * is compiled bounded to that many (kept when it spills at most 256 bytes) */
+  FGT_ROW_OCCUPANCY_STEP = 1,
+  /* exp computed by CUDA's expf everywhere, instead of the library's exp
+   * (2^f by ex2.approx, 2^n in the exponent field) in redoable row phases */
+  FGT_ROW_EXPF = 2
+} fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
 typedef struct fgt_comm fgt_comm;   /* opaque: one rank of an NCCL communicator   */
