@@ -506,9 +506,15 @@ def run_only(args):
     rows, cols = W.FULL[cfg]
     rows = args.rows or rows
     device = torch.device("cuda", 0)
-    engine = ft.Engine("cuda:0")
+    # --geometry e,r,c,f: that row geometry (no measured choice), so a capture
+    # sees no tuning launches before the partition's own
+    engine = ft.Engine("cuda:0", tune=args.geometry is None)
     tens = device_inputs(cfg, rows, cols, dtype, device)
     spec, ins = compile_partition(engine, cfg, variant, rows, cols, dtype, tens)
+    if args.geometry:
+        from fugatensor_b200 import _fgt
+        e, r, c, f = (int(x) for x in args.geometry.split(","))
+        spec = _fgt.Spec(spec.descriptor, row_elems=e, ring_kb=r, row_cluster=c, row_flags=f)
     L = Launcher(spec, ins, device)
     stream = torch.cuda.current_stream(device)
     for _ in range(args.iters):
@@ -523,6 +529,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None, help="cfg/variant/dtype: launch one partition (profiling)")
     ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--geometry", default=None, help="with --only: row geometry e,r,c,f (elements, ring KB, cluster, flags)")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
