@@ -896,7 +896,7 @@ struct Emitter {
     out.push_back("}");
     if (!cross_warp) return;
     for (auto& [t, a] : accs) {
-      kdecl.push_back("__shared__ " + t.acc_t + " sm_" + a + tag + PD + "[" + std::to_string(NW) + "];");
+      kdecl.push_back("__shared__ __align__(16) " + t.acc_t + " sm_" + a + tag + PD + "[" + std::to_string(NW) + "];");
       if (t.arg) kdecl.push_back("__shared__ fgt_i64 smi_" + a + tag + PD + "[" + std::to_string(NW) + "];");
     }
     out.push_back("if ((tid & 31) == 0) {");
@@ -908,21 +908,41 @@ struct Emitter {
     out.push_back("__syncthreads();");
     if (butterfly && NW > 1 && (NW & (NW - 1)) == 0 && NW <= 32) {
       const std::string mask = std::to_string(NW - 1);
+      bool any_arg = false;
       for (auto& [t, a] : accs) {
-        out.push_back(a + " = sm_" + a + tag + PB + "[tid & " + mask + "];");
-        if (t.arg) out.push_back(a + "i = smi_" + a + tag + PB + "[tid & " + mask + "];");
-      }
-      out.push_back("#pragma unroll");
-      out.push_back("for (int m_ = 1; m_ < " + std::to_string(NW) + "; m_ <<= 1) {");
-      for (auto& [t, a] : accs) {
-        if (t.arg) {
-          out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); const fgt_i64 oi = fgt_shfl_xor(" + a +
-                        "i, m_); " + arg_stmt(t, a, a + "i", "ov", "oi") + " }");
+        if (!t.arg) {
+          // Every thread reads the NW warp partials (broadcast loads) and
+          // folds them in the pairwise tree the butterfly forms, which is
+          // the same value bit for bit, without its dependent shuffles.
+          const std::string sm = "sm_" + a + tag + PB;
+          std::vector<std::string> lv;
+          for (int w = 0; w < NW; ++w) lv.push_back(sm + "[" + std::to_string(w) + "]");
+          for (int lvl = 0; lv.size() > 1; ++lvl) {
+            std::vector<std::string> nx;
+            for (size_t i = 0; i + 1 < lv.size(); i += 2) {
+              const std::string tv = a + tag + "_t" + std::to_string(lvl) + "_" + std::to_string(i / 2);
+              out.push_back(t.acc_t + " " + tv + " = " + lv[i] + "; " + comb_stmt(t, tv, lv[i + 1]));
+              nx.push_back(tv);
+            }
+            lv = nx;
+          }
+          out.push_back(a + " = " + lv[0] + ";");
         } else {
-          out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); " + comb_stmt(t, a, "ov") + " }");
+          any_arg = true;
+          out.push_back(a + " = sm_" + a + tag + PB + "[tid & " + mask + "];");
+          out.push_back(a + "i = smi_" + a + tag + PB + "[tid & " + mask + "];");
         }
       }
-      out.push_back("}");
+      if (any_arg) {
+        out.push_back("#pragma unroll");
+        out.push_back("for (int m_ = 1; m_ < " + std::to_string(NW) + "; m_ <<= 1) {");
+        for (auto& [t, a] : accs) {
+          if (!t.arg) continue;
+          out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); const fgt_i64 oi = fgt_shfl_xor(" + a +
+                        "i, m_); " + arg_stmt(t, a, a + "i", "ov", "oi") + " }");
+        }
+        out.push_back("}");
+      }
       cluster_exchange(out, accs, tag);
       if (trailing_sync) out.push_back("__syncthreads();");
       return;
