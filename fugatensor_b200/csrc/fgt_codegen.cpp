@@ -883,9 +883,19 @@ struct Emitter {
     const std::string PB = parity ? "[it_ & 1]" : "";
     const std::string PD = parity ? "[2]" : "";
     if (accs.empty()) return;
-    out.push_back("#pragma unroll");
-    out.push_back("for (int m_ = 1; m_ < " + std::to_string(TW) + "; m_ <<= 1) {");
+    // f32 max / min over a whole warp: one redux.sync instead of the butterfly
+    auto redux = [&](const RedText& t) {
+      return TW == 32 && !t.arg && t.acc_t == "float" && (t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN);
+    };
+    bool any_shfl = false;
     for (auto& [t, a] : accs) {
+      if (redux(t)) out.push_back(a + " = fgt_redux_" + std::string(t.op == FGT_OP_REDUCE_MAX ? "max" : "min") + "(" + a + ");");
+      else any_shfl = true;
+    }
+    if (any_shfl) out.push_back("#pragma unroll");
+    if (any_shfl) out.push_back("for (int m_ = 1; m_ < " + std::to_string(TW) + "; m_ <<= 1) {");
+    for (auto& [t, a] : accs) {
+      if (redux(t)) continue;
       if (t.arg) {
         out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); const fgt_i64 oi = fgt_shfl_xor(" + a +
                       "i, m_); " + arg_stmt(t, a, a + "i", "ov", "oi") + " }");
@@ -893,7 +903,7 @@ struct Emitter {
         out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); " + comb_stmt(t, a, "ov") + " }");
       }
     }
-    out.push_back("}");
+    if (any_shfl) out.push_back("}");
     if (!cross_warp) return;
     for (auto& [t, a] : accs) {
       kdecl.push_back("__shared__ __align__(16) " + t.acc_t + " sm_" + a + tag + PD + "[" + std::to_string(NW) + "];");

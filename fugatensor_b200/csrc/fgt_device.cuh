@@ -180,6 +180,19 @@ FGT_DEV float2 fgt_exp_q2(float2 x) {
   return make_float2(__int_as_float(__float_as_int(fgt_ex2_approx(f.x)) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(fgt_ex2_approx(f.y)) + (__float_as_int(t.y) << 23)));
 }
+// Warp-wide f32 max / min in one instruction (sm_100a redux.sync with .NaN:
+// a NaN input gives NaN), the same IEEE maximum / minimum as fgt_fmax /
+// fgt_fmin over the warp's 32 values.
+FGT_DEV float fgt_redux_max(float x) {
+  float r;
+  asm("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+  return r;
+}
+FGT_DEV float fgt_redux_min(float x) {
+  float r;
+  asm("redux.sync.min.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+  return r;
+}
 FGT_DEV void fgt_exp_note(float& mx, float x) { mx = fgt_fmax(mx, fabsf(x)); }
 FGT_DEV bool fgt_exp_ok(float mx) { return mx <= 86.0f; }
 FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {

@@ -238,3 +238,28 @@ def test_row_phase_exp_within_two_ulp():
     assert np.array_equal(np.isinf(got), np.isinf(ref32))
     tiny = np.isfinite(ref32) & ~normal  # zero and subnormal results
     assert np.all(np.abs(got[tiny] - ref[tiny]) <= 2 * 2.0 ** -149)
+
+
+@pytest.mark.parametrize("cols", [1024, 64])
+def test_row_max_min_signed_zeros_and_nan(cols):
+    """Row max / min combine warps with redux.sync (rows of 32-lane groups) or
+    shuffles (narrower groups): +0 beats -0 for max, -0 beats +0 for min, and a
+    NaN anywhere in the row gives NaN, bit for bit as the oracle."""
+    from fugatensor_b200 import ir
+    rng = np.random.default_rng(cols)
+    rows = 256
+    x = np.where(rng.random((rows, cols)) < 0.5, np.float32(0.0), np.float32(-0.0)).astype(np.float32)
+    x[: rows // 4] = -0.0                      # all -0: max is -0
+    x[rows // 4: rows // 2] = 0.0              # all +0: min is +0
+    one = rng.integers(0, cols, rows)
+    x[np.arange(rows // 2, 3 * rows // 4), one[rows // 2: 3 * rows // 4]] = np.nan
+    x[3 * rows // 4:, :] = rng.standard_normal((rows // 4, cols)).astype(np.float32)
+    g = ir.Graph()
+    xv = g.parameter("f32", (rows, cols))
+    desc = g.descriptor([g.reduce_max(xv, (1,)), g.reduce_min(xv, (1,))])
+    got = _run_spec(desc, [x], True)
+    ref = O.evaluate(desc, [x])
+    for u, r in zip(got, ref):
+        both_nan = np.isnan(u) & np.isnan(r)
+        assert not ((_bits(u) != _bits(r)) & ~both_nan).any()
+        assert np.array_equal(np.isnan(u), np.isnan(r))
