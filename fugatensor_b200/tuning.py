@@ -92,25 +92,30 @@ def _synthetic(dt, shape, device, gen):
     return torch.randint(-1000, 1001, shape, device=device, generator=gen).to(tdt)
 
 
-def _time(spec, inputs, device, flush, reps=5):
+def _time_all(specs, inputs, device, flush, rounds=9):
+    """Median launch time of each spec, timed round-robin (one launch of every
+    spec per round, L2 flushed before each) so that clock drift during the
+    measurement affects all candidates alike."""
     import torch
-    outs = [torch.empty(s, dtype=_fgt.torch_dtype(dt), device=device) for dt, s in spec.output_types]
-    ws = torch.empty(max(spec.workspace_bytes, 1), dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     ptrs_in = [t.data_ptr() for t in inputs]
-    ptrs_out = [t.data_ptr() for t in outs]
-    times = []
-    for i in range(reps + 2):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        spec.launch(ptrs_in, ptrs_out, ws.data_ptr(), spec.workspace_bytes, stream.cuda_stream)
-        b.record(stream)
-        b.synchronize()
-        if i >= 2:
-            times.append(a.elapsed_time(b))
-    times.sort()
-    return times[len(times) // 2]
+    bound = []
+    for spec in specs:
+        outs = [torch.empty(s, dtype=_fgt.torch_dtype(dt), device=device) for dt, s in spec.output_types]
+        ws = torch.empty(max(spec.workspace_bytes, 1), dtype=torch.uint8, device=device)
+        bound.append((spec, [t.data_ptr() for t in outs], ws, outs))
+    times = [[] for _ in specs]
+    for rnd in range(rounds + 2):
+        for k, (spec, ptrs_out, ws, _) in enumerate(bound):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            spec.launch(ptrs_in, ptrs_out, ws.data_ptr(), spec.workspace_bytes, stream.cuda_stream)
+            b.record(stream)
+            b.synchronize()
+            if rnd >= 2:
+                times[k].append(a.elapsed_time(b))
+    return [sorted(t)[len(t) // 2] for t in times]
 
 
 def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
@@ -147,7 +152,8 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     with torch.cuda.device(dev):
         inputs = [_synthetic(dt, s, dev, gen) for dt, s in default.input_types]
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-        timed = [(_time(s, inputs, dev, flush), g, s) for g, s in specs]
+        ms_all = _time_all([s for _, s in specs], inputs, dev, flush)
+        timed = [(ms, g, s) for ms, (g, s) in zip(ms_all, specs)]
         del inputs, flush
     ms, geom, best = min(timed, key=lambda t: t[0])
     _store(path, key, {"geometry": list(geom), "ms": round(ms, 5),
