@@ -1384,22 +1384,17 @@ struct Emitter {
       // redo computes them with expf.
       const bool track = (div_phases.count(p) || exp_phases.count(p)) && !col_phases.count(p) && cached;
       const std::string dx = "dgx" + std::to_string(p), dn = "dgn" + std::to_string(p), de = "dge" + std::to_string(p);
-      const std::string sq = P.opt.sq_notes ? "_sq" : "";
       if (track)
-        o << "    float " << dx << " = 0.0f, " << dx << "_b = 0.0f, " << dn << " = __int_as_float(0x7f800000), " << de
-          << " = 0.0f;\n";
+        o << "    float " << dx << " = 0.0f, " << dn << " = __int_as_float(0x7f800000), " << de << " = 0.0f;\n";
       o << "    if (rv) {\n";
       phase_loop(p,
-                 track ? div_form(lane[p], "fgt_div_q", "fgt_div_note" + sq + "(" + dx + ", " + dn + ", ", "fgt_exp_q",
+                 track ? div_form(lane[p], "fgt_div_q", "fgt_div_note(" + dx + ", " + dn + ", ", "fgt_exp_q",
                                   "fgt_exp_note(" + de + ", ")
                        : div_form(lane[p], "fgt_div_by", ""),
                  "    ");
       o << "    }\n";
       if (track) {
-        if (P.opt.sq_notes)
-          o << "    if (rv && !(fgt_div_ok_sq(" << dx << " + " << dx << "_b, " << dn << ") && fgt_exp_ok(" << de << "))) {\n";
-        else
-          o << "    if (rv && !(fgt_div_ok(" << dx << ", " << dn << ") && fgt_exp_ok(" << de << "))) {\n";
+        o << "    if (rv && !(fgt_div_ok(" << dx << ", " << dn << ") && fgt_exp_ok(" << de << "))) {\n";
         put(o, resets[p], "      ");
         phase_loop(p, div_form(lane[p], "fgt_div_ieee", ""), "    ");
         o << "    }\n";
@@ -1817,7 +1812,6 @@ struct Emitter {
       return trim(b) == slot_b(trim(a));
     };
     std::vector<std::string> out;
-    std::map<std::string, std::string> paired_q;  // slot-a quotient -> its float2 pair
     for (const std::string& sa : body) {
       const std::string sb = slot_b(sa);
       const std::string a = trim(sa), b = trim(sb);
@@ -1873,20 +1867,8 @@ struct Emitter {
           if (xa.size() == 3 && xb.size() == 3 && xa[1] == xb[1] && xa[2] == xb[2]) {
             out.push_back("const float2 " + pv + " = fgt_div_q2(make_float2(" + xa[0] + ", " + xb[0] + "), " + xa[1] + ", " +
                           xa[2] + "); const float " + na + " = " + pv + ".x; const float " + nb + " = " + pv + ".y;");
-            paired_q[na] = pv;
             done = true;
           }
-        }
-      }
-      // fgt_div_note_sq(SQ, MN, q) of a paired quotient: one packed FMA into
-      // the slots' own sum trackers (SQ and SQ_b)
-      std::string na_args;
-      if (!done && call_of(a.substr(0, a.size() - 1), "fgt_div_note_sq", &na_args)) {
-        auto xs = split_args(na_args);
-        auto it = xs.size() == 3 ? paired_q.find(trim(xs[2])) : paired_q.end();
-        if (it != paired_q.end()) {
-          out.push_back("fgt_div_note2_sq(" + trim(xs[0]) + ", " + trim(xs[0]) + "_b, " + trim(xs[1]) + ", " + it->second + ");");
-          done = true;
         }
       }
       // L = L + X; over a registered f32 sum accumulator with distinct slots

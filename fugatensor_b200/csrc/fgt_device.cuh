@@ -200,22 +200,6 @@ FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
   mn = fminf(mn, fabsf(q));
 }
 FGT_DEV bool fgt_div_ok(float mx, float mn) { return mx <= 1.32922800e+36f && mn >= 7.52316385e-37f; }
-// The same range check with the upper bound as a sum of squares: sq += q^2
-// (an FMA, on the FMA pipe and pairable, instead of an ALU max) is
-// non-decreasing, +inf once any |q| passes about 1.8e19 and NaN for a NaN
-// quotient, so sq <= FLT_MAX bounds every |q| well inside the exact range.
-FGT_DEV void fgt_div_note_sq(float& sq, float& mn, float q) {
-  sq = __fmaf_rn(q, q, sq);
-  mn = fminf(mn, fabsf(q));
-}
-FGT_DEV void fgt_div_note2_sq(float& sq, float& sq_b, float& mn, float2 q) {
-  const float2 s = __ffma2_rn(q, q, make_float2(sq, sq_b));
-  sq = s.x;
-  sq_b = s.y;
-  mn = fminf(mn, fabsf(q.x));
-  mn = fminf(mn, fabsf(q.y));
-}
-FGT_DEV bool fgt_div_ok_sq(float sq, float mn) { return sq <= 3.40282347e+38f && mn >= 7.52316385e-37f; }
 FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // Max / min of a packed accumulator with a register row piece of N bf16
 // values, two values per instruction (max.NaN / min.NaN on bf16x2: NaN wins,

@@ -1243,7 +1243,6 @@ struct Planner {
     mix(opt.row_staging);
     mix(opt.lane_pairs);
     mix(opt.own_exp);
-    mix(opt.sq_notes);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);
     mix(opt.row_cluster);
