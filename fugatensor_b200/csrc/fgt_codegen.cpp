@@ -376,6 +376,7 @@ struct Emitter {
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
   std::set<std::string> f32_sum_accs;       // f32 sum accumulators (arrays) whose two lanes may add as a pair
+  int64_t col_smem = 0;                     // bytes of column accumulators in shared memory (before the ring)
   const Domain& d;
   std::set<int64_t>* temps_loaded;
   std::vector<RedDef> fin_reds;
@@ -1176,18 +1177,36 @@ struct Emitter {
         post[p].push_back("const " + vt_t(t.dt) + " " + red_var[rd->node] + " = " + finalize(t, a, t.acc_t) + ";");
       }
     }
-    // column reductions: per-thread accumulators across the CTA's rows
+    // column reductions: per-thread accumulators across the CTA's rows, in
+    // registers, or (FGT_ROW_SMEM_COLS) in a thread-private shared-memory
+    // region at the start of the dynamic shared memory: slot
+    // ((c * VEC/4 + v/4) * NT + tid) * 4 + v%4 keeps a thread's four
+    // consecutive elements in one 16-byte word and neighbouring threads'
+    // words adjacent (no bank conflicts for 16-byte accesses)
     std::vector<std::string> colfin;
     for (auto* rd : cols) {
       RedText t = red_text(g, rd->node, P.opt.accumulation, CTX_COL);
       int p = cphase[rd];
       col_phases.insert(p);
       std::string a = fresh("cacc");
-      std::string dims = "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "]";
-      kdecl.push_back(t.acc_t + " " + a + dims + ";");
-      if (t.arg) kdecl.push_back("fgt_i64 " + a + "i" + dims + ";");
+      const bool in_smem = P.opt.smem_cols && K.cluster == 1 && !t.arg;
+      std::string el = a + "[c][v]";
+      if (in_smem) {
+        const int64_t esz = t.acc_t == "double" ? 8 : 4;
+        const std::string NTC = std::to_string(K.nt);
+        if (K.vec % 4 == 0)
+          el = a + "[((c * " + std::to_string(K.vec / 4) + " + v / 4) * " + NTC + " + tid) * 4 + v % 4]";
+        else
+          el = a + "[(c * " + std::to_string(K.vec) + " + v) * " + NTC + " + tid]";
+        kdecl.push_back(t.acc_t + "* const " + a + " = (" + t.acc_t + "*)(fgt_dsmem + " + std::to_string(col_smem) + ");");
+        col_smem += ((int64_t)K.nt * K.nch * K.vec * esz + 15) / 16 * 16;
+      } else {
+        std::string dims = "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "]";
+        kdecl.push_back(t.acc_t + " " + a + dims + ";");
+        if (t.arg) kdecl.push_back("fgt_i64 " + a + "i" + dims + ";");
+      }
       std::string init = "for (int c = 0; c < " + std::to_string(K.nch) + "; ++c) for (int v = 0; v < " + std::to_string(K.vec) +
-                         "; ++v) { " + a + "[c][v] = " + t.ident + ";" + (t.arg ? " " + a + "i[c][v] = " + t.identi + ";" : std::string()) + " }";
+                         "; ++v) { " + el + " = " + t.ident + ";" + (t.arg ? " " + a + "i[c][v] = " + t.identi + ";" : std::string()) + " }";
       kdecl.push_back(init);
       std::string v = val(g.nodes[rd->node].args[0], rd->opmap, Sc{SC_LANE, p});
       if (t.arg) {
@@ -1195,14 +1214,14 @@ struct Emitter {
         if (rd->index_offset) ix = "(" + ix + "+" + std::to_string(rd->index_offset) + "LL)";
         lane[p].push_back("{ const fgt_i64 ix = " + ix + "; " + scan_stmt(t, a + "[c][v]", a + "i[c][v]", v, "ix") + " }");
       } else {
-        lane[p].push_back(comb_stmt(t, a + "[c][v]", v));
+        lane[p].push_back(comb_stmt(t, el, v));
         if (t.acc_t == "float" && t.op == FGT_OP_REDUCE_SUM && !t.storage) f32_sum_accs.insert(a);
       }
       std::string slot = "(" + std::string(K.cluster > 1 ? "(fgt_i64)(blockIdx.x / " + std::to_string(K.cluster) + ")"
                                                           : "(fgt_i64)blockIdx.x") +
                          " * " + std::to_string(K.rows_per_cta) + " + grp)";
       std::string pv = "((" + t.part_t + "*)(p.ws+" + std::to_string(rd->part_val) + "LL))";
-      std::string body = pv + "[" + slot + "*" + std::to_string(d.NI) + "LL + e] = (" + t.part_t + ")" + a + "[c][v];";
+      std::string body = pv + "[" + slot + "*" + std::to_string(d.NI) + "LL + e] = (" + t.part_t + ")" + el + ";";
       if (t.arg) body += " ((fgt_i64*)(p.ws+" + std::to_string(rd->part_idx) + "LL))[" + slot + "*" + std::to_string(d.NI) +
                          "LL + e] = " + a + "i[c][v];";
       colfin.push_back(body);
@@ -1241,6 +1260,7 @@ struct Emitter {
       o << "  const int tid = threadIdx.x; const int lane = tid % " << TPR << "; const int grp = tid / " << TPR << ";\n";
     }
     o << "  (void)lane; (void)grp;\n";
+    o << "  extern __shared__ __align__(16) unsigned char fgt_dsmem[];\n";
     o << "  const fgt_i64 NR = " << d.NR << "LL, NI = " << d.NI << "LL; (void)NI;\n";
     put(o, kdecl, "  ");
     if (cached && !prolane.empty()) {
@@ -1264,7 +1284,7 @@ struct Emitter {
     if (!staged_sites.empty()) {
       // rows in flight per CTA: as many as fit the ring budget (96 KB: two CTAs per SM)
       stages = (int)std::min<int64_t>(8, std::max<int64_t>(1, ((int64_t)P.opt.ring_kb * 1024) / std::max<int64_t>(1, stage_bytes)));
-      int64_t off = 0;
+      int64_t off = col_smem;  // the ring follows any shared-memory column accumulators
       for (auto* rs : staged_sites) {
         rs->smem_off = off;
         off += (int64_t)stages * K.rows_per_cta * K.nch * (K.tpr / K.cluster) * rs->bytes;
@@ -1305,10 +1325,7 @@ struct Emitter {
       if (!rs.staged) o << " " << rs.st << " " << rs.name << "_n" << dims << ";";
       o << "\n";
     }
-    if (stages) {
-      o << "  extern __shared__ __align__(16) unsigned char fgt_dsmem[];\n";
-      o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n";
-    }
+    if (stages) o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n";
     // Ring invariant at the top of iteration i: registers hold row i, ring
     // stage (i+k) % S holds row i+k for k = 1..S (S cp.async groups pending).
     const std::string S = std::to_string(stages);
@@ -1936,7 +1953,7 @@ void generate_sources(Plan& plan) {
     k.stores = keep;
     Emitter em(plan, k, &loaded);
     k.source = em.build();
-    k.smem_bytes = (int64_t)em.stages * em.stage_bytes;
+    k.smem_bytes = em.col_smem + (int64_t)em.stages * em.stage_bytes;
     k.row_phases = em.row_phases;
   }
 }

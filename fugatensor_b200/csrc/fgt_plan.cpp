@@ -1243,6 +1243,7 @@ struct Planner {
     mix(opt.row_staging);
     mix(opt.lane_pairs);
     mix(opt.own_exp);
+    mix(opt.smem_cols);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);
     mix(opt.row_cluster);

@@ -33,10 +33,12 @@ from . import _fgt, ir
 # cluster barrier), so they are not candidates; the option stays available through the spec
 # options. Row flags (fgt_row_flag): 1 bounds a kernel's registers to fit one more CTA per SM
 # when it is close; 2 computes exp with CUDA's expf instead of the library's exp, whose extra
-# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers).
+# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers); 4 keeps
+# column-reduction accumulators in shared memory instead of registers (the LayerNorm VJP holds two
+# per element: 64 of its 243 registers at 32 elements per thread).
 # Candidates a flag leaves unchanged compile to the same source and are timed once.
 _GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
-CANDIDATES = tuple(g + (f,) for f in (0, 1, 2) for g in _GEOMETRIES)
+CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 4, 5) for g in _GEOMETRIES)
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 _lock = threading.Lock()
 

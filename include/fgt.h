@@ -154,7 +154,10 @@ typedef enum fgt_row_flag {
   FGT_ROW_OCCUPANCY_STEP = 1,
   /* exp computed by CUDA's expf everywhere, instead of the library's exp
    * (2^f by ex2.approx, 2^n in the exponent field) in redoable row phases */
-  FGT_ROW_EXPF = 2
+  FGT_ROW_EXPF = 2,
+  /* column-reduction accumulators in shared memory (one private slot per
+   * thread and element) instead of registers */
+  FGT_ROW_SMEM_COLS = 4
 } fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */

@@ -263,3 +263,35 @@ def test_row_max_min_signed_zeros_and_nan(cols):
         both_nan = np.isnan(u) & np.isnan(r)
         assert not ((_bits(u) != _bits(r)) & ~both_nan).any()
         assert np.array_equal(np.isnan(u), np.isnan(r))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_shared_memory_column_accumulators_change_no_bit(dtype):
+    """Column reductions with their accumulators in shared memory (row flag 4)
+    add the same values in the same order as in registers: every output of a
+    LayerNorm VJP equals the register kernel's bit for bit."""
+    import torch
+    import fugatensor_b200.nn.functional as F
+    from fugatensor_b200 import _fgt
+    rng = np.random.default_rng(5)
+    rows, cols = 300, 4096
+    eng = ft.Engine("cuda:0", tune=False)
+    tdt = ft.fp32 if dtype == "f32" else ft.bf16
+    host = {"x": rng.standard_normal((rows, cols)), "dy": rng.standard_normal((rows, cols)),
+            "w": rng.uniform(0.5, 1.5, cols), "b": rng.standard_normal(cols) * 0.1}
+    host = {k: (v.astype(np.float32) if dtype == "f32" else O.f32_to_bf16_bits(v.astype(np.float32))) for k, v in host.items()}
+    T = {k: eng.tensor(v, dtype=tdt) for k, v in host.items()}
+    y = F.layer_norm(T["x"], (cols,), T["w"], T["b"])
+    outs = ft.grad(y, [T["x"], T["w"], T["b"]], seed=T["dy"])
+    desc, leaves, roots = eng.trace(*outs)
+    ins = [l._data for l in leaves]
+    res = []
+    for flags in (0, 4):
+        spec = _fgt.Spec(desc, row_elems=32, ring_kb=32, row_flags=flags)
+        src = "".join(spec.kernel_source(i) for i in range(spec.kernel_count))
+        assert ("* const cacc" in src) == (flags == 4)
+        out = _fgt.run(spec, *ins)
+        torch.cuda.synchronize()
+        res.append([(o.view(torch.int16) if o.dtype == torch.bfloat16 else o).cpu().numpy() for o in out])
+    for k, (u, w) in enumerate(zip(*res)):
+        assert np.array_equal(u.view(np.uint8), w.view(np.uint8)), f"output {k}"
