@@ -1,6 +1,8 @@
 """Seeded random partitions for the planner and the kernels.
 
-Each graph draws one to three leaf tensors, then a random mix of continuous
+Each graph draws one to three leaf tensors (f32 or i32; bf16 instead of f32 for
+seeds from 1000 on, a range of its own so earlier seeds keep their graphs), then
+a random mix of continuous
 elementwise chains, broadcasts and transposes, slices / pads / concatenations,
 selects on comparisons of leaf values, and row, column, whole-tensor and arg
 reductions. Its outputs mix element, row and scalar results. Values stay in
@@ -14,6 +16,7 @@ import numpy as np
 
 import fugatensor_b200 as ft
 from fugatensor_b200 import ir
+from fugatensor_b200 import workloads as W
 
 
 def _leaf_shapes(rng):
@@ -31,11 +34,16 @@ def build(seed):
     shape = _leaf_shapes(rng)
     arrays, vals = [], []
     kind = "i32" if rng.random() < 0.2 else "f32"
+    if kind == "f32" and seed >= 1000:
+        kind = "bf16"
+    fl = kind in ("f32", "bf16")
     for _ in range(int(rng.integers(1, 4))):
         if kind == "i32":
             a = rng.integers(-50, 50, shape, dtype=np.int32)
         else:
             a = (rng.standard_normal(shape) * rng.choice([0.5, 1.0, 3.0])).astype(np.float32)
+            if kind == "bf16":
+                a = W.f32_to_bf16_bits(a)
         arrays.append(a)
         vals.append(g.parameter(kind, shape))
     leaves = list(vals)
@@ -54,11 +62,11 @@ def build(seed):
         y = pick()
         if op in ("add", "mul", "max", "min") and same_shape(x, y) and x.dtype == y.dtype:
             name = {"add": "add", "mul": "mul", "max": "maximum", "min": "minimum"}[op]
-            if op == "mul" and kind == "f32":
+            if op == "mul" and fl:
                 # keep products bounded
                 y = g.tanh(y)
             pool.append(getattr(g, name)(x, y))
-        elif op == "unary" and x.dtype == "f32":
+        elif op == "unary" and x.dtype in ("f32", "bf16"):
             u = rng.choice(["tanh", "exp_tanh", "abs", "square", "sqrt_abs", "neg"])
             if u == "tanh":
                 pool.append(g.tanh(x))
@@ -70,9 +78,9 @@ def build(seed):
                 t = g.tanh(x)
                 pool.append(g.mul(t, t))
             elif u == "sqrt_abs":
-                pool.append(g.sqrt(g.add(g.abs(x), g.filled(1.0, "f32", x.shape))))
+                pool.append(g.sqrt(g.add(g.abs(x), g.filled(1.0, x.dtype, x.shape))))
             else:
-                pool.append(g.mul(x, g.filled(-1.0, "f32", x.shape)))
+                pool.append(g.mul(x, g.filled(-1.0, x.dtype, x.shape)))
         elif op == "select" and len(leaves) >= 2 and same_shape(x, leaves[0]) and x.dtype == leaves[0].dtype:
             c = g.compare(leaves[0], leaves[-1], rng.choice(["gt", "le", "eq"]))
             y2 = y if same_shape(y, x) and y.dtype == x.dtype else x
@@ -104,7 +112,7 @@ def build(seed):
             lo = tuple(int(rng.integers(0, 3)) for _ in x.shape)
             hi = tuple(int(rng.integers(0, 3)) for _ in x.shape)
             inner = tuple(int(rng.integers(0, 2)) if d < 100 else 0 for d in x.shape)
-            pv = g.constant(0.5 if x.dtype == "f32" else 7, x.dtype)
+            pv = g.constant(0.5 if x.dtype in ("f32", "bf16") else 7, x.dtype)
             pool.append(g.pad(x, pv, lo, hi, inner))
         elif op == "concat" and x.rank >= 1:
             ax = int(rng.integers(0, x.rank))
@@ -132,9 +140,9 @@ def build(seed):
             outs.append(g.argmax(x, int(rng.integers(0, x.rank))))
         elif r == "full_sum":
             outs.append(g.reduce_sum(x, tuple(range(x.rank))))
-        elif r == "mean_last" and x.dtype == "f32" and x.shape[-1] > 0:
+        elif r == "mean_last" and x.dtype in ("f32", "bf16") and x.shape[-1] > 0:
             s = g.reduce_sum(x, (x.rank - 1,))
-            outs.append(g.div(s, g.filled(float(x.shape[-1]), "f32", s.shape)))
+            outs.append(g.div(s, g.filled(float(x.shape[-1]), x.dtype, s.shape)))
         elif r == "min_mid" and x.rank >= 2 and all(s > 0 for s in x.shape):
             outs.append(g.reduce_min(x, (x.rank // 2,)))
     return g, outs, arrays
