@@ -713,7 +713,20 @@ struct Emitter {
         require(id == K.scatter_node && K.scatter_stage == 3, "internal: scatter_add read before it is complete",
                 FGT_ERR_UNSUPPORTED);
         const std::string bv = val(n.args[0], m, D);
-        const std::string av = scatter_acc_ptr() + "[" + itext(to_linear(m, n.shape, d)) + "]";
+        std::string av = scatter_acc_ptr() + "[" + itext(to_linear(m, n.shape, d)) + "]";
+        if (K.scatter_csr) {
+          // this element's row bucket: the update rows scattered to it, each
+          // read once by pointer, summed in the accumulator type
+          const Node& up = g.nodes[n.args[2]];
+          const std::string H = std::to_string(n.n() / n.shape[0]) + "LL";
+          const std::string A = csr_acc_t();
+          av = fresh("sa");
+          add(D, A + " " + av + " = 0; { const fgt_i64 l_ = " + itext(to_linear(m, n.shape, d)) +
+                     "; const fgt_i64 r_ = l_ / " + H + ", h_ = l_ - r_ * " + H + "; const int b_ = " + csr_arr(2) +
+                     "[r_], c_ = " + csr_arr(0) + "[r_]; for (int k_ = 0; k_ < c_; ++k_) { const fgt_i64 u_ = " + csr_arr(3) +
+                     "[b_ + k_]; " + av + " += (" + A + ")(" + ld_conv(up.dt, ptr_of(n.args[2]) + "[u_ * " + H + " + h_]") +
+                     "); } }");
+        }
         std::string expr;
         if (n.dt == FGT_F32) expr = "__double2float_rn((double)" + bv + " + " + av + ")";
         else if (is_float(n.dt)) expr = rnd(n.dt, "fgt_f64_to_f32_odd((double)" + bv + " + " + av + ")");
@@ -1460,6 +1473,45 @@ struct Emitter {
   std::string scatter_acc_ptr() const {
     return "((" + scatter_acc_t() + "*)(p.ws+" + std::to_string(K.scatter_acc) + "LL))";
   }
+  // CSR scatter: int32 arrays 0 counts, 1 fill cursors, 2 bucket offsets (R
+  // each), 3 update ids (one per index)
+  std::string csr_arr(int k) const {
+    const int64_t R = g.nodes[K.scatter_node].shape[0];
+    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * R * k) + "LL))";
+  }
+  // bucket sums: f64 for floats (rounded once with the base), unsigned
+  // (wrapping) for integers
+  std::string csr_acc_t() const {
+    const Node& n = g.nodes[K.scatter_node];
+    if (is_float(n.dt)) return "double";
+    return n.dt == FGT_I64 ? "unsigned long long" : "unsigned int";
+  }
+  // stage 13: exclusive scan of the R bucket counts into offsets, one CTA of
+  // 1024 threads, four counts per thread per step (warp shuffles, then the
+  // warp totals), carrying the running total across steps
+  std::string build_scan() {
+    const int64_t R = g.nodes[K.scatter_node].shape[0];
+    std::ostringstream o;
+    o << args_struct();
+    o << "extern \"C\" __global__ void __launch_bounds__(1024) " << K.name << "(const FgtArgs p) {\n";
+    o << "  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;\n";
+    o << "  const fgt_i64 R = " << R << "LL;\n";
+    o << "  const int* cnt = " << csr_arr(0) << "; int* off = " << csr_arr(2) << ";\n";
+    o << "  __shared__ int wsum_[32];\n  int carry = 0;\n";
+    o << "  for (fgt_i64 base = 0; base < R; base += 4096) {\n";
+    o << "    int v[4]; int s = 0;\n";
+    o << "    #pragma unroll\n    for (int j = 0; j < 4; ++j) { const fgt_i64 i = base + (fgt_i64)tid * 4 + j; v[j] = i < R ? cnt[i] : 0; s += v[j]; }\n";
+    o << "    int x = s;\n";
+    o << "    #pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= d) x += y; }\n";
+    o << "    if (lane == 31) wsum_[wid] = x;\n    __syncthreads();\n";
+    o << "    if (wid == 0) {\n      int w = wsum_[lane];\n";
+    o << "      #pragma unroll\n      for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, w, d); if (lane >= d) w += y; }\n";
+    o << "      wsum_[lane] = w;\n    }\n    __syncthreads();\n";
+    o << "    int run = carry + (wid > 0 ? wsum_[wid - 1] : 0) + x - s;\n";
+    o << "    #pragma unroll\n    for (int j = 0; j < 4; ++j) { const fgt_i64 i = base + (fgt_i64)tid * 4 + j; if (i < R) off[i] = run; run += v[j]; }\n";
+    o << "    carry += wsum_[31];\n    __syncthreads();\n  }\n}\n";
+    return o.str();
+  }
 
   std::string build_elem() {
     nphase = 1;
@@ -1471,6 +1523,22 @@ struct Emitter {
     std::vector<std::pair<RedText, std::string>> accs;
     std::vector<std::string> partial_store;
     if (K.scatter_stage == 1) lane[0].push_back(scatter_acc_ptr() + "[e] = 0;");
+    if (K.scatter_stage == 11) lane[0].push_back(csr_arr(0) + "[e] = 0; " + csr_arr(1) + "[e] = 0;");
+    if (K.scatter_stage == 12 || K.scatter_stage == 14) {
+      // over the indices: count each in-range index's update, then place its
+      // id in the row's bucket (a cursor per row; order within a bucket free)
+      const Node& n = g.nodes[K.scatter_node];
+      Map mi;
+      mi.lin = true;
+      mi.l = idx_const(d.nd(), 0);
+      for (int j = 0; j < d.nd(); ++j) mi.l.c[j] = d.iw[j];
+      const std::string iv = val(n.args[1], mi, Sc{SC_LANE, 0});
+      const std::string R = std::to_string(n.shape[0]) + "LL";
+      const std::string body = K.scatter_stage == 12
+                                   ? "atomicAdd(" + csr_arr(0) + " + gi_, 1);"
+                                   : csr_arr(3) + "[" + csr_arr(2) + "[gi_] + atomicAdd(" + csr_arr(1) + " + gi_, 1)] = (int)e;";
+      lane[0].push_back("{ const fgt_i64 gi_ = (fgt_i64)(" + iv + "); if (gi_ >= 0LL && gi_ < " + R + ") " + body + " }");
+    }
     if (K.scatter_stage == 2) {
       // updates domain: base offset of update i = its coordinates with the
       // scattered axis replaced by indices[i]
@@ -1925,7 +1993,7 @@ struct Emitter {
   }
 
   std::string build() {
-    std::string src = row ? build_row() : elem ? build_elem() : build_fin();
+    std::string src = row ? build_row() : elem ? (K.scatter_stage == 13 ? build_scan() : build_elem()) : build_fin();
     // kernels without per-phase tracking keep the per-element guarded division
     std::istringstream in(src);
     std::ostringstream out;

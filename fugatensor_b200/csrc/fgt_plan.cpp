@@ -663,8 +663,14 @@ struct Planner {
     const Node& base = g.nodes[n.args[0]];
     const Node& up = g.nodes[n.args[2]];
     const int ax = (int)n.attrs[0], ir = g.nodes[n.args[1]].rank();
+    // Counting-sort form for row scatters whose updates are materialised
+    // (read by pointer at any update row): every update is read once and no
+    // base-sized accumulator is zeroed, updated atomically and read back.
+    const bool csr = ax == 0 && ir == 1 && base.rank() >= 1 && loc[n.args[2]].kind != Loc::NONE && base.shape[0] > 0 &&
+                     base.shape[0] < (1LL << 31) && g.nodes[n.args[1]].n() < (1LL << 31);
     const int acc_bytes = is_float(n.dt) ? 8 : dtype_size(n.dt);
-    const int64_t acc = alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
+    const int64_t R = base.rank() >= 1 ? base.shape[0] : 1, NU = g.nodes[n.args[1]].n();
+    const int64_t acc = csr ? alloc((3 * R + std::max<int64_t>(1, NU)) * 4) : alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
     auto make = [&](const Shape& shape, int stage) {
       KernelDef k;
       k.kind = KKind::ELEM;
@@ -674,8 +680,40 @@ struct Planner {
       k.scatter_node = s;
       k.scatter_stage = stage;
       k.scatter_acc = acc;
+      k.scatter_csr = csr;
       return k;
     };
+    auto indices_kernel = [&](int stage) {
+      // over the indices: reads indices[i] (any expression of the inputs)
+      KernelDef k = make(g.nodes[n.args[1]].shape, stage);
+      Analyzer an(g, loc, k.kind, k.dom);
+      Map mi;
+      mi.lin = true;
+      mi.l = idx_const(k.dom.nd(), 0);
+      for (int j = 0; j < k.dom.nd(); ++j) mi.l.c[j] = k.dom.iw[j];
+      try {
+        an.run(n.args[1], mi);
+      } catch (NotFusible&) {
+        fail(FGT_ERR_UNSUPPORTED, "internal: scatter_add indices not evaluable");
+      }
+      k.vec = 1;
+      geometry_elem(k);
+      return k;
+    };
+    if (csr) {
+      KernelDef z = make(Shape{R}, 11);
+      z.vec = 1;
+      geometry_elem(z);
+      plan.kernels.push_back(z);
+      if (NU > 0) plan.kernels.push_back(indices_kernel(12));
+      KernelDef sc = make(Shape{R}, 13);
+      sc.nt = 1024;
+      sc.tpr = 1024;
+      sc.vec = 1;
+      sc.max_ctas = 1;
+      plan.kernels.push_back(sc);
+      if (NU > 0) plan.kernels.push_back(indices_kernel(14));
+    }
     auto identity = [&](const KernelDef& k) {
       Map m;
       m.lin = true;
@@ -684,12 +722,14 @@ struct Planner {
       return m;
     };
     // 1: accumulator <- 0
-    KernelDef k1 = make(base.shape, 1);
-    k1.vec = 1;
-    geometry_elem(k1);
-    plan.kernels.push_back(k1);
+    if (!csr) {
+      KernelDef k1 = make(base.shape, 1);
+      k1.vec = 1;
+      geometry_elem(k1);
+      plan.kernels.push_back(k1);
+    }
     // 2: accumulator[.., indices[i..], ..] += updates[.., i.., ..]
-    if (up.n() > 0) {
+    if (!csr && up.n() > 0) {
       KernelDef k2 = make(up.shape, 2);
       Analyzer an(g, loc, k2.kind, k2.dom);
       const Map mu = identity(k2);

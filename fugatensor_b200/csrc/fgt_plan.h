@@ -122,7 +122,13 @@ struct KernelDef {
   // the accumulator, 2 adds the in-range updates atomically, 3 combines base
   // and accumulator into the result
   int scatter_node = -1, scatter_stage = 0;
-  int64_t scatter_acc = -1;       // workspace offset of the accumulator
+  int64_t scatter_acc = -1;       // workspace offset of the accumulator (CSR: of the row buckets)
+  // Row scatter (axis 0, 1-D indices, materialised updates) as a counting
+  // sort: 11 zeroes the per-row counters, 12 counts the updates of each base
+  // row, 13 scans the counts into bucket offsets (one CTA), 14 fills each
+  // row's bucket with its update ids, and 3 sums each output element's bucket
+  // in the accumulator type and adds the base (reading every update once).
+  bool scatter_csr = false;
   int row_phases = 0;             // ROW: dependency levels holding row reductions (block barriers per row)
   int regs = -1, spill_bytes = -1;  // from the sm_100a compile (-1: unknown)
 };
