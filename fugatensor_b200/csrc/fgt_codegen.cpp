@@ -718,14 +718,36 @@ struct Emitter {
           // this element's row bucket: the update rows scattered to it, each
           // read once by pointer, summed in the accumulator type
           const Node& up = g.nodes[n.args[2]];
-          const std::string H = std::to_string(n.n() / n.shape[0]) + "LL";
+          const int64_t HN = n.n() / n.shape[0];
+          const std::string H = std::to_string(HN) + "LL";
           const std::string A = csr_acc_t();
+          const std::string lin = itext(to_linear(m, n.shape, d));
+          if (elem && D.k == SC_LANE && lin == "(0LL+1LL*e)" && HN % K.vec == 0) {
+            // a chunk's VEC elements share one row: walk its bucket once and
+            // read VEC consecutive update values per entry
+            auto it = memo.find("csr_chunk");
+            std::string sa;
+            if (it != memo.end()) sa = it->second;
+            else {
+              sa = fresh("sa");
+              memo["csr_chunk"] = sa;
+              const std::string V = std::to_string(K.vec);
+              chunkpre[0].push_back(A + " " + sa + "[" + V + "]; for (int v = 0; v < " + V + "; ++v) " + sa + "[v] = 0; { const fgt_i64 r_ = e0 / " +
+                                    H + ", h_ = e0 - r_ * " + H + "; const int b_ = " + csr_arr(2) + "[r_], c_ = " + csr_arr(0) +
+                                    "[r_]; for (int k_ = 0; k_ < c_; ++k_) { const fgt_i64 u_ = " + csr_arr(3) + "[b_ + k_]; " +
+                                    st_t(up.dt) + " uv_[" + V + "]; fgt_vload_keep(uv_, " + ptr_of(n.args[2]) + " + u_ * " + H +
+                                    " + h_); for (int v = 0; v < " + V + "; ++v) " + sa + "[v] += (" + A + ")(" +
+                                    ld_conv(up.dt, "uv_[v]") + "); } }");
+            }
+            av = sa + "[v]";
+          } else {
           av = fresh("sa");
-          add(D, A + " " + av + " = 0; { const fgt_i64 l_ = " + itext(to_linear(m, n.shape, d)) +
+          add(D, A + " " + av + " = 0; { const fgt_i64 l_ = " + lin +
                      "; const fgt_i64 r_ = l_ / " + H + ", h_ = l_ - r_ * " + H + "; const int b_ = " + csr_arr(2) +
                      "[r_], c_ = " + csr_arr(0) + "[r_]; for (int k_ = 0; k_ < c_; ++k_) { const fgt_i64 u_ = " + csr_arr(3) +
                      "[b_ + k_]; " + av + " += (" + A + ")(" + ld_conv(up.dt, ptr_of(n.args[2]) + "[u_ * " + H + " + h_]") +
                      "); } }");
+          }
         }
         std::string expr;
         if (n.dt == FGT_F32) expr = "__double2float_rn((double)" + bv + " + " + av + ")";
