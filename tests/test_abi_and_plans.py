@@ -232,3 +232,26 @@ def test_column_reductions_over_long_rows_plan_as_tiles():
     s = _fgt.Spec(g.descriptor([g.reduce_sum(x, (0,))]))
     k0 = s.execution_plan["cuda_lowering"]["kernels"][0]
     assert k0["threads_per_row"] == 512 and not k0["streaming"] and k0["col_tiles"] == 1
+
+
+def test_row_scatter_plans_as_counting_sort():
+    """scatter_add along axis 0 with 1-D indices and materialised updates takes
+    the counting-sort form (zero, count, scan on one CTA, fill, bucket sums);
+    other scatters keep the atomic accumulator form."""
+    from fugatensor_b200 import _fgt
+    g = ir.Graph()
+    b, i, u = g.parameter("f32", (1000, 64)), g.parameter("i32", (300,)), g.parameter("f32", (300, 64))
+    s = _fgt.Spec(g.descriptor([g.scatter_add(b, i, u, 0)]))
+    ks = s.execution_plan["cuda_lowering"]["kernels"]
+    assert len(ks) == 5 and ks[2]["threads"] == 1024
+    assert "atomicAdd" not in s.kernel_source(4) and "fgt_vload_keep(uv_" in s.kernel_source(4)
+    # along axis 1: the accumulator form
+    g = ir.Graph()
+    b, i, u = g.parameter("f32", (64, 1000)), g.parameter("i32", (300,)), g.parameter("f32", (64, 300))
+    s = _fgt.Spec(g.descriptor([g.scatter_add(b, i, u, 1)]))
+    assert s.kernel_count == 3 and "atomicAdd" in s.kernel_source(1)
+    # computed updates (not materialised): the accumulator form
+    g = ir.Graph()
+    b, i, u = g.parameter("f32", (1000, 64)), g.parameter("i32", (300,)), g.parameter("f32", (300, 64))
+    s = _fgt.Spec(g.descriptor([g.scatter_add(b, i, g.mul(u, u), 0)]))
+    assert s.kernel_count == 3
