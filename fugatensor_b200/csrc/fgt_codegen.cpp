@@ -1919,7 +1919,6 @@ struct Emitter {
       return trim(b) == slot_b(trim(a));
     };
     std::vector<std::string> out;
-    std::map<std::string, std::string> paired_q;  // slot-a quotient -> its float2 pair
     for (const std::string& sa : body) {
       const std::string sb = slot_b(sa);
       const std::string a = trim(sa), b = trim(sb);
@@ -1975,29 +1974,8 @@ struct Emitter {
           if (xa.size() == 3 && xb.size() == 3 && xa[1] == xb[1] && xa[2] == xb[2]) {
             out.push_back("const float2 " + pv + " = fgt_div_q2(make_float2(" + xa[0] + ", " + xb[0] + "), " + xa[1] + ", " +
                           xa[2] + "); const float " + na + " = " + pv + ".x; const float " + nb + " = " + pv + ".y;");
-            paired_q[na] = pv;
             done = true;
           }
-        }
-      }
-      // range notes of both slots in one three-input max / min: a paired
-      // quotient's fgt_div_note, and fgt_exp_note of two arguments
-      std::string nargs;
-      if (!done && P.opt.note3 && call_of(a.substr(0, a.size() - 1), "fgt_div_note", &nargs)) {
-        auto xs = split_args(nargs);
-        auto it = xs.size() == 3 ? paired_q.find(trim(xs[2])) : paired_q.end();
-        if (it != paired_q.end()) {
-          out.push_back("fgt_div_note2(" + trim(xs[0]) + ", " + trim(xs[1]) + ", " + it->second + ");");
-          done = true;
-        }
-      }
-      std::string nb_args;
-      if (!done && P.opt.note3 && call_of(a.substr(0, a.size() - 1), "fgt_exp_note", &nargs) &&
-          call_of(b.substr(0, b.size() - 1), "fgt_exp_note", &nb_args)) {
-        auto xs = split_args(nargs), ys = split_args(nb_args);
-        if (xs.size() == 2 && ys.size() == 2 && trim(xs[0]) == trim(ys[0])) {
-          out.push_back("fgt_exp_note2(" + trim(xs[0]) + ", make_float2(" + trim(xs[1]) + ", " + trim(ys[1]) + "));");
-          done = true;
         }
       }
       // L = L + X; over a registered f32 sum accumulator with distinct slots

@@ -200,16 +200,6 @@ FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
   mn = fminf(mn, fabsf(q));
 }
 FGT_DEV bool fgt_div_ok(float mx, float mn) { return mx <= 1.32922800e+36f && mn >= 7.52316385e-37f; }
-// The notes of two lanes' quotients (or exp arguments) in one three-input
-// max / min each (sm_100a): the same max.NaN / IEEE-min semantics.
-FGT_DEV void fgt_div_note2(float& mx, float& mn, float2 q) {
-  const float a = fabsf(q.x), b = fabsf(q.y);
-  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(mx) : "f"(mx), "f"(a), "f"(b));
-  asm("min.f32 %0, %1, %2, %3;" : "=f"(mn) : "f"(mn), "f"(a), "f"(b));
-}
-FGT_DEV void fgt_exp_note2(float& mx, float2 x) {
-  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(mx) : "f"(mx), "f"(fabsf(x.x)), "f"(fabsf(x.y)));
-}
 FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // Max / min of a packed accumulator with a register row piece of N bf16
 // values, two values per instruction (max.NaN / min.NaN on bf16x2: NaN wins,

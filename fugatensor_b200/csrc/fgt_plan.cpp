@@ -1283,7 +1283,6 @@ struct Planner {
     mix(opt.row_staging);
     mix(opt.lane_pairs);
     mix(opt.own_exp);
-    mix(opt.note3);
     mix(opt.smem_cols);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);

@@ -143,7 +143,6 @@ struct Options {
   int lane_pairs = 1;             // element loops pair lanes for f32x2 arithmetic (FGT_LANE_PAIRS=0: one lane at a time)
   int occupancy_step = 0;         // row kernels: bound registers to fit one more CTA per SM when close (FGT_ROW_OCCUPANCY_STEP)
   int smem_cols = 0;              // row kernels: column accumulators in shared memory (FGT_ROW_SMEM_COLS)
-  int note3 = 1;                  // paired lanes' range notes as three-input max / min (FGT_NOTE3=0: two-input)
   int own_exp = 1;                // exp in redoable row phases by fgt_exp_q, else expf (FGT_ROW_EXPF, or FGT_OWN_EXP=0)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
   int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)
