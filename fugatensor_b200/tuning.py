@@ -33,12 +33,13 @@ from . import _fgt, ir
 # cluster barrier), so they are not candidates; the option stays available through the spec
 # options. Row flags (fgt_row_flag): 1 bounds a kernel's registers to fit one more CTA per SM
 # when it is close; 2 computes exp with CUDA's expf instead of the library's exp, whose extra
-# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers); 4 keeps
-# column-reduction accumulators in shared memory instead of registers (the LayerNorm VJP holds two
-# per element: 64 of its 243 registers at 32 elements per thread).
-# Candidates a flag leaves unchanged compile to the same source and are timed once.
+# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers).
+# Flag 4 (column accumulators in shared memory) measured no faster on any benchmark partition (the
+# LayerNorm VJP keeps one CTA per SM at 169 registers, and two with the occupancy step spill), so it
+# is not a candidate. Candidates a flag leaves unchanged compile to the same source (kernel names
+# aside) and are timed once.
 _GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
-CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 4, 5) for g in _GEOMETRIES)
+CANDIDATES = tuple(g + (f,) for f in (0, 1, 2) for g in _GEOMETRIES)
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 _lock = threading.Lock()
 
@@ -142,7 +143,8 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     for e, r, c, o in CANDIDATES:
         s = default if (e, r, c, o) == (0, 0, 0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
                                                                    row_elems=e, ring_kb=r, row_cluster=c, row_flags=o)
-        src = tuple(s.kernel_source(i) for i in range(s.kernel_count))
+        src = tuple(s.kernel_source(i).replace(k["name"], "K")
+                    for i, k in enumerate(s.execution_plan["cuda_lowering"]["kernels"]))
         if src in seen:
             continue
         seen[src] = True
