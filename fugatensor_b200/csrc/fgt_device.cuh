@@ -166,19 +166,25 @@ FGT_DEV float fgt_ex2_approx(float f) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(f));
   return r;
 }
+// bits(p) + (bits(t) << 23) as one integer multiply-add (FMA pipe) rather
+// than a shift and an add (ALU pipe); the same bits modulo 2^32
+FGT_DEV float fgt_exp_scale(float p, float t) {
+  int r;
+  asm("mad.lo.s32 %0, %1, 8388608, %2;" : "=r"(r) : "r"(__float_as_int(t)), "r"(__float_as_int(p)));
+  return __int_as_float(r);
+}
 FGT_DEV float fgt_exp_q(float x) {
   const float t = __fmaf_rn(x, __int_as_float(0x3fb8aa3b), __int_as_float(0x4b400000));
   const float nn = __fsub_rn(__int_as_float(0x4b400000), t);  // -n, exact
   const float f = __fmaf_rn(x, __int_as_float(0x32a57060), __fmaf_rn(x, __int_as_float(0x3fb8aa3b), nn));
-  return __int_as_float(__float_as_int(fgt_ex2_approx(f)) + (__float_as_int(t) << 23));
+  return fgt_exp_scale(fgt_ex2_approx(f), t);
 }
 FGT_DEV float2 fgt_exp_q2(float2 x) {
   const float2 t = __ffma2_rn(x, make_float2(__int_as_float(0x3fb8aa3b), __int_as_float(0x3fb8aa3b)), make_float2(__int_as_float(0x4b400000), __int_as_float(0x4b400000)));
   const float2 nn = __ffma2_rn(t, make_float2(-1.0f, -1.0f), make_float2(__int_as_float(0x4b400000), __int_as_float(0x4b400000)));
   const float2 f1 = __ffma2_rn(x, make_float2(__int_as_float(0x3fb8aa3b), __int_as_float(0x3fb8aa3b)), nn);
   const float2 f = __ffma2_rn(x, make_float2(__int_as_float(0x32a57060), __int_as_float(0x32a57060)), f1);
-  return make_float2(__int_as_float(__float_as_int(fgt_ex2_approx(f.x)) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(fgt_ex2_approx(f.y)) + (__float_as_int(t.y) << 23)));
+  return make_float2(fgt_exp_scale(fgt_ex2_approx(f.x), t.x), fgt_exp_scale(fgt_ex2_approx(f.y), t.y));
 }
 // Warp-wide f32 max / min in one instruction (sm_100a redux.sync with .NaN:
 // a NaN input gives NaN), the same IEEE maximum / minimum as fgt_fmax /
