@@ -1880,7 +1880,10 @@ struct Emitter {
         if (n >= T.size() || T[n].s != "=" || (n + 1 < T.size() && T[n + 1].s == "=")) continue;
         size_t j = i;  // previous non-space token
         while (j > 0 && T[j - 1].s == " ") --j;
-        if (j > 0 && T[j - 1].ident && T[j - 1].s != "else" && T[j - 1].s != "return") renamed.insert(T[i].s);
+        // a type before the name, or a comma (later declarators of one
+        // declaration: the generated code has no other `, name =`)
+        if (j > 0 && ((T[j - 1].ident && T[j - 1].s != "else" && T[j - 1].s != "return") || T[j - 1].s == ","))
+          renamed.insert(T[i].s);
       }
     }
     auto slot_b = [&](const std::string& st) {
