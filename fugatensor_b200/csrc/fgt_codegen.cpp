@@ -721,8 +721,13 @@ struct Emitter {
           const int64_t HN = n.n() / n.shape[0];
           const std::string H = std::to_string(HN) + "LL";
           const std::string A = csr_acc_t();
-          const std::string lin = itext(to_linear(m, n.shape, d));
-          if (elem && D.k == SC_LANE && lin == "(0LL+1LL*e)" && HN % K.vec == 0) {
+          const Idx li = to_linear(m, n.shape, d);
+          const std::string lin = itext(li);
+          // the element's linear index is the kernel's element index e (the
+          // base's own row-major order): a chunk is VEC consecutive elements
+          bool ident = li.aff && li.k == 0 && (int)li.c.size() == d.nd();
+          for (int j = 0; ident && j < d.nd(); ++j) ident = li.c[j] == d.iw[j];
+          if (elem && D.k == SC_LANE && ident && n.n() == d.NI && HN % K.vec == 0) {
             // a chunk's VEC elements share one row: walk its bucket once and
             // read VEC consecutive update values per entry
             auto it = memo.find("csr_chunk");
