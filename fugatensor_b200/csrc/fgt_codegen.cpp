@@ -1514,20 +1514,28 @@ struct Emitter {
     return n.dt == FGT_I64 ? "unsigned long long" : "unsigned int";
   }
   // stage 13: exclusive scan of the R bucket counts into offsets, one CTA of
-  // 1024 threads, four counts per thread per step (warp shuffles, then the
-  // warp totals), carrying the running total across steps
+  // 1024 threads, 16 consecutive counts per thread per step (four 16-byte
+  // loads issued together), warp shuffles over the thread totals, then over
+  // the warp totals, carrying the running total across steps
   std::string build_scan() {
     const int64_t R = g.nodes[K.scatter_node].shape[0];
+    const int64_t RP = (R + 3) / 4 * 4;  // the counts array is read in int4 words up to here
     std::ostringstream o;
     o << args_struct();
     o << "extern \"C\" __global__ void __launch_bounds__(1024) " << K.name << "(const FgtArgs p) {\n";
     o << "  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;\n";
-    o << "  const fgt_i64 R = " << R << "LL;\n";
+    o << "  const fgt_i64 R = " << R << "LL, RP = " << RP << "LL;\n";
     o << "  const int* cnt = " << csr_arr(0) << "; int* off = " << csr_arr(2) << ";\n";
     o << "  __shared__ int wsum_[32];\n  int carry = 0;\n";
-    o << "  for (fgt_i64 base = 0; base < R; base += 4096) {\n";
-    o << "    int v[4]; int s = 0;\n";
-    o << "    #pragma unroll\n    for (int j = 0; j < 4; ++j) { const fgt_i64 i = base + (fgt_i64)tid * 4 + j; v[j] = i < R ? cnt[i] : 0; s += v[j]; }\n";
+    o << "  for (fgt_i64 base = 0; base < R; base += 16384) {\n";
+    o << "    int v[16]; int s = 0;\n";
+    o << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n";
+    o << "      const fgt_i64 i = base + (fgt_i64)tid * 16 + q * 4;\n";
+    o << "      int4 w = make_int4(0, 0, 0, 0);\n";
+    o << "      if (i < RP) w = *reinterpret_cast<const int4*>(cnt + i);\n";
+    o << "      v[q * 4] = i < R ? w.x : 0; v[q * 4 + 1] = i + 1 < R ? w.y : 0; v[q * 4 + 2] = i + 2 < R ? w.z : 0; v[q * 4 + 3] = i + 3 < R ? w.w : 0;\n";
+    o << "    }\n";
+    o << "    #pragma unroll\n    for (int j = 0; j < 16; ++j) s += v[j];\n";
     o << "    int x = s;\n";
     o << "    #pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= d) x += y; }\n";
     o << "    if (lane == 31) wsum_[wid] = x;\n    __syncthreads();\n";
@@ -1535,7 +1543,7 @@ struct Emitter {
     o << "      #pragma unroll\n      for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, w, d); if (lane >= d) w += y; }\n";
     o << "      wsum_[lane] = w;\n    }\n    __syncthreads();\n";
     o << "    int run = carry + (wid > 0 ? wsum_[wid - 1] : 0) + x - s;\n";
-    o << "    #pragma unroll\n    for (int j = 0; j < 4; ++j) { const fgt_i64 i = base + (fgt_i64)tid * 4 + j; if (i < R) off[i] = run; run += v[j]; }\n";
+    o << "    #pragma unroll\n    for (int j = 0; j < 16; ++j) { const fgt_i64 i = base + (fgt_i64)tid * 16 + j; if (i < R) off[i] = run; run += v[j]; }\n";
     o << "    carry += wsum_[31];\n    __syncthreads();\n  }\n}\n";
     return o.str();
   }
