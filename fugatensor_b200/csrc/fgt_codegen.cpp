@@ -1501,10 +1501,11 @@ struct Emitter {
     return "((" + scatter_acc_t() + "*)(p.ws+" + std::to_string(K.scatter_acc) + "LL))";
   }
   // CSR scatter: int32 arrays 0 counts, 1 fill cursors, 2 bucket offsets (R
-  // each), 3 update ids (one per index)
+  // each, padded to a multiple of 4 so every array is 16-byte aligned), 3
+  // update ids (one per index)
   std::string csr_arr(int k) const {
-    const int64_t R = g.nodes[K.scatter_node].shape[0];
-    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * R * k) + "LL))";
+    const int64_t RA = (g.nodes[K.scatter_node].shape[0] + 3) / 4 * 4;
+    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * RA * k) + "LL))";
   }
   // bucket sums: f64 for floats (rounded once with the base), unsigned
   // (wrapping) for integers
@@ -1543,7 +1544,13 @@ struct Emitter {
     o << "      #pragma unroll\n      for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, w, d); if (lane >= d) w += y; }\n";
     o << "      wsum_[lane] = w;\n    }\n    __syncthreads();\n";
     o << "    int run = carry + (wid > 0 ? wsum_[wid - 1] : 0) + x - s;\n";
-    o << "    #pragma unroll\n    for (int j = 0; j < 16; ++j) { const fgt_i64 i = base + (fgt_i64)tid * 16 + j; if (i < R) off[i] = run; run += v[j]; }\n";
+    // offsets written as 16-byte words where the whole word is in range
+    o << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n";
+    o << "      const fgt_i64 i = base + (fgt_i64)tid * 16 + q * 4;\n";
+    o << "      int4 w; w.x = run; run += v[q * 4]; w.y = run; run += v[q * 4 + 1]; w.z = run; run += v[q * 4 + 2]; w.w = run; run += v[q * 4 + 3];\n";
+    o << "      if (i + 3 < R) *reinterpret_cast<int4*>(off + i) = w;\n";
+    o << "      else { if (i < R) off[i] = w.x; if (i + 1 < R) off[i + 1] = w.y; if (i + 2 < R) off[i + 2] = w.z; }\n";
+    o << "    }\n";
     o << "    carry += wsum_[31];\n    __syncthreads();\n  }\n}\n";
     return o.str();
   }

@@ -670,7 +670,10 @@ struct Planner {
                      base.shape[0] < (1LL << 31) && g.nodes[n.args[1]].n() < (1LL << 31);
     const int acc_bytes = is_float(n.dt) ? 8 : dtype_size(n.dt);
     const int64_t R = base.rank() >= 1 ? base.shape[0] : 1, NU = g.nodes[n.args[1]].n();
-    const int64_t acc = csr ? alloc((3 * R + std::max<int64_t>(1, NU)) * 4) : alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
+    // CSR arrays: counts, cursors and offsets of RA = R rounded up to 4 ints
+    // each (every array 16-byte aligned), then one update id per index
+    const int64_t RA = (R + 3) / 4 * 4;
+    const int64_t acc = csr ? alloc((3 * RA + std::max<int64_t>(1, NU)) * 4) : alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
     auto make = [&](const Shape& shape, int stage) {
       KernelDef k;
       k.kind = KKind::ELEM;

@@ -53,10 +53,12 @@ def test_gather_rows_and_columns(rows, cols):
     _check(outs, {id(X): x, id(RI): ri, id(CI): ci})
 
 
+@pytest.mark.parametrize("rows,cols,n", [(512, 96, 4000), (1021, 33, 3000), (70001, 8, 50000)])
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "i32", "i64"])
-def test_scatter_add_random(dtype):
-    rng = np.random.default_rng(11)
-    rows, cols, n = 512, 96, 4000
+def test_scatter_add_random(dtype, rows, cols, n):
+    """Row scatter_add (the counting-sort form) against the oracle: duplicate and
+    out-of-range indices, odd row counts, and more rows than one scan step."""
+    rng = np.random.default_rng(11 + rows)
     idx = rng.integers(-5, rows + 5, n).astype(np.int32)
     if dtype in ("i32", "i64"):
         base = rng.integers(-1000, 1000, (rows, cols)).astype(np.int32 if dtype == "i32" else np.int64)
