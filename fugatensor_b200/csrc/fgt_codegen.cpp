@@ -961,7 +961,7 @@ struct Emitter {
       const std::string mask = std::to_string(NW - 1);
       bool any_arg = false;
       for (auto& [t, a] : accs) {
-        if (!t.arg) {
+        if (!t.arg && P.opt.xw_tree) {
           // Every thread reads the NW warp partials (broadcast loads) and
           // folds them in the pairwise tree the butterfly forms, which is
           // the same value bit for bit, without its dependent shuffles.
@@ -979,16 +979,20 @@ struct Emitter {
           }
           out.push_back(a + " = " + lv[0] + ";");
         } else {
-          any_arg = true;
+          any_arg = true;  // folded by the butterfly below
           out.push_back(a + " = sm_" + a + tag + PB + "[tid & " + mask + "];");
-          out.push_back(a + "i = smi_" + a + tag + PB + "[tid & " + mask + "];");
+          if (t.arg) out.push_back(a + "i = smi_" + a + tag + PB + "[tid & " + mask + "];");
         }
       }
       if (any_arg) {
         out.push_back("#pragma unroll");
         out.push_back("for (int m_ = 1; m_ < " + std::to_string(NW) + "; m_ <<= 1) {");
         for (auto& [t, a] : accs) {
-          if (!t.arg) continue;
+          if (!t.arg && P.opt.xw_tree) continue;
+          if (!t.arg) {
+            out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); " + comb_stmt(t, a, "ov") + " }");
+            continue;
+          }
           out.push_back("  { const " + t.acc_t + " ov = fgt_shfl_xor(" + a + ", m_); const fgt_i64 oi = fgt_shfl_xor(" + a +
                         "i, m_); " + arg_stmt(t, a, a + "i", "ov", "oi") + " }");
         }

@@ -1286,6 +1286,7 @@ struct Planner {
     mix(opt.row_staging);
     mix(opt.lane_pairs);
     mix(opt.own_exp);
+    mix(opt.xw_tree);
     mix(opt.smem_cols);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);

@@ -467,6 +467,7 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
     if (const char* st = std::getenv("FGT_ROW_STAGING")) opt.row_staging = std::atoi(st) != 0;
     if (const char* lp = std::getenv("FGT_LANE_PAIRS")) opt.lane_pairs = std::atoi(lp) != 0;
     if (const char* ox = std::getenv("FGT_OWN_EXP")) opt.own_exp = std::atoi(ox) != 0;
+    if (const char* xs = std::getenv("FGT_XW_SHUFFLE")) opt.xw_tree = std::atoi(xs) == 0;
     bool row_elems_forced = options && options->row_elems > 0;
     if (const char* re = std::getenv("FGT_ROW_ELEMS")) {
       opt.row_elems = std::max(1, std::min(64, std::atoi(re)));
