@@ -143,7 +143,7 @@ struct Options {
   int lane_pairs = 1;             // element loops pair lanes for f32x2 arithmetic (FGT_LANE_PAIRS=0: one lane at a time)
   int occupancy_step = 0;         // row kernels: bound registers to fit one more CTA per SM when close (FGT_ROW_OCCUPANCY_STEP)
   int smem_cols = 0;              // row kernels: column accumulators in shared memory (FGT_ROW_SMEM_COLS)
-  int xw_tree = 1;                // cross-warp row reductions: tree over the warp partials (FGT_XW_SHUFFLE=1: butterfly)
+  int xw_tree = 1;                // cross-warp row reductions: tree over the warp partials (FGT_ROW_XW_SHUFFLE: butterfly)
   int own_exp = 1;                // exp in redoable row phases by fgt_exp_q, else expf (FGT_ROW_EXPF, or FGT_OWN_EXP=0)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
   int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)

@@ -33,13 +33,15 @@ from . import _fgt, ir
 # cluster barrier), so they are not candidates; the option stays available through the spec
 # options. Row flags (fgt_row_flag): 1 bounds a kernel's registers to fit one more CTA per SM
 # when it is close; 2 computes exp with CUDA's expf instead of the library's exp, whose extra
-# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers).
+# independent work can cost a CTA per SM (the bf16 softmax forward: 58 -> 79 registers); 8 folds
+# the warp partials of a row reduction with a shuffle butterfly instead of a tree read from shared
+# memory (faster for the LayerNorm forward, 0.93 -> 0.97 of peak, slower for the VJPs).
 # Flag 4 (column accumulators in shared memory) measured no faster on any benchmark partition (the
 # LayerNorm VJP keeps one CTA per SM at 169 registers, and two with the occupancy step spill), so it
 # is not a candidate. Candidates a flag leaves unchanged compile to the same source (kernel names
 # aside) and are timed once.
 _GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
-CANDIDATES = tuple(g + (f,) for f in (0, 1, 2) for g in _GEOMETRIES)
+CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 8) for g in _GEOMETRIES)
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 _lock = threading.Lock()
 

@@ -157,7 +157,10 @@ typedef enum fgt_row_flag {
   FGT_ROW_EXPF = 2,
   /* column-reduction accumulators in shared memory (one private slot per
    * thread and element) instead of registers */
-  FGT_ROW_SMEM_COLS = 4
+  FGT_ROW_SMEM_COLS = 4,
+  /* cross-warp row reductions by a shuffle butterfly over the warp partials,
+   * instead of every thread folding them from shared memory */
+  FGT_ROW_XW_SHUFFLE = 8
 } fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
