@@ -503,9 +503,23 @@ def run_only(args):
     import fugatensor_b200 as ft
     from fugatensor_b200 import workloads as W
     cfg, variant, dtype = args.only.split("/")
+    device = torch.device("cuda", 0)
+    if cfg == "index":
+        # index-transform workloads (gather_rows, scatter_add_rows, pad_concat) at their bench sizes
+        engine = ft.Engine("cuda:0", tune=False)
+        tt = W.index_inputs(variant, device)
+        t = {k: ft.Tensor(engine, W.INDEX_DTYPES[variant][k], tuple(v.shape), data=v) for k, v in tt.items()}
+        spec, desc, leaves, roots = engine.compile(*W.index_build(variant, t))
+        L = Launcher(spec, [l._data for l in leaves], device)
+        stream = torch.cuda.current_stream(device)
+        for _ in range(args.iters):
+            L(stream.cuda_stream)
+        torch.cuda.synchronize()
+        print(json.dumps({"only": args.only, "kernels": spec.kernel_count, "algorithmic_bytes": W.index_bytes(variant),
+                          "geometry": spec.execution_plan["cuda_lowering"]["kernels"]}), flush=True)
+        return
     rows, cols = W.FULL[cfg]
     rows = args.rows or rows
-    device = torch.device("cuda", 0)
     # --geometry e,r,c,f: that row geometry (no measured choice), so a capture
     # sees no tuning launches before the partition's own
     engine = ft.Engine("cuda:0", tune=args.geometry is None)
