@@ -1511,6 +1511,12 @@ struct Emitter {
     const int64_t RA = (g.nodes[K.scatter_node].shape[0] + 3) / 4 * 4;
     return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * RA * k) + "LL))";
   }
+  // the bucket-space cursor, after the update ids
+  std::string csr_cursor() const {
+    const Node& n = g.nodes[K.scatter_node];
+    const int64_t RA = (n.shape[0] + 3) / 4 * 4, NU = std::max<int64_t>(1, g.nodes[n.args[1]].n());
+    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * (3 * RA + NU)) + "LL))";
+  }
   // bucket sums: f64 for floats (rounded once with the base), unsigned
   // (wrapping) for integers
   std::string csr_acc_t() const {
@@ -1518,44 +1524,29 @@ struct Emitter {
     if (is_float(n.dt)) return "double";
     return n.dt == FGT_I64 ? "unsigned long long" : "unsigned int";
   }
-  // stage 13: exclusive scan of the R bucket counts into offsets, one CTA of
-  // 1024 threads, 16 consecutive counts per thread per step (four 16-byte
-  // loads issued together), warp shuffles over the thread totals, then over
-  // the warp totals, carrying the running total across steps
+  // stage 13: bucket offsets. A row's bucket only has to be a contiguous
+  // slot of the id array, in any place, so each warp takes 32 rows, scans
+  // their counts with shuffles and reserves one block for them from the
+  // cursor with a single atomicAdd (one atomic per 32 rows, all CTAs at
+  // once). The loop bound is uniform per warp: every lane reaches the
+  // shuffles.
   std::string build_scan() {
     const int64_t R = g.nodes[K.scatter_node].shape[0];
-    const int64_t RP = (R + 3) / 4 * 4;  // the counts array is read in int4 words up to here
     std::ostringstream o;
     o << args_struct();
-    o << "extern \"C\" __global__ void __launch_bounds__(1024) " << K.name << "(const FgtArgs p) {\n";
-    o << "  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;\n";
-    o << "  const fgt_i64 R = " << R << "LL, RP = " << RP << "LL;\n";
-    o << "  const int* cnt = " << csr_arr(0) << "; int* off = " << csr_arr(2) << ";\n";
-    o << "  __shared__ int wsum_[32];\n  int carry = 0;\n";
-    o << "  for (fgt_i64 base = 0; base < R; base += 16384) {\n";
-    o << "    int v[16]; int s = 0;\n";
-    o << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n";
-    o << "      const fgt_i64 i = base + (fgt_i64)tid * 16 + q * 4;\n";
-    o << "      int4 w = make_int4(0, 0, 0, 0);\n";
-    o << "      if (i < RP) w = *reinterpret_cast<const int4*>(cnt + i);\n";
-    o << "      v[q * 4] = i < R ? w.x : 0; v[q * 4 + 1] = i + 1 < R ? w.y : 0; v[q * 4 + 2] = i + 2 < R ? w.z : 0; v[q * 4 + 3] = i + 3 < R ? w.w : 0;\n";
-    o << "    }\n";
-    o << "    #pragma unroll\n    for (int j = 0; j < 16; ++j) s += v[j];\n";
-    o << "    int x = s;\n";
+    o << "extern \"C\" __global__ void __launch_bounds__(" << K.nt << ") " << K.name << "(const FgtArgs p) {\n";
+    o << "  const int lane = threadIdx.x & 31;\n";
+    o << "  const fgt_i64 R = " << R << "LL;\n";
+    o << "  const int* cnt = " << csr_arr(0) << "; int* off = " << csr_arr(2) << "; int* cursor = " << csr_cursor() << ";\n";
+    o << "  const fgt_i64 nw = (fgt_i64)gridDim.x * (blockDim.x >> 5);\n";
+    o << "  for (fgt_i64 w0 = ((fgt_i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; w0 < R; w0 += nw * 32) {\n";
+    o << "    const fgt_i64 i = w0 + lane;\n";
+    o << "    const int c = i < R ? cnt[i] : 0;\n";
+    o << "    int x = c;\n";
     o << "    #pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= d) x += y; }\n";
-    o << "    if (lane == 31) wsum_[wid] = x;\n    __syncthreads();\n";
-    o << "    if (wid == 0) {\n      int w = wsum_[lane];\n";
-    o << "      #pragma unroll\n      for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, w, d); if (lane >= d) w += y; }\n";
-    o << "      wsum_[lane] = w;\n    }\n    __syncthreads();\n";
-    o << "    int run = carry + (wid > 0 ? wsum_[wid - 1] : 0) + x - s;\n";
-    // offsets written as 16-byte words where the whole word is in range
-    o << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n";
-    o << "      const fgt_i64 i = base + (fgt_i64)tid * 16 + q * 4;\n";
-    o << "      int4 w; w.x = run; run += v[q * 4]; w.y = run; run += v[q * 4 + 1]; w.z = run; run += v[q * 4 + 2]; w.w = run; run += v[q * 4 + 3];\n";
-    o << "      if (i + 3 < R) *reinterpret_cast<int4*>(off + i) = w;\n";
-    o << "      else { if (i < R) off[i] = w.x; if (i + 1 < R) off[i + 1] = w.y; if (i + 2 < R) off[i + 2] = w.z; }\n";
-    o << "    }\n";
-    o << "    carry += wsum_[31];\n    __syncthreads();\n  }\n}\n";
+    o << "    int base = 0;\n    if (lane == 31) base = atomicAdd(cursor, x);\n";
+    o << "    base = __shfl_sync(0xffffffffu, base, 31);\n";
+    o << "    if (i < R) off[i] = base + x - c;\n  }\n}\n";
     return o.str();
   }
 
@@ -1569,7 +1560,8 @@ struct Emitter {
     std::vector<std::pair<RedText, std::string>> accs;
     std::vector<std::string> partial_store;
     if (K.scatter_stage == 1) lane[0].push_back(scatter_acc_ptr() + "[e] = 0;");
-    if (K.scatter_stage == 11) lane[0].push_back(csr_arr(0) + "[e] = 0; " + csr_arr(1) + "[e] = 0;");
+    if (K.scatter_stage == 11)
+      lane[0].push_back(csr_arr(0) + "[e] = 0; " + csr_arr(1) + "[e] = 0; if (e == 0) " + csr_cursor() + "[0] = 0;");
     if (K.scatter_stage == 12 || K.scatter_stage == 14) {
       // over the indices: count each in-range index's update, then place its
       // id in the row's bucket (a cursor per row; order within a bucket free)

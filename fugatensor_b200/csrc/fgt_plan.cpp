@@ -671,9 +671,11 @@ struct Planner {
     const int acc_bytes = is_float(n.dt) ? 8 : dtype_size(n.dt);
     const int64_t R = base.rank() >= 1 ? base.shape[0] : 1, NU = g.nodes[n.args[1]].n();
     // CSR arrays: counts, cursors and offsets of RA = R rounded up to 4 ints
-    // each (every array 16-byte aligned), then one update id per index
+    // each (every array 16-byte aligned), one update id per index, then the
+    // cursor that hands out bucket space
     const int64_t RA = (R + 3) / 4 * 4;
-    const int64_t acc = csr ? alloc((3 * RA + std::max<int64_t>(1, NU)) * 4) : alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
+    const int64_t acc = csr ? alloc((3 * RA + std::max<int64_t>(1, NU) + 1) * 4)
+                            : alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
     auto make = [&](const Shape& shape, int stage) {
       KernelDef k;
       k.kind = KKind::ELEM;
@@ -710,10 +712,8 @@ struct Planner {
       plan.kernels.push_back(z);
       if (NU > 0) plan.kernels.push_back(indices_kernel(12));
       KernelDef sc = make(Shape{R}, 13);
-      sc.nt = 1024;
-      sc.tpr = 1024;
       sc.vec = 1;
-      sc.max_ctas = 1;
+      geometry_elem(sc);
       plan.kernels.push_back(sc);
       if (NU > 0) plan.kernels.push_back(indices_kernel(14));
     }

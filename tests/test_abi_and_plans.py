@@ -236,14 +236,14 @@ def test_column_reductions_over_long_rows_plan_as_tiles():
 
 def test_row_scatter_plans_as_counting_sort():
     """scatter_add along axis 0 with 1-D indices and materialised updates takes
-    the counting-sort form (zero, count, scan on one CTA, fill, bucket sums);
+    the counting-sort form (zero, count, bucket allocation, fill, bucket sums);
     other scatters keep the atomic accumulator form."""
     from fugatensor_b200 import _fgt
     g = ir.Graph()
     b, i, u = g.parameter("f32", (1000, 64)), g.parameter("i32", (300,)), g.parameter("f32", (300, 64))
     s = _fgt.Spec(g.descriptor([g.scatter_add(b, i, u, 0)]))
     ks = s.execution_plan["cuda_lowering"]["kernels"]
-    assert len(ks) == 5 and ks[2]["threads"] == 1024
+    assert len(ks) == 5 and "atomicAdd(cursor" in s.kernel_source(2)
     assert "atomicAdd" not in s.kernel_source(4) and "fgt_vload_keep(uv_" in s.kernel_source(4)
     # along axis 1: the accumulator form
     g = ir.Graph()
