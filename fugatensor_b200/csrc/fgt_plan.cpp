@@ -522,13 +522,21 @@ Level Analyzer::compute(int id, const Map& m) {
     return join(L, of_idx(to_linear(m, n.shape, d)));
   }
   if (loc[id].kind != Loc::NONE) {
-    Level L = of_idx(to_linear(m, n.shape, d));
+    const Idx A = to_linear(m, n.shape, d);
+    Level L = of_idx(A);
     if (!m.guard.empty()) {
       // a predicated element load is computed where its guard is known
       if (m.gdep_o) L.kind |= 1;
       if (m.gdep_i) L.kind |= 2;
     }
-    if (L.kind & 2) loads.insert(id);
+    if (L.kind & 2) {
+      loads.insert(id);
+      // guarded loads are read one element at a time, and a load that does
+      // not move with the innermost digit is read once per chunk: neither
+      // limits the vector width
+      const bool inner = !A.aff || (d.nd() > 0 && (int)A.c.size() == d.nd() && A.c[d.nd() - 1] != 0);
+      if (m.guard.empty() && inner) vec_loads.insert(id);
+    }
     return L;
   }
   switch (n.op) {
@@ -745,7 +753,7 @@ struct Planner {
       } catch (NotFusible&) {
         fail(FGT_ERR_UNSUPPORTED, "internal: scatter_add operands not evaluable");
       }
-      choose_vec(k2, an.loads, {});
+      choose_vec(k2, an.vec_loads, {});
       geometry_elem(k2);
       plan.kernels.push_back(k2);
     }
@@ -779,7 +787,7 @@ struct Planner {
       k3.stores.push_back(st);
       outs.push_back(s);
     }
-    choose_vec(k3, an.loads, outs);
+    choose_vec(k3, an.vec_loads, outs);
     geometry_elem(k3);
     plan.kernels.push_back(k3);
     loc[s] = L;
@@ -935,7 +943,7 @@ struct Planner {
         outs.push_back(o);
         done_outputs.insert(o);
       }
-      choose_vec(k, an.loads, outs);
+      choose_vec(k, an.vec_loads, outs);
       geometry_elem(k);
       plan.kernels.push_back(k);
     }
@@ -1010,6 +1018,7 @@ struct Planner {
     // Re-run the analysis of the final group to collect loads.
     an.memo.clear();
     an.loads.clear();
+    an.vec_loads.clear();
     for (auto& rd : reds) an.run(g.nodes[rd.node].args[0], rd.opmap);
     bool has_col = false, has_full = false;
     for (auto& rd : reds) {
@@ -1107,7 +1116,7 @@ struct Planner {
     std::vector<int> eo;
     for (auto& st : k.stores)
       if (st.level == 0) eo.push_back(st.node);
-    choose_vec(k, an.loads, eo);
+    choose_vec(k, an.vec_loads, eo);
     if (k.kind == KKind::ROW) geometry_row(k);
     else geometry_elem(k);
     // Column reductions need register accumulators per element, so not in

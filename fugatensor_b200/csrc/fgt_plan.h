@@ -195,6 +195,8 @@ struct Analyzer {
   std::map<std::string, Level> memo;
   std::map<int, int> red_phase;        // row reduction -> element loop it runs in
   std::set<int> loads;                 // nodes loaded with in-row dependence
+  std::set<int> vec_loads;             // of those, the unguarded ones whose address moves with the innermost
+                                       // digit: the only loads that may be read as vectors
   Analyzer(const Graph& g_, const std::vector<Loc>& l, KKind k, const Domain& d_) : g(g_), loc(l), kind(k), d(d_) {}
   Level run(int id, const Map& m);
 
