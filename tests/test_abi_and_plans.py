@@ -255,3 +255,19 @@ def test_row_scatter_plans_as_counting_sort():
     b, i, u = g.parameter("f32", (1000, 64)), g.parameter("i32", (300,)), g.parameter("f32", (300, 64))
     s = _fgt.Spec(g.descriptor([g.scatter_add(b, i, g.mul(u, u), 0)]))
     assert s.kernel_count == 3
+
+
+def test_vector_width_ignores_per_row_and_guarded_loads():
+    """The vector width follows the loads that can be vector loads: a row gather
+    of f32 rows with i64 indices (one index per row, guarded element reads)
+    runs at 4 elements per chunk, not the 2 an 8-byte load would allow."""
+    from fugatensor_b200 import _fgt
+    g = ir.Graph()
+    t, i = g.parameter("f32", (1000, 512)), g.parameter("i64", (300,))
+    s = _fgt.Spec(g.descriptor([g.gather(t, i, 0)]))
+    assert [k["vector"] for k in s.execution_plan["cuda_lowering"]["kernels"]] == [4]
+    # a contiguous i64 operand still limits the width to two 8-byte elements
+    g = ir.Graph()
+    a, b = g.parameter("i64", (1000, 512)), g.parameter("f32", (1000, 512))
+    s = _fgt.Spec(g.descriptor([g.add(g.cast(a, "f32"), b)]))
+    assert [k["vector"] for k in s.execution_plan["cuda_lowering"]["kernels"]] == [2]
