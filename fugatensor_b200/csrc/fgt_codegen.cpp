@@ -1080,10 +1080,24 @@ struct Emitter {
       s += "const fgt_i64 o" + std::to_string(k) + " = (r / " + std::to_string(d.ow[k]) + "LL) % " + std::to_string(d.od[k]) + "LL; ";
     return s;
   }
-  std::string digits_i() {
+  // Element digits. When the innermost extent is a whole number of vector
+  // chunks, every element of the chunk at e0 shares its outer digits and the
+  // innermost one is e0's plus the lane offset `vv`; the digits are then taken
+  // from e0 (unsigned: e0 >= 0), which the unrolled lanes share.
+  bool chunk_digits() const {
+    return !d.id.empty() && d.iw.back() == 1 && K.vec > 1 && d.id.back() % K.vec == 0;
+  }
+  std::string digits_i(bool from_e0 = false, const std::string& vv = "v") {
     std::string s;
-    for (int k = 0; k < (int)d.id.size(); ++k)
-      s += "const fgt_i64 i" + std::to_string(k) + " = (e / " + std::to_string(d.iw[k]) + "LL) % " + std::to_string(d.id[k]) + "LL; ";
+    const int n = (int)d.id.size();
+    for (int k = 0; k < n; ++k) {
+      const std::string w = std::to_string(d.iw[k]), m = std::to_string(d.id[k]);
+      if (from_e0 && chunk_digits())
+        s += "const fgt_i64 i" + std::to_string(k) + " = (fgt_i64)(((unsigned long long)e0 / " + w + "ULL) % " + m +
+             "ULL)" + (k == n - 1 ? " + " + vv : std::string()) + "; ";
+      else
+        s += "const fgt_i64 i" + std::to_string(k) + " = (e / " + w + "LL) % " + m + "LL; ";
+    }
     return s;
   }
 
@@ -1313,7 +1327,7 @@ struct Emitter {
       o << "    " << CHK << " {\n";
       put(o, prosites, "      ");
       o << "      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
-      o << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+      o << "        const fgt_i64 e = e0 + v; " << digits_i(true) << "\n";
       put(o, prolane, "        ");
       o << "      }\n    }\n  }\n";
     }
@@ -1426,7 +1440,7 @@ struct Emitter {
         put(o, pair_body(body), ind + "        ");
       } else {
         o << ind << "      for (int v = 0; v < " << VEC << "; ++v) {\n";
-        o << ind << "        const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+        o << ind << "        const fgt_i64 e = e0 + v; " << digits_i(true) << "\n";
         put(o, body, ind + "        ");
       }
       o << ind << "      }\n";
@@ -1669,7 +1683,7 @@ struct Emitter {
       put(o, pair_body(lane[0]), "          ");
     } else {
       o << "        for (int v = 0; v < " << VEC << "; ++v) {\n";
-      o << "          const fgt_i64 e = e0 + v; " << digits_i() << "\n";
+      o << "          const fgt_i64 e = e0 + v; " << digits_i(true) << "\n";
       put(o, lane[0], "          ");
     }
     o << "        }\n";
@@ -2027,11 +2041,11 @@ struct Emitter {
   }
   // loop header over lane pairs (slot b's element index and digits included)
   std::string pair_header(const std::string& vec) {
-    std::string dg = digits_i(), db;
-    for (auto& t : tokens(dg)) db += (t.ident && (t.s == "e" || (t.s.size() > 1 && t.s[0] == 'i' &&
-                                                                   std::isdigit((unsigned char)t.s[1]))))
-                                        ? t.s + "_b"
-                                        : t.s;
+    std::string dg = digits_i(true), db;
+    for (auto& t : tokens(digits_i(true, "(v + 1)")))
+      db += (t.ident && (t.s == "e" || (t.s.size() > 1 && t.s[0] == 'i' && std::isdigit((unsigned char)t.s[1]))))
+                ? t.s + "_b"
+                : t.s;
     return "for (int v = 0; v < " + vec + "; v += 2) {\n" + "const fgt_i64 e = e0 + v; " + dg + "\n" +
            "const fgt_i64 e_b = e0 + v + 1; " + db + " (void)e_b;\n";
   }
