@@ -271,3 +271,16 @@ def test_vector_width_ignores_per_row_and_guarded_loads():
     a, b = g.parameter("i64", (1000, 512)), g.parameter("f32", (1000, 512))
     s = _fgt.Spec(g.descriptor([g.add(g.cast(a, "f32"), b)]))
     assert [k["vector"] for k in s.execution_plan["cuda_lowering"]["kernels"]] == [2]
+
+
+def test_digits_taken_once_per_chunk():
+    """When the innermost extent is a whole number of vector chunks the element
+    digits come from the chunk's first element; otherwise each element divides."""
+    from fugatensor_b200 import _fgt
+    def src(cols):
+        g = ir.Graph()
+        x = g.parameter("f32", (64, cols))
+        r = g.slice(x, (0, cols - 1), (64, -1), (1, -1))
+        return _fgt.Spec(g.descriptor([g.concatenate([x, r], 1)])).kernel_source(0)
+    assert "(unsigned long long)e0" in src(256)
+    assert "(unsigned long long)e0" not in src(255)
