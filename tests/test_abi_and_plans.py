@@ -284,3 +284,23 @@ def test_digits_taken_once_per_chunk():
         return _fgt.Spec(g.descriptor([g.concatenate([x, r], 1)])).kernel_source(0)
     assert "(unsigned long long)e0" in src(256)
     assert "(unsigned long long)e0" not in src(255)
+
+
+def test_chunk_digit_rule_matches_per_element_digits():
+    """The per-chunk digit rule the generator uses: with the innermost extent a
+    whole number of vector chunks (innermost weight 1), the digits of element
+    e0 + v equal e0's outer digits and e0's innermost digit plus v."""
+    import numpy as np
+    rng = np.random.default_rng(3)
+    for _ in range(200):
+        vec = int(rng.choice([2, 4, 8]))
+        dims = [int(rng.integers(1, 7)) for _ in range(int(rng.integers(1, 4)))]
+        dims.append(vec * int(rng.integers(1, 9)))
+        weights = [int(np.prod(dims[k + 1:])) for k in range(len(dims))]
+        n = int(np.prod(dims))
+        for e0 in range(0, n, vec):
+            for v in range(vec):
+                full = [((e0 + v) // w) % m for w, m in zip(weights, dims)]
+                chunk = [(e0 // w) % m for w, m in zip(weights, dims)]
+                chunk[-1] += v
+                assert full == chunk
