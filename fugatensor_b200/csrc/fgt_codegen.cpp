@@ -1090,11 +1090,16 @@ struct Emitter {
   std::string digits_i(bool from_e0 = false, const std::string& vv = "v") {
     std::string s;
     const int n = (int)d.id.size();
+    // digits below 2^30 are 32-bit values: the guards and offsets built on
+    // them then compare and add in 32 bits where the compiler can narrow them
+    bool narrow = true;
+    for (int64_t m : d.id) narrow = narrow && m < (int64_t(1) << 30);
     for (int k = 0; k < n; ++k) {
       const std::string w = std::to_string(d.iw[k]), m = std::to_string(d.id[k]);
       if (from_e0 && chunk_digits())
-        s += "const fgt_i64 i" + std::to_string(k) + " = (fgt_i64)(((unsigned long long)e0 / " + w + "ULL) % " + m +
-             "ULL)" + (k == n - 1 ? " + " + vv : std::string()) + "; ";
+        s += std::string(narrow ? "const int i" : "const fgt_i64 i") + std::to_string(k) + " = (" +
+             (narrow ? "int" : "fgt_i64") + ")(((unsigned long long)e0 / " + w + "ULL) % " + m + "ULL)" +
+             (k == n - 1 ? " + " + vv : std::string()) + "; ";
       else
         s += "const fgt_i64 i" + std::to_string(k) + " = (e / " + w + "LL) % " + m + "LL; ";
     }
