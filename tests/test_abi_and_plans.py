@@ -284,6 +284,8 @@ def test_digits_taken_once_per_chunk():
         return _fgt.Spec(g.descriptor([g.concatenate([x, r], 1)])).kernel_source(0)
     assert "(unsigned long long)e0" in src(256)
     assert "(unsigned long long)e0" not in src(255)
+    # extents below 2^30: the digits are 32-bit values
+    assert "const int i0 = (int)(((unsigned long long)e0" in src(256)
 
 
 def test_chunk_digit_rule_matches_per_element_digits():
