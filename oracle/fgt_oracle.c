@@ -303,8 +303,9 @@ static void cast_one(const Buf* x, int64_t i, Buf* o, int64_t j) {
     return;
   }
   if (is_float(to)) {
-    long double v = is_float(from) ? (long double)((float*)x->v)[i] : (long double)geti(x, i);
-    ((float*)o->v)[j] = rnd_dt(v, to);
+    /* a float source is an exact f32 value: the f32-input rounding is exact */
+    if (is_float(from)) ((float*)o->v)[j] = rnd_f(((float*)x->v)[i], to);
+    else ((float*)o->v)[j] = rnd_dt((long double)geti(x, i), to);
     return;
   }
   if (is_float(from)) {
@@ -331,112 +332,240 @@ static int arg_better(int is_max, int fl, long double a, int64_t ia, long double
   return ia < ib;
 }
 
-static int eval_reduce(const fgt_node* nd, const Buf* x, Buf* o, int mode) {
+/* Partial state of one reduction over a range of its reduced elements. */
+typedef struct {
+  long double accd;
+  float accf;
+  int64_t acci;
+  int have;
+  long double best;
+  int64_t besti;
+  float mf;
+  int64_t mi;
+  int bacc;
+} RedPart;
+
+typedef struct {
+  const fgt_node* nd;
+  const Buf* x;
+  int mode, fl, nr, trailing;
+  int isred[FGT_MAX_RANK];
+  int64_t xs[FGT_MAX_RANK], red[FGT_MAX_RANK], rstride0;
+} RedCtx;
+
+static void red_init(const RedCtx* c, RedPart* p) {
+  const int op = c->nd->opcode;
+  p->accd = op == FGT_OP_REDUCE_PROD ? 1.0L : 0.0L;
+  p->accf = op == FGT_OP_REDUCE_PROD ? 1.0f : 0.0f;
+  p->acci = op == FGT_OP_REDUCE_PROD ? 1 : 0;
+  p->have = 0;
+  p->best = 0;
+  p->besti = 0;
+  p->mf = 0;
+  p->mi = 0;
+  p->bacc = op == FGT_OP_REDUCE_ALL ? 1 : 0;
+}
+
+/* Offset of reduced element ri (row-major over the reduced axes) from the
+ * kept coordinates' base. One reduced axis and trailing contiguous reduced
+ * axes (every benchmark partition) take the direct forms. */
+static int64_t red_off(const RedCtx* c, int64_t base, int64_t ri) {
+  if (c->nr == 1) return base + ri * c->rstride0;
+  if (c->trailing) return base + ri;
+  int64_t rc[FGT_MAX_RANK];
+  unravel(ri, c->red, c->nr, rc);
+  int64_t off = base;
+  int t = 0;
+  for (int k = 0; k < c->x->rank; ++k)
+    if (c->isred[k]) off += rc[t++] * c->xs[k];
+  return off;
+}
+
+/* Fold reduced elements [lo, hi) into p, left to right. */
+static void red_range(const RedCtx* c, int64_t base, int64_t lo, int64_t hi, RedPart* p) {
+  const int op = c->nd->opcode, fl = c->fl, mode = c->mode;
+  const Buf* x = c->x;
+  for (int64_t ri = lo; ri < hi; ++ri) {
+    const int64_t off = red_off(c, base, ri);
+    switch (op) {
+      case FGT_OP_REDUCE_SUM:
+      case FGT_OP_REDUCE_PROD:
+        if (fl) {
+          float v = ((float*)x->v)[off];
+          if (mode == MODE_ACCURATE)
+            p->accd = op == FGT_OP_REDUCE_SUM ? p->accd + (double)v : (long double)((double)p->accd * (double)v);
+          else p->accf = rnd_f(op == FGT_OP_REDUCE_SUM ? p->accf + v : p->accf * v, x->dt);
+        } else {
+          int64_t v = geti(x, off);
+          p->acci = wrap(op == FGT_OP_REDUCE_SUM ? (int64_t)((uint64_t)p->acci + (uint64_t)v)
+                                                 : (int64_t)((uint64_t)p->acci * (uint64_t)v), x->dt);
+        }
+        break;
+      case FGT_OP_REDUCE_MAX:
+      case FGT_OP_REDUCE_MIN:
+        if (fl) {
+          float v = ((float*)x->v)[off];
+          p->mf = !p->have ? v : (op == FGT_OP_REDUCE_MAX ? fmax_ieee(p->mf, v) : fmin_ieee(p->mf, v));
+        } else {
+          int64_t v = geti(x, off);
+          p->mi = !p->have ? v : (op == FGT_OP_REDUCE_MAX ? (v > p->mi ? v : p->mi) : (v < p->mi ? v : p->mi));
+        }
+        p->have = 1;
+        break;
+      case FGT_OP_REDUCE_ANY: p->bacc = p->bacc || ((uint8_t*)x->v)[off]; break;
+      case FGT_OP_REDUCE_ALL: p->bacc = p->bacc && ((uint8_t*)x->v)[off]; break;
+      case FGT_OP_ARGMAX:
+      case FGT_OP_ARGMIN: {
+        /* one reduced axis: the index along it is ri */
+        long double v = getf(x, off);
+        if (!p->have || arg_better(op == FGT_OP_ARGMAX, fl, v, ri, p->best, p->besti)) {
+          p->best = v;
+          p->besti = ri;
+        }
+        p->have = 1;
+        break;
+      }
+    }
+  }
+}
+
+/* p <- p followed by q (q covers the elements after p's). Only for the
+ * reductions red_splittable() admits, where this equals one left-to-right
+ * fold up to the rounding of the long double sum. */
+static void red_merge(const RedCtx* c, RedPart* p, const RedPart* q) {
+  const int op = c->nd->opcode, fl = c->fl;
+  switch (op) {
+    case FGT_OP_REDUCE_SUM:
+      if (fl) p->accd = p->accd + q->accd;
+      else p->acci = wrap((int64_t)((uint64_t)p->acci + (uint64_t)q->acci), c->x->dt);
+      break;
+    case FGT_OP_REDUCE_PROD: p->acci = wrap((int64_t)((uint64_t)p->acci * (uint64_t)q->acci), c->x->dt); break;
+    case FGT_OP_REDUCE_MAX:
+    case FGT_OP_REDUCE_MIN:
+      if (!q->have) break;
+      if (!p->have) {
+        p->mf = q->mf;
+        p->mi = q->mi;
+      } else if (fl) p->mf = op == FGT_OP_REDUCE_MAX ? fmax_ieee(p->mf, q->mf) : fmin_ieee(p->mf, q->mf);
+      else p->mi = op == FGT_OP_REDUCE_MAX ? (q->mi > p->mi ? q->mi : p->mi) : (q->mi < p->mi ? q->mi : p->mi);
+      p->have = 1;
+      break;
+    case FGT_OP_REDUCE_ANY: p->bacc = p->bacc || q->bacc; break;
+    case FGT_OP_REDUCE_ALL: p->bacc = p->bacc && q->bacc; break;
+    case FGT_OP_ARGMAX:
+    case FGT_OP_ARGMIN:
+      if (q->have && (!p->have || arg_better(op == FGT_OP_ARGMAX, fl, q->best, q->besti, p->best, p->besti))) {
+        p->best = q->best;
+        p->besti = q->besti;
+      }
+      p->have = p->have || q->have;
+      break;
+  }
+}
+
+/* Reductions whose result does not depend on how the range is split:
+ * integer sums/products (wrapping arithmetic is associative), max/min,
+ * arg-reductions (index tie-break), any/all, and ACCURATE float sums (long
+ * double partials; the split changes only bits far below the f64 result that
+ * is rounded once). LITERAL float sums fix a left-to-right order and float
+ * products a double-rounding order, so they stay sequential. */
+static int red_splittable(const RedCtx* c) {
+  const int op = c->nd->opcode;
+  if (op == FGT_OP_REDUCE_PROD) return !c->fl;
+  if (op == FGT_OP_REDUCE_SUM) return !c->fl || c->mode == MODE_ACCURATE;
+  return 1;
+}
+
+#define RED_CHUNK ((int64_t)1 << 20)
+/* loops over fewer elements than this run on the calling thread */
+#define PAR_MIN ((int64_t)1 << 15)
+
+static int eval_reduce(const fgt_node* nd, const Buf* x, Buf* o, int mode, int threads) {
+  RedCtx c;
+  memset(&c, 0, sizeof c);
+  c.nd = nd;
+  c.x = x;
+  c.mode = mode;
+  c.fl = is_float(x->dt);
   int axes[FGT_MAX_RANK] = {0};
   int nax = 0;
-  int isred[FGT_MAX_RANK] = {0};
   if (nd->opcode == FGT_OP_ARGMAX || nd->opcode == FGT_OP_ARGMIN) {
     axes[0] = (int)nd->attrs[0];
     nax = 1;
   } else {
     for (int k = 0; k < nd->num_attrs; ++k) axes[nax++] = (int)nd->attrs[k];
   }
-  for (int k = 0; k < nax; ++k) isred[axes[k]] = 1;
-  int64_t xs[FGT_MAX_RANK];
-  strides(x->shape, x->rank, xs);
-  int64_t kept[FGT_MAX_RANK], red[FGT_MAX_RANK];
-  int nk = 0, nr = 0;
+  for (int k = 0; k < nax; ++k) c.isred[axes[k]] = 1;
+  strides(x->shape, x->rank, c.xs);
+  int64_t kept[FGT_MAX_RANK];
+  int nk = 0;
   for (int k = 0; k < x->rank; ++k) {
-    if (isred[k]) red[nr++] = x->shape[k];
-    else kept[nk++] = x->shape[k];
+    if (c.isred[k]) {
+      if (c.nr == 0) c.rstride0 = c.xs[k];
+      c.red[c.nr++] = x->shape[k];
+    } else kept[nk++] = x->shape[k];
   }
-  int64_t nred = numel(red, nr);
+  c.trailing = 1;
+  for (int k = x->rank - c.nr; k < x->rank; ++k)
+    if (k < 0 || !c.isred[k]) c.trailing = 0;
+  const int64_t nred = numel(c.red, c.nr);
   const int op = nd->opcode;
-  const int fl = is_float(x->dt);
+  const int64_t nchunks = (nred + RED_CHUNK - 1) / RED_CHUNK;
+  /* one output over a long range (a whole-tensor reduction): split the range
+   * into fixed chunks, folded in parallel and merged in order (the result does
+   * not depend on the thread count); otherwise one output per iteration */
+  const int split = red_splittable(&c) && nchunks > 1 && o->n == 1;
+  RedPart whole;
+  red_init(&c, &whole);
+  if (split) {
+    RedPart* parts = (RedPart*)malloc(sizeof(RedPart) * (size_t)nchunks);
+    if (!parts) return 1;
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 1)
+    for (int64_t q = 0; q < nchunks; ++q) {
+      red_init(&c, &parts[q]);
+      const int64_t hi = (q + 1) * RED_CHUNK < nred ? (q + 1) * RED_CHUNK : nred;
+      red_range(&c, 0, q * RED_CHUNK, hi, &parts[q]);
+    }
+    for (int64_t q = 1; q < nchunks; ++q) red_merge(&c, &parts[0], &parts[q]);
+    whole = parts[0];
+    free(parts);
+  }
+#pragma omp parallel for num_threads(threads) schedule(static) if (!split && o->n > 1)
   for (int64_t oi = 0; oi < o->n; ++oi) {
-    int64_t oc[FGT_MAX_RANK], rc[FGT_MAX_RANK];
-    unravel(oi, kept, nk, oc);
-    /* base offset from kept coords */
-    int64_t base = 0;
-    {
+    RedPart p;
+    if (split) {
+      p = whole;
+    } else {
+      int64_t oc[FGT_MAX_RANK];
+      unravel(oi, kept, nk, oc);
+      int64_t base = 0;
       int t = 0;
       for (int k = 0; k < x->rank; ++k)
-        if (!isred[k]) base += oc[t++] * xs[k];
-    }
-    long double accd = op == FGT_OP_REDUCE_PROD ? 1.0L : 0.0L;
-    float accf = op == FGT_OP_REDUCE_PROD ? 1.0f : 0.0f;
-    int64_t acci = op == FGT_OP_REDUCE_PROD ? 1 : 0;
-    int have = 0;
-    long double best = 0;
-    int64_t besti = 0;
-    float mf = 0;
-    int64_t mi = 0;
-    int bacc = op == FGT_OP_REDUCE_ALL ? 1 : 0;
-    for (int64_t ri = 0; ri < nred; ++ri) {
-      unravel(ri, red, nr, rc);
-      int64_t off = base;
-      {
-        int t = 0;
-        for (int k = 0; k < x->rank; ++k)
-          if (isred[k]) off += rc[t++] * xs[k];
-      }
-      switch (op) {
-        case FGT_OP_REDUCE_SUM:
-        case FGT_OP_REDUCE_PROD:
-          if (fl) {
-            float v = ((float*)x->v)[off];
-            if (mode == MODE_ACCURATE) accd = op == FGT_OP_REDUCE_SUM ? accd + (double)v : (long double)((double)accd * (double)v);
-            else accf = rnd_f(op == FGT_OP_REDUCE_SUM ? accf + v : accf * v, x->dt);
-          } else {
-            int64_t v = geti(x, off);
-            acci = wrap(op == FGT_OP_REDUCE_SUM ? (int64_t)((uint64_t)acci + (uint64_t)v) : (int64_t)((uint64_t)acci * (uint64_t)v), x->dt);
-          }
-          break;
-        case FGT_OP_REDUCE_MAX:
-        case FGT_OP_REDUCE_MIN:
-          if (fl) {
-            float v = ((float*)x->v)[off];
-            mf = !have ? v : (op == FGT_OP_REDUCE_MAX ? fmax_ieee(mf, v) : fmin_ieee(mf, v));
-          } else {
-            int64_t v = geti(x, off);
-            mi = !have ? v : (op == FGT_OP_REDUCE_MAX ? (v > mi ? v : mi) : (v < mi ? v : mi));
-          }
-          have = 1;
-          break;
-        case FGT_OP_REDUCE_ANY: bacc = bacc || ((uint8_t*)x->v)[off]; break;
-        case FGT_OP_REDUCE_ALL: bacc = bacc && ((uint8_t*)x->v)[off]; break;
-        case FGT_OP_ARGMAX:
-        case FGT_OP_ARGMIN: {
-          long double v = getf(x, off);
-          if (!have || arg_better(op == FGT_OP_ARGMAX, fl, v, rc[0], best, besti)) {
-            best = v;
-            besti = rc[0];
-          }
-          have = 1;
-          break;
-        }
-      }
+        if (!c.isred[k]) base += oc[t++] * c.xs[k];
+      red_init(&c, &p);
+      red_range(&c, base, 0, nred, &p);
     }
     switch (op) {
       case FGT_OP_REDUCE_SUM:
       case FGT_OP_REDUCE_PROD:
-        if (fl) ((float*)o->v)[oi] = mode == MODE_ACCURATE ? rnd_dt((long double)(double)accd, x->dt) : accf;
-        else put_int(o, oi, acci);
+        if (c.fl) ((float*)o->v)[oi] = mode == MODE_ACCURATE ? rnd_dt((long double)(double)p.accd, x->dt) : p.accf;
+        else put_int(o, oi, p.acci);
         break;
       case FGT_OP_REDUCE_MAX:
       case FGT_OP_REDUCE_MIN:
-        if (fl) ((float*)o->v)[oi] = mf;
-        else put_int(o, oi, mi);
+        if (c.fl) ((float*)o->v)[oi] = p.mf;
+        else put_int(o, oi, p.mi);
         break;
       case FGT_OP_REDUCE_ANY:
-      case FGT_OP_REDUCE_ALL: ((uint8_t*)o->v)[oi] = (uint8_t)bacc; break;
-      default: ((int64_t*)o->v)[oi] = besti; break;
+      case FGT_OP_REDUCE_ALL: ((uint8_t*)o->v)[oi] = (uint8_t)p.bacc; break;
+      default: ((int64_t*)o->v)[oi] = p.besti; break;
     }
   }
   return 0;
 }
 
-static void load_input(Buf* b, const void* src) {
+static void load_input(Buf* b, const void* src, int threads) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (b->n >= PAR_MIN)
   for (int64_t i = 0; i < b->n; ++i) {
     switch (b->dt) {
       case FGT_BOOL: ((uint8_t*)b->v)[i] = ((const uint8_t*)src)[i] != 0; break;
@@ -448,7 +577,8 @@ static void load_input(Buf* b, const void* src) {
     }
   }
 }
-static void store_output(const Buf* b, void* dst) {
+static void store_output(const Buf* b, void* dst, int threads) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (b->n >= PAR_MIN)
   for (int64_t i = 0; i < b->n; ++i) {
     switch (b->dt) {
       case FGT_BOOL: ((uint8_t*)dst)[i] = ((uint8_t*)b->v)[i]; break;
@@ -472,9 +602,37 @@ static float const_value_f(int dt, uint64_t bits) {
   return bf16_decode((uint16_t)bits);
 }
 
-/* Evaluate a partition: mode 0 literal, 1 accurate. Returns 0 on success. */
-int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* inputs, void* const* outputs, char* err,
-                    size_t errcap) {
+/* o[j] = a[off(j)] with off(j) = sum_k coord_k(j) * step[k]: one unravel per
+ * run of the innermost output axis, then a strided walk. */
+static void gather_runs(const Buf* a, Buf* o, const int64_t* step, int threads) {
+  const int r = o->rank;
+  const int64_t inner = r ? o->shape[r - 1] : 1;
+  const int64_t runs = inner ? o->n / inner : 0;
+  const int64_t istep = r ? step[r - 1] : 0;
+  const size_t w = vsize(o->dt);
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
+  for (int64_t q = 0; q < runs; ++q) {
+    int64_t cc[FGT_MAX_RANK];
+    unravel(q * inner, o->shape, r, cc);
+    int64_t off = 0;
+    for (int k = 0; k + 1 < r; ++k) off += cc[k] * step[k];
+    char* dst = (char*)o->v + (size_t)(q * inner) * w;
+    const char* src = (const char*)a->v;
+    if (w == 4) {
+      for (int64_t i = 0; i < inner; ++i) ((uint32_t*)dst)[i] = ((const uint32_t*)src)[off + i * istep];
+    } else if (w == 8) {
+      for (int64_t i = 0; i < inner; ++i) ((uint64_t*)dst)[i] = ((const uint64_t*)src)[off + i * istep];
+    } else {
+      for (int64_t i = 0; i < inner; ++i) dst[i] = src[off + i * istep];
+    }
+  }
+}
+
+/* Evaluate a partition: mode 0 literal, 1 accurate, on `threads` threads
+ * (every result is independent of the thread count). Returns 0 on success. */
+static int eval_impl(const fgt_partition_desc* d, int mode, const void* const* inputs, void* const* outputs, char* err,
+                     size_t errcap, int threads) {
+  if (threads < 1) threads = 1;
   const int N = d->num_nodes;
   Buf* B = (Buf*)calloc((size_t)N, sizeof(Buf));
   int* last = (int*)malloc(sizeof(int) * (size_t)N);
@@ -507,7 +665,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
     int64_t os[FGT_MAX_RANK], as[FGT_MAX_RANK], cc[FGT_MAX_RANK], xc[FGT_MAX_RANK];
     strides(o->shape, o->rank, os);
     switch (op) {
-      case FGT_OP_PARAMETER: load_input(o, inputs[nd->attrs[0]]); break;
+      case FGT_OP_PARAMETER: load_input(o, inputs[nd->attrs[0]], threads); break;
       case FGT_OP_CONSTANT:
         if (is_float(o->dt)) ((float*)o->v)[0] = const_value_f(o->dt, nd->constant_bits);
         else if (o->dt == FGT_I32) ((int32_t*)o->v)[0] = (int32_t)(uint32_t)nd->constant_bits;
@@ -515,29 +673,29 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
         else ((uint8_t*)o->v)[0] = (nd->constant_bits & 0xff) != 0;
         break;
       case FGT_OP_SPLAT:
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
         for (int64_t j = 0; j < o->n; ++j) memcpy((char*)o->v + j * vsize(o->dt), a->v, vsize(o->dt));
         break;
       case FGT_OP_RESHAPE:
       case FGT_OP_STOP_GRADIENT: memcpy(o->v, a->v, (size_t)o->n * vsize(o->dt)); break;
       case FGT_OP_BROADCAST_IN_DIM:
+      case FGT_OP_TRANSPOSE: {
+        /* output element j reads operand offset sum_k coord_k * step_k, where
+         * step_k is the operand stride that output axis k moves (0 for an
+         * expanded axis); walked one innermost run at a time */
         strides(a->shape, a->rank, as);
-        for (int64_t j = 0; j < o->n; ++j) {
-          unravel(j, o->shape, o->rank, cc);
-          int64_t off = 0;
-          for (int k = 0; k < a->rank; ++k) off += (a->shape[k] == 1 ? 0 : cc[nd->attrs[k]]) * as[k];
-          memcpy((char*)o->v + j * vsize(o->dt), (char*)a->v + off * vsize(o->dt), vsize(o->dt));
+        int64_t step[FGT_MAX_RANK] = {0};
+        if (op == FGT_OP_TRANSPOSE) {
+          for (int k = 0; k < o->rank; ++k) step[k] = as[nd->attrs[k]];
+        } else {
+          for (int k = 0; k < a->rank; ++k)
+            if (a->shape[k] != 1) step[nd->attrs[k]] += as[k];
         }
+        gather_runs(a, o, step, threads);
         break;
-      case FGT_OP_TRANSPOSE:
-        strides(a->shape, a->rank, as);
-        for (int64_t j = 0; j < o->n; ++j) {
-          unravel(j, o->shape, o->rank, cc);
-          int64_t off = 0;
-          for (int k = 0; k < o->rank; ++k) off += cc[k] * as[nd->attrs[k]];
-          memcpy((char*)o->v + j * vsize(o->dt), (char*)a->v + off * vsize(o->dt), vsize(o->dt));
-        }
-        break;
+      }
       case FGT_OP_IOTA:
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN) private(cc)
         for (int64_t j = 0; j < o->n; ++j) {
           unravel(j, o->shape, o->rank, cc);
           int64_t v = cc[nd->attrs[0]];
@@ -546,9 +704,11 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
         }
         break;
       case FGT_OP_CAST:
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
         for (int64_t j = 0; j < o->n; ++j) cast_one(a, j, o, j);
         break;
       case FGT_OP_COMPARE:
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
         for (int64_t j = 0; j < o->n; ++j) {
           int r;
           if (is_float(a->dt)) {
@@ -576,6 +736,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
         }
         break;
       case FGT_OP_SELECT:
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
         for (int64_t j = 0; j < o->n; ++j) {
           const Buf* s = ((uint8_t*)a->v)[j] ? b : c;
           memcpy((char*)o->v + j * vsize(o->dt), (char*)s->v + j * vsize(o->dt), vsize(o->dt));
@@ -587,6 +748,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
       case FGT_OP_SLICE: {
         const int r = a->rank;
         strides(a->shape, r, as);
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN) private(cc)
         for (int64_t j = 0; j < o->n; ++j) {
           unravel(j, o->shape, r, cc);
           int64_t off = 0;
@@ -598,6 +760,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
       case FGT_OP_PAD: {
         const int r = a->rank;
         strides(a->shape, r, as);
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN) private(cc)
         for (int64_t j = 0; j < o->n; ++j) {
           unravel(j, o->shape, r, cc);
           int in = 1;
@@ -617,6 +780,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
         int64_t bs[FGT_MAX_RANK];
         strides(a->shape, r, as);
         strides(b->shape, r, bs);
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN) private(cc)
         for (int64_t j = 0; j < o->n; ++j) {
           unravel(j, o->shape, r, cc);
           const int first = cc[ax] < a->shape[ax];
@@ -632,6 +796,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
         strides(a->shape, pr, as);
         int64_t is_[FGT_MAX_RANK];
         strides(b->shape, ir, is_);
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN) private(cc)
         for (int64_t j = 0; j < o->n; ++j) {
           unravel(j, o->shape, o->rank, cc);
           int64_t ioff = 0;
@@ -684,8 +849,9 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
       }
       default:
         if (op >= FGT_OP_REDUCE_SUM && op <= FGT_OP_ARGMIN) {
-          rc = eval_reduce(nd, a, o, mode);
+          rc = eval_reduce(nd, a, o, mode, threads);
         } else if (op >= FGT_OP_ADD && op <= FGT_OP_SHIFT_RIGHT) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
           for (int64_t j = 0; j < o->n; ++j) {
             if (is_float(o->dt)) ((float*)o->v)[j] = rnd_f(f_binary(op, ((float*)a->v)[j], ((float*)b->v)[j]), o->dt);
             else if (o->dt == FGT_BOOL) {
@@ -697,6 +863,7 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
             } else put_int(o, j, i_binary(op, geti(a, j), geti(b, j), o->dt));
           }
         } else if (op >= FGT_OP_EXP && op <= FGT_OP_BITWISE_NOT) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (o->n >= PAR_MIN)
           for (int64_t j = 0; j < o->n; ++j) {
             if (is_float(o->dt)) ((float*)o->v)[j] = rnd_f(f_unary(op, ((float*)a->v)[j]), o->dt);
             else if (o->dt == FGT_BOOL) ((uint8_t*)o->v)[j] = !((uint8_t*)a->v)[j];
@@ -720,9 +887,20 @@ int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* in
     }
   }
   if (!rc)
-    for (int k = 0; k < d->num_outputs; ++k) store_output(&B[d->outputs[k]], outputs[k]);
+    for (int k = 0; k < d->num_outputs; ++k) store_output(&B[d->outputs[k]], outputs[k], threads);
   for (int i = 0; i < N; ++i) free(B[i].v);
   free(B);
   free(last);
   return rc;
+}
+
+int fgt_oracle_eval(const fgt_partition_desc* d, int mode, const void* const* inputs, void* const* outputs, char* err,
+                    size_t errcap) {
+  return eval_impl(d, mode, inputs, outputs, err, errcap, 1);
+}
+
+/* The same evaluation on `threads` OpenMP threads. */
+int fgt_oracle_eval_mt(const fgt_partition_desc* d, int mode, const void* const* inputs, void* const* outputs,
+                       char* err, size_t errcap, int threads) {
+  return eval_impl(d, mode, inputs, outputs, err, errcap, threads);
 }

@@ -36,6 +36,8 @@ def _load():
     lib.fgt_oracle_eval.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                                     ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p, ctypes.c_size_t]
     lib.fgt_oracle_eval.restype = ctypes.c_int
+    lib.fgt_oracle_eval_mt.argtypes = lib.fgt_oracle_eval.argtypes + [ctypes.c_int]
+    lib.fgt_oracle_eval_mt.restype = ctypes.c_int
     return lib
 
 
@@ -71,8 +73,12 @@ def as_float(array, dtype):
 
 
 # ---------------------------------------------------------------- eval ---
-def evaluate(descriptor, inputs, mode=ACCURATE):
-    """Evaluate a partition descriptor on numpy inputs; returns output arrays."""
+def evaluate(descriptor, inputs, mode=ACCURATE, threads=1):
+    """Evaluate a partition descriptor on numpy inputs; returns output arrays.
+
+    threads > 1 runs the oracle's loops on that many OpenMP threads; every
+    result is the same for any thread count (whole-tensor sums fold fixed
+    chunks of 2^20 elements in order)."""
     in_types = descriptor.input_types()
     if len(inputs) != len(in_types):
         raise ValueError("input count mismatch")
@@ -86,7 +92,10 @@ def evaluate(descriptor, inputs, mode=ACCURATE):
     in_ptrs = (ctypes.c_void_p * max(1, len(ins)))(*[a.ctypes.data for a in ins])
     out_ptrs = (ctypes.c_void_p * max(1, len(outs)))(*[o.ctypes.data for o in outs])
     err = ctypes.create_string_buffer(512)
-    rc = lib().fgt_oracle_eval(ctypes.addressof(descriptor.struct), mode, in_ptrs, out_ptrs, err, 512)
+    if threads > 1:
+        rc = lib().fgt_oracle_eval_mt(ctypes.addressof(descriptor.struct), mode, in_ptrs, out_ptrs, err, 512, threads)
+    else:
+        rc = lib().fgt_oracle_eval(ctypes.addressof(descriptor.struct), mode, in_ptrs, out_ptrs, err, 512)
     if rc:
         raise RuntimeError("oracle failed: " + err.value.decode())
     return outs
