@@ -101,29 +101,8 @@ class ClockSampler:
 # --------------------------------------------------------------- helpers ----
 def device_inputs(cfg, rows, cols, dtype, device, seed=0):
     """Synthetic inputs generated on the device with the workload's distributions."""
-    import torch
-    from fugatensor_b200 import workloads as W, _fgt
-    g = torch.Generator(device=device).manual_seed(seed)
-    dts = W.input_dtypes(cfg, dtype)
-    shapes = {"x": (rows, cols), "y": (rows, cols), "X": (rows, cols), "dY": (rows, cols), "gamma": (cols,),
-              "beta": (cols,), "A": (rows, cols), "B": (rows, 1), "C": (1, cols)}
-    out = {}
-    for k, dt in dts.items():
-        shape = shapes[k]
-        if dt == "i32":
-            v = torch.randint(-1000, 1001, shape, device=device, dtype=torch.int32, generator=g)
-        elif cfg == "c1":
-            v = torch.rand(shape, device=device, generator=g) * 2 - 1
-        elif cfg == "c2" and k == "X":
-            v = torch.randn(shape, device=device, generator=g) * 2
-        elif cfg == "c3" and k == "gamma":
-            v = torch.rand(shape, device=device, generator=g) + 0.5
-        elif cfg == "c3" and k == "beta":
-            v = torch.randn(shape, device=device, generator=g) * 0.1
-        else:
-            v = torch.randn(shape, device=device, generator=g)
-        out[k] = v.to(_fgt.torch_dtype(dt)).contiguous()
-    return out
+    from fugatensor_b200 import workloads as W
+    return W.device_inputs(cfg, rows, cols, dtype, device, seed)
 
 
 def compile_partition(engine, cfg, variant, rows, cols, dtype, tensors):

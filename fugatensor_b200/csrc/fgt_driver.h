@@ -32,6 +32,8 @@ struct Driver {
   CUresult (*FuncSetAttribute)(CUfunction, CUfunction_attribute, int) = nullptr;
   CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
                            void**, void**) = nullptr;
+  // optional (CUDA 12.0+ drivers): a context's process-unique id
+  CUresult (*CtxGetId)(CUcontext, unsigned long long*) = nullptr;
 };
 
 inline Driver& drv() {
@@ -65,6 +67,7 @@ inline Driver& drv() {
     sym(d.FuncSetAttribute, "cuFuncSetAttribute");
     d.ok = all;
     if (!all) d.err = "libcuda.so.1 lacks a required driver entry point";
+    d.CtxGetId = reinterpret_cast<decltype(d.CtxGetId)>(dlsym(h, "cuCtxGetId"));
   });
   return d;
 }

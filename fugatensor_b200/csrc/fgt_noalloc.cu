@@ -7,7 +7,9 @@
 //
 // It computes the same results as the whole-tensor reduction partition
 // (sum, amax, argmax, mean of one f32 array) launched through
-// fgt_spec_launch: per-thread f32 chunk sums folded into f64, IEEE max
+// fgt_spec_launch: every element is added into an f64 accumulator and the
+// total is rounded to f32 once (so exactly cancelling terms sum to the exact
+// result, as in the generated kernel), IEEE max
 // (NaN propagates, +0 beats -0), first-occurrence argmax with NaN counted as
 // the maximum, mean = sum / n with one IEEE division. The difference is where
 // the scratch lives: the per-CTA partials are kept in a file-scope device
@@ -21,9 +23,15 @@
 //   - every GPU that loads the library holds the array (64 KiB) until exit;
 //   - all calls on a device share the array: calls that overlap on the GPU
 //     (different streams, or graphs replayed concurrently) race on it;
-//   - the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (once per device, under a lock); make that first
-//     call before any stream capture;
+//   - set-up: the first call on a device looks up the array's device address
+//     with cudaGetSymbolAddress (once per device and CUDA context, under a
+//     lock). With CUDA's lazy module loading (the default since 12.2) that
+//     first lookup is also when the driver loads this module and commits the
+//     64 KiB array, so the first call on each device is the one that touches
+//     device memory: make it at start-up, outside any allocator hook and
+//     before any stream capture. If the context is destroyed and re-created
+//     (cudaDeviceReset), the next call sees a new context id and repeats the
+//     set-up;
 //   - nothing in the array needs to start at zero: every slot the finalising
 //     kernel reads is written earlier in the same call.
 #include <cuda_runtime.h>
@@ -33,6 +41,7 @@
 
 #include "fgt.h"
 #include "fgt_device.cuh"
+#include "fgt_driver.h"
 
 namespace fgt {
 fgt_status record_error(fgt_status s, const std::string& m);  // fgt_runtime.cpp
@@ -110,18 +119,17 @@ __global__ void __launch_bounds__(kThreads) noalloc_partials(const float* __rest
   for (long long e0 = lo + (long long)threadIdx.x * kVec; e0 < vhi; e0 += (long long)kThreads * kVec) {
     float v[kVec];
     fgt_vload(v, x + e0);
-    float ls = 0.0f, lm = v[0], la = v[0];
+    float lm = v[0], la = v[0];
     int li = 0;
 #pragma unroll
     for (int k = 0; k < kVec; ++k) {
-      ls = ls + v[k];
+      sum += (double)v[k];  // each element into the f64 lane: the total rounds once, at the end
       lm = fgt_fmax(lm, v[k]);
       if (k && fgt_arg_scan_f<true>(v[k], la, li, 0x7fffffff)) {
         la = v[k];
         li = k;
       }
     }
-    sum += (double)ls;
     mx = fgt_fmax(mx, lm);
     const long long gi = e0 + li;
     if (fgt_arg_scan_f<true>(la, av, ai, 9223372036854775807ll)) {
@@ -175,8 +183,25 @@ __global__ void __launch_bounds__(kThreads) noalloc_finalize(const Slot* slots, 
   }
 }
 
+// Set-up state per device ordinal: the array's device address in the CUDA
+// context it was looked up in (identified by the driver's process-unique
+// context id, or by the context handle on a driver without cuCtxGetId).
+struct Setup {
+  void* addr = nullptr;
+  unsigned long long ctx_id = 0;
+};
 std::mutex g_setup_mu;
-void* g_scratch_addr[64] = {};
+Setup g_setup[64];
+
+bool current_context_id(unsigned long long* id) {
+  fgt::Driver& d = fgt::drv();
+  if (!d.ok) return false;
+  CUcontext ctx = nullptr;
+  if (d.CtxGetCurrent(&ctx) != CUDA_SUCCESS || !ctx) return false;
+  if (d.CtxGetId) return d.CtxGetId(ctx, id) == CUDA_SUCCESS;
+  *id = (unsigned long long)(uintptr_t)ctx;
+  return true;
+}
 
 // Failures are reported like every other entry point: status code plus the
 // thread's fgt_last_error() message.
@@ -197,25 +222,40 @@ extern "C" fgt_status fgt_reduce_f32_noalloc(const float* x, int64_t n, float* s
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(FGT_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(FGT_ERR_CUDA, "fgt_reduce_f32_noalloc: device ordinal out of range");
+  // An error left pending by earlier, unrelated CUDA work on this thread is
+  // reported as such (and left pending), not blamed on this call's launches.
+  e = cudaPeekAtLastError();
+  if (e != cudaSuccess)
+    return fail(FGT_ERR_CUDA, std::string("fgt_reduce_f32_noalloc: an earlier CUDA error is pending on this thread (") +
+                                  cudaGetErrorString(e) + "); nothing was launched");
   void* scratch = nullptr;
   {
-    // Set-up, once per device, with that device current: the array's device
-    // address. Host code only ever sees this address, never the symbol.
+    // Set-up, once per device and context, with that device current: the
+    // array's device address. Host code only ever passes this address to the
+    // kernels, never the symbol (a host-side stand-in).
     std::lock_guard<std::mutex> lock(g_setup_mu);
-    if (!g_scratch_addr[dev]) {
+    Setup& su = g_setup[dev];
+    unsigned long long id = 0;
+    const bool have_id = current_context_id(&id);
+    if (!su.addr || !have_id || id != su.ctx_id) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, fgt_noalloc_scratch);
       if (e != cudaSuccess) return fail(FGT_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_scratch_addr[dev] = p;
+      // the lookup made the device's context current if none was
+      if (!current_context_id(&id)) return fail(FGT_ERR_CUDA, "fgt_reduce_f32_noalloc: no current CUDA context");
+      su.addr = p;
+      su.ctx_id = id;
     }
-    scratch = g_scratch_addr[dev];
+    scratch = su.addr;
   }
   const int nslots = (int)((n + FGT_NOALLOC_ELEMS_PER_SLOT - 1) / FGT_NOALLOC_ELEMS_PER_SLOT);
   cudaStream_t st = (cudaStream_t)stream;
   Slot* slots = static_cast<Slot*>(scratch);
   noalloc_partials<<<nslots, kThreads, 0, st>>>(x, (long long)n, slots);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FGT_ERR_CUDA, std::string("launch (partials): ") + cudaGetErrorString(e));
   noalloc_finalize<<<1, kThreads, 0, st>>>(slots, nslots, (long long)n, sum, max, (long long*)argmax, mean);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(FGT_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  if (e != cudaSuccess) return fail(FGT_ERR_CUDA, std::string("launch (finalize): ") + cudaGetErrorString(e));
   return FGT_OK;
 }

@@ -12,10 +12,14 @@ inputs of the partition's own types and shapes (CUDA events, L2 flushed
 between launches), and keeps the fastest. The choice is stored in
 ``tuning.json`` in the kernel cache directory, keyed by the partition's
 structure, the GPU, and the library build, so later processes skip the
-measurement. Every geometry computes the partition's results within its
-tolerances; floating-point sums may differ in the last bits between
-geometries (a row's summation order follows how its elements are spread over
-threads), and the persisted choice keeps one geometry per partition.
+measurement. Every geometry must compute the partition's results within its
+tolerances: before a candidate is kept, its outputs on the tuning inputs are
+compared with the default geometry's (integer, bool and index outputs bit for
+bit; floats within 1e-5 for f32 and 1e-2 for f16/bf16 of the output's scale),
+and a candidate that disagrees is rejected and recorded. Floating-point sums
+may still differ in the last bits between geometries (a row's summation
+order follows how its elements are spread over threads), and the persisted
+choice keeps one geometry per partition.
 """
 from __future__ import annotations
 
@@ -43,6 +47,7 @@ from . import _fgt, ir
 _GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
 CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 8) for g in _GEOMETRIES)
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
+RTOL = {"f32": 1e-5, "f16": 1e-2, "bf16": 1e-2}  # agreement with the default geometry
 _lock = threading.Lock()
 
 
@@ -123,6 +128,41 @@ def _time_all(specs, inputs, device, flush, rounds=9):
     return [sorted(t)[len(t) // 2] for t in times]
 
 
+def _outputs(spec, inputs, device):
+    import torch
+    outs = [torch.empty(s, dtype=_fgt.torch_dtype(dt), device=device) for dt, s in spec.output_types]
+    ws = torch.empty(max(spec.workspace_bytes, 1), dtype=torch.uint8, device=device)
+    spec.launch([t.data_ptr() for t in inputs], [t.data_ptr() for t in outs], ws.data_ptr(), spec.workspace_bytes,
+                torch.cuda.current_stream(device).cuda_stream)
+    torch.cuda.current_stream(device).synchronize()
+    return outs
+
+
+def agrees(outs, ref, types):
+    """Outputs `outs` agree with `ref`: non-float outputs bit for bit; floats with
+    the same NaN and inf positions and |a - b| <= rtol * (|b| + max|b|)."""
+    import torch
+    for (dt, _), a, b in zip(types, outs, ref):
+        if dt not in RTOL:
+            if not torch.equal(a, b):
+                return False
+            continue
+        a, b = a.double().reshape(-1), b.double().reshape(-1)
+        if not torch.equal(torch.isnan(a), torch.isnan(b)):
+            return False
+        inf = torch.isinf(b)
+        if not torch.equal(torch.isinf(a), inf) or not torch.equal(a[inf], b[inf]):
+            return False
+        fin = torch.isfinite(b)
+        if not bool(fin.any()):
+            continue
+        bf, af = b[fin], a[fin]
+        scale = bf.abs().max()
+        if bool(((af - bf).abs() > RTOL[dt] * (bf.abs() + scale) + 1e-30).any()):
+            return False
+    return True
+
+
 def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     """The spec of `desc` with the fastest measured row geometry (default geometry without a GPU)."""
     import torch
@@ -159,9 +199,16 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
         inputs = [_synthetic(dt, s, dev, gen) for dt, s in default.input_types]
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         ms_all = _time_all([s for _, s in specs], inputs, dev, flush)
-        timed = [(ms, g, s) for ms, (g, s) in zip(ms_all, specs)]
-        del inputs, flush
-    ms, geom, best = min(timed, key=lambda t: t[0])
-    _store(path, key, {"geometry": list(geom), "ms": round(ms, 5),
+        timed = sorted(((ms, g, s) for ms, (g, s) in zip(ms_all, specs)), key=lambda t: t[0])
+        del flush
+        # the fastest candidate whose outputs agree with the default geometry's
+        ref = _outputs(default, inputs, dev)
+        rejected = []
+        for ms, geom, best in timed:
+            if geom == (0, 0, 0, 0) or agrees(_outputs(best, inputs, dev), ref, default.output_types):
+                break
+            rejected.append("x".join(map(str, geom)))
+        del inputs, ref
+    _store(path, key, {"geometry": list(geom), "ms": round(ms, 5), "rejected": rejected,
                        "candidates": {"x".join(map(str, g)): round(t, 5) for t, g, _ in timed}})
     return best

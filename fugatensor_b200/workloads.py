@@ -26,6 +26,10 @@ FULL = {
     "c5": (8192, 8192),
 }
 
+# rows of the medium-size check that runs every row partition in every
+# candidate geometry of the tuner (several rows per CTA on 148 SMs)
+PARITY_ROWS = 2048
+
 VARIANTS = {
     "c1": ("chain_rowsum",),
     "c2": ("softmax_fwd", "softmax_vjp"),
@@ -94,6 +98,36 @@ def input_dtypes(cfg, dtype=None):
     if cfg == "c2" and dtype == "bf16":
         d = {"X": "bf16", "dY": "bf16"}
     return d
+
+
+SHAPES = lambda rows, cols: {"x": (rows, cols), "y": (rows, cols), "X": (rows, cols), "dY": (rows, cols),
+                              "gamma": (cols,), "beta": (cols,), "A": (rows, cols), "B": (rows, 1), "C": (1, cols)}
+
+
+def device_inputs(cfg, rows, cols, dtype, device, seed=0):
+    """Seeded inputs generated on the device (torch) with the workload's
+    distributions; the benchmark and the full-size parity checks use these
+    (the numpy generator of make_inputs is too slow for 2^31 elements)."""
+    import torch
+    from . import _fgt
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for k, dt in input_dtypes(cfg, dtype).items():
+        shape = SHAPES(rows, cols)[k]
+        if dt == "i32":
+            v = torch.randint(-1000, 1001, shape, device=device, dtype=torch.int32, generator=g)
+        elif cfg == "c1":
+            v = torch.rand(shape, device=device, generator=g) * 2 - 1
+        elif cfg == "c2" and k == "X":
+            v = torch.randn(shape, device=device, generator=g) * 2
+        elif cfg == "c3" and k == "gamma":
+            v = torch.rand(shape, device=device, generator=g) + 0.5
+        elif cfg == "c3" and k == "beta":
+            v = torch.randn(shape, device=device, generator=g) * 0.1
+        else:
+            v = torch.randn(shape, device=device, generator=g)
+        out[k] = v.to(_fgt.torch_dtype(dt)).contiguous()
+    return out
 
 
 def build(cfg, variant, t, eps=1e-6):

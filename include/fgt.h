@@ -251,8 +251,10 @@ fgt_status fgt_spec_launch_sharded(const fgt_spec* spec, fgt_comm* comm, const v
  * device memory and pass only input/output buffers). Computes the sum, IEEE
  * max, first-occurrence argmax (NaN counts as the maximum) and mean (sum / n)
  * of x[0..n), like the whole-tensor reduction partition through
- * fgt_spec_launch, but keeps its per-CTA partials in a static 64 KiB device
- * array instead of a caller workspace; it calls no allocator.
+ * fgt_spec_launch (every element added into an f64 accumulator, the total
+ * rounded to f32 once), but keeps its per-CTA partials in a static 64 KiB
+ * device array instead of a caller workspace. It calls no cudaMalloc,
+ * cudaFree or allocating library routine.
  *   - x: device pointer, 16-byte aligned; sum/max/mean: device f32 scalars;
  *     argmax: device i64 scalar; stream: cudaStream_t (NULL = default).
  *   - n must be in [1, 2^31] (FGT_NOALLOC_SLOTS x FGT_NOALLOC_ELEMS_PER_SLOT);
@@ -261,9 +263,16 @@ fgt_status fgt_spec_launch_sharded(const fgt_spec* spec, fgt_comm* comm, const v
  *     exit. All calls on a device share it: calls that overlap on the GPU
  *     race. Nothing in it needs to start at zero (each call writes every slot
  *     it reads).
- *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress, once per device); make it before any stream
- *     capture. */
+ *   - Set-up: the first call on a device (and in each new CUDA context of it,
+ *     e.g. after cudaDeviceReset) looks up the array's device address with
+ *     cudaGetSymbolAddress. Under CUDA's lazy module loading (the default
+ *     since 12.2) that lookup is when the driver loads the library's module
+ *     and commits the array's device memory. So make the first call on each
+ *     device at start-up (a call on a small valid input will do), outside any
+ *     allocator hook and before any stream capture; later calls touch no
+ *     device memory beyond their inputs, outputs and the array.
+ *   - A CUDA error already pending on the calling thread is reported (and left
+ *     pending) without launching. */
 fgt_status fgt_reduce_f32_noalloc(const float* x, int64_t n, float* sum, float* max, int64_t* argmax, float* mean,
                                   void* stream);
 

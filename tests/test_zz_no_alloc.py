@@ -65,7 +65,7 @@ def check_same(got, ref):
             assert abs(g - r) <= RTOL * abs(r) + 1e-30, (g, r)
 
 
-@pytest.mark.parametrize("n", [1, 3, 1000003, (1 << 22) + 1])
+@pytest.mark.parametrize("n", [1, 3, 1000003, 1 << 20, 2 << 20, (1 << 22) + 1])
 def test_matches_regular_entry_point_on_two_calls(n):
     gen = torch.Generator(device="cuda").manual_seed(n)
     x1 = torch.rand(n, device="cuda", generator=gen) + 0.25
@@ -85,11 +85,51 @@ def test_nan_counts_as_maximum():
     assert got[2] == ref[2] == 12345 and np.isnan(got[1]) and np.isnan(got[0])
 
 
+def test_cancelling_terms_match_bit_for_bit():
+    """Chunks of [2^24, 1, -2^24, 0]: an f32 running sum loses every 1 (2^24 + 1
+    rounds to 2^24); adding each element in f64, as both entry points do, keeps
+    them. Also a cancelling triple spread over three scratch slots."""
+    n = 1 << 20
+    chunk = torch.tensor([2.0 ** 24, 1.0, -(2.0 ** 24), 0.0], device="cuda")
+    x1 = chunk.repeat(n // 4)
+    x2 = torch.zeros(3 << 20, device="cuda")
+    x2[5], x2[(1 << 20) + 7], x2[(2 << 20) + 9] = 2.0 ** 24, 1.0, -(2.0 ** 24)
+    for x, total in ((x1, n // 4), (x2, 1)):
+        for _ in range(2):
+            got, ref = no_alloc(x), regular(x)
+            assert got[0] == ref[0] == float(total)
+            assert got == ref  # every output bit for bit (sum, max, argmax, mean)
+
+
+def test_exact_size_limit():
+    """n = 2^31 (FGT_NOALLOC_SLOTS x FGT_NOALLOC_ELEMS_PER_SLOT, 8 GiB of f32) is
+    accepted and matches the regular entry point; one more element is rejected
+    before anything is launched."""
+    limit = 2048 * (1 << 20)
+    torch.cuda.empty_cache()
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    x = torch.randn(limit, device="cuda", generator=gen)
+    x[limit - 1] = 1e30  # the maximum sits in the last element of the last slot
+    for _ in range(2):
+        got, ref = no_alloc(x), regular(x)
+        check_same(got, ref)
+        assert got[2] == limit - 1
+    out = torch.zeros(4, device="cuda")
+    st = lib.fgt_reduce_f32_noalloc(x.data_ptr(), limit + 1, out.data_ptr(), out.data_ptr(), out.data_ptr(),
+                                    out.data_ptr(), 0)
+    assert st == 1 and b"exceeds the static scratch limit" in lib.fgt_last_error()
+    del x
+    torch.cuda.empty_cache()
+
+
 def test_sizes_beyond_the_static_scratch_are_rejected():
     x = torch.zeros(16, device="cuda")
     out = torch.zeros(4, device="cuda")
-    too_big = FGT_MAX = 2048 * (1 << 20) + 1
-    st = lib.fgt_reduce_f32_noalloc(x.data_ptr(), too_big, out.data_ptr(), out.data_ptr(), out.data_ptr(),
-                                    out.data_ptr(), 0)
-    assert st == 1 and b"exceeds the static scratch limit" in lib.fgt_last_error()
-    assert FGT_MAX == too_big
+    for n in (2048 * (1 << 20) + 1, 1 << 40):
+        st = lib.fgt_reduce_f32_noalloc(x.data_ptr(), n, out.data_ptr(), out.data_ptr(), out.data_ptr(),
+                                        out.data_ptr(), 0)
+        assert st == 1 and b"exceeds the static scratch limit" in lib.fgt_last_error()
+    for n in (0, -1):
+        st = lib.fgt_reduce_f32_noalloc(x.data_ptr(), n, out.data_ptr(), out.data_ptr(), out.data_ptr(),
+                                        out.data_ptr(), 0)
+        assert st == 1 and b"n must be positive" in lib.fgt_last_error()
