@@ -398,6 +398,12 @@ struct Emitter {
     int64_t smem_off = 0;  // region of this operand in the ring
   };
   std::vector<RowSite> row_sites;
+  // Ring-resident rows (FGT_ROW_RING_RESIDENT): a staged operand's current row
+  // stays in its ring stage, and each phase that reads it copies the thread's
+  // own pieces of the chunk into a phase-local array (the name maps to the
+  // operand's index in row_sites).
+  std::map<std::string, int> resident_loc;
+  bool resident() const { return P.opt.ring_resident && cached && K.cluster == 1; }
   int stages = 0;                  // shared-memory ring depth (0: register path)
   int64_t stage_bytes = 0;         // bytes of one stage (all staged operands)
   // Shared-memory address (bytes from the dynamic base) of a thread's piece.
@@ -521,6 +527,23 @@ struct Emitter {
     return "((const " + T + "*)(p.ws+" + std::to_string(L.offset) + "LL))";
   }
 
+  // Phase p's copy of staged operand row_sites[idx] for the current chunk:
+  // read from the current row's ring stage at the top of the chunk (the
+  // stage offset is resolved when the ring is laid out: @PIECE<idx>@).
+  std::string resident_local(int idx, int p) {
+    const RowSite& rs = row_sites[idx];
+    const std::string key = "rloc|" + rs.name + "|" + std::to_string(p);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+    const std::string loc = fresh("rs");
+    memo[key] = loc;
+    resident_loc[loc] = idx;
+    const std::string W = std::to_string(rs.packed ? K.vec / 2 : K.vec);
+    chunkpre[p].push_back(rs.st + " " + loc + "[" + W + "]; fgt_lds(" + loc + ", (const " + rs.st + "*)(fgt_dsmem + @PIECE" +
+                          std::to_string(idx) + "@));");
+    return loc;
+  }
+
   std::string load(int id, const Map& m, Sc D) {
     const Node& n = g.nodes[id];
     Idx A = to_linear(m, n.shape, d);
@@ -579,8 +602,10 @@ struct Emitter {
           // cp.async moves 4, 8 or 16 bytes; a stage (one row of every staged
           // operand) must fit the ring budget.
           const int64_t piece = (int64_t)K.rows_per_cta * K.nch * (K.tpr / K.cluster) * rs.bytes;
+          // ring-resident rows need two stages: the current row and the next
+          const int64_t budget = (int64_t)P.opt.ring_kb * 1024 / (resident() ? 2 : 1);
           rs.staged = P.opt.row_staging && (rs.bytes == 4 || rs.bytes == 8 || rs.bytes == 16) &&
-                      stage_bytes + piece <= (int64_t)P.opt.ring_kb * 1024;
+                      stage_bytes + piece <= budget;
           if (rs.staged) stage_bytes += piece;
           row_sites.push_back(rs);
         } else if (elem) {
@@ -590,7 +615,13 @@ struct Emitter {
           chunkpre[D.p].push_back(SS + " " + s + "[" + vec + "]; fgt_vload(" + s + ", " + src + ");");
         }
       }
-      const std::string arr = prol ? s : cached ? s + "[c]" : elem ? s + "[u]" : s;
+      std::string arr = prol ? s : cached ? s + "[c]" : elem ? s + "[u]" : s;
+      if (cached && !prol && resident()) {
+        int idx = -1;
+        for (size_t k = 0; k < row_sites.size(); ++k)
+          if (row_sites[k].name == s) idx = (int)k;
+        if (idx >= 0 && row_sites[idx].staged) arr = resident_local(idx, D.k == SC_LANE ? D.p : 0);
+      }
       if (pack16(n.dt)) return ld_conv(n.dt, "fgt_h16(" + arr + ", v)");
       return ld_conv(n.dt, arr + "[v]");
     }
@@ -654,9 +685,16 @@ struct Emitter {
     } else if (persisted) {
       std::string v = val(id, m, Sc{SC_PROLANE, 0});
       std::string cname = fresh("cv");
-      kdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
-      prolane.push_back(cname + "[c][v] = " + v + ";");
-      r = cname + "[c][v]";
+      if (resident() && pack16(n.dt)) {
+        // a 16-bit value is exact in its storage bits: two per register
+        kdecl.push_back("fgt_u32 " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec / 2) + "];");
+        prolane.push_back("fgt_set_h16(" + cname + "[c], v, " + st_conv(n.dt, v) + ");");
+        r = ld_conv(n.dt, "fgt_h16(" + cname + "[c], v)");
+      } else {
+        kdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
+        prolane.push_back(cname + "[c][v] = " + v + ";");
+        r = cname + "[c][v]";
+      }
       memo[key] = r;
       return r;
     } else {
@@ -1168,18 +1206,25 @@ struct Emitter {
       // max/min of a widened bf16 register row: packed bf16x2 max/min over
       // the row's 32-bit words (exact: no rounding), folded into the f32
       // accumulator after the phase.
-      std::string pk_site;
+      std::string pk_site;  // the chunk's words of the site (text valid in the chunk loop)
       {
         auto te = texpr.find(v);
         const std::string& ex = te == texpr.end() ? v : te->second;
         const bool pk = pack16(FGT_BF16);
         const std::string pre = pk ? "fgt_bf16_to_f32(fgt_h16(" : "fgt_bf16_to_f32(", suf = pk ? "[c], v))" : "[c][v])";
-        if ((t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN) && t.fl && !t.storage && cached && K.vec % 2 == 0 &&
-            ex.size() > pre.size() + suf.size() && ex.compare(0, pre.size(), pre) == 0 &&
-            ex.compare(ex.size() - suf.size(), suf.size(), suf) == 0) {
+        const std::string lsuf = pk ? ", v))" : "[v])";  // a ring-resident phase-local array
+        const bool maxmin = (t.op == FGT_OP_REDUCE_MAX || t.op == FGT_OP_REDUCE_MIN) && t.fl && !t.storage && cached &&
+                            K.vec % 2 == 0 && ex.compare(0, pre.size(), pre) == 0;
+        if (maxmin && ex.size() > pre.size() + suf.size() && ex.compare(ex.size() - suf.size(), suf.size(), suf) == 0) {
           const std::string site = ex.substr(pre.size(), ex.size() - pre.size() - suf.size());
           for (auto& rs : row_sites)
-            if (rs.name == site && rs.st == (pk ? "fgt_u32" : "fgt_u16") && !rs.uniform) pk_site = site;
+            if (rs.name == site && rs.st == (pk ? "fgt_u32" : "fgt_u16") && !rs.uniform) pk_site = site + "[c]";
+        }
+        if (maxmin && pk_site.empty() && ex.size() > pre.size() + lsuf.size() &&
+            ex.compare(ex.size() - lsuf.size(), lsuf.size(), lsuf) == 0) {
+          const std::string loc = ex.substr(pre.size(), ex.size() - pre.size() - lsuf.size());
+          auto rl = resident_loc.find(loc);
+          if (rl != resident_loc.end() && row_sites[rl->second].st == (pk ? "fgt_u32" : "fgt_u16")) pk_site = loc;
         }
       }
       resets[p].push_back(a + " = " + t.ident + ";");
@@ -1189,7 +1234,7 @@ struct Emitter {
         rowsc[p].push_back("fgt_u32 " + a + "_pk = " + init + ";");
         resets[p].push_back(a + "_pk = " + init + ";");
         chunkpost[p].push_back(a + "_pk = fgt_" + (mx ? std::string("max") : std::string("min")) + "_bf16x2_row(" + a + "_pk, " +
-                               pk_site + "[c]);");
+                               pk_site + ");");
         post[p].push_back(comb_stmt(t, a, "fgt_bf16_to_f32((fgt_u16)(" + a + "_pk & 0xffffu))"));
         post[p].push_back(comb_stmt(t, a, "fgt_bf16_to_f32((fgt_u16)(" + a + "_pk >> 16))"));
         phase_accs[p].push_back({t, a});
@@ -1344,14 +1389,26 @@ struct Emitter {
     // (b) other operands are double-buffered in registers.
     std::vector<RowSite*> staged_sites, reg_sites;
     for (auto& rs : row_sites) (rs.staged ? staged_sites : reg_sites).push_back(&rs);
+    const bool res = resident() && !staged_sites.empty();
     if (!staged_sites.empty()) {
-      // rows in flight per CTA: as many as fit the ring budget (96 KB: two CTAs per SM)
-      stages = (int)std::min<int64_t>(8, std::max<int64_t>(1, ((int64_t)P.opt.ring_kb * 1024) / std::max<int64_t>(1, stage_bytes)));
+      // rows in flight per CTA: as many as fit the ring budget (96 KB: two CTAs per SM);
+      // ring-resident rows keep the current row in a stage too (at least two)
+      stages = (int)std::min<int64_t>(8, std::max<int64_t>(res ? 2 : 1, ((int64_t)P.opt.ring_kb * 1024) / std::max<int64_t>(1, stage_bytes)));
       int64_t off = col_smem;  // the ring follows any shared-memory column accumulators
       for (auto* rs : staged_sites) {
         rs->smem_off = off;
         off += (int64_t)stages * K.rows_per_cta * K.nch * (K.tpr / K.cluster) * rs->bytes;
       }
+    }
+    if (res) {
+      // phase-local copies read the current row's stage `stg`
+      for (auto& cp : chunkpre)
+        for (auto& st : cp)
+          for (size_t k = 0; k < row_sites.size(); ++k) {
+            const std::string ph = "@PIECE" + std::to_string(k) + "@";
+            for (size_t at = st.find(ph); at != std::string::npos; at = st.find(ph))
+              st.replace(at, ph.size(), piece_off(row_sites[k], "stg"));
+          }
     }
     const std::string stride = K.cluster > 1 ? "(fgt_i64)(gridDim.x / " + std::to_string(K.cluster) + ") * " + RPC
                                              : "(fgt_i64)gridDim.x * " + RPC;
@@ -1382,6 +1439,7 @@ struct Emitter {
       });
     };
     for (auto& rs : row_sites) {
+      if (res && rs.staged) continue;  // read from the ring by each phase
       const std::string W = rs.packed ? std::to_string(K.vec / 2) : VEC;
       std::string dims = rs.uniform ? "[" + NCH + "]" : "[" + NCH + "][" + W + "]";
       o << "  " << rs.st << " " << rs.name << dims << ";";
@@ -1391,12 +1449,20 @@ struct Emitter {
     if (stages) o << "  const unsigned sbase_ = fgt_smem_addr(fgt_dsmem);\n";
     // Ring invariant at the top of iteration i: registers hold row i, ring
     // stage (i+k) % S holds row i+k for k = 1..S (S cp.async groups pending).
+    // Ring-resident rows: stage i % S holds row i and stages of rows i+1 ..
+    // i+S-1 are in flight; the wait at the top of the iteration completes
+    // row i's group, and its stage refills with row i+S once the row is done.
     const std::string S = std::to_string(stages);
     if (!row_sites.empty()) {
       o << "  { const fgt_i64 r0_ = " << CB << " * " << RPC << " + grp;\n    if (r0_ < NR) {\n";
       reg_loads(o, "      ", "r0_", false);
       o << "    }\n";
-      if (stages) {
+      if (res) {
+        o << "    for (int k_ = 0; k_ < " << S << "; ++k_) {\n";
+        o << "      const fgt_i64 rk_ = r0_ + (fgt_i64)k_ * " << stride << ";\n      if (rk_ < NR) {\n";
+        issue(o, "        ", "rk_", "k_");
+        o << "      }\n      fgt_cp_commit();\n    }\n";
+      } else if (stages) {
         o << "    for (int k_ = 0; k_ < " << S << "; ++k_) {\n";
         o << "      const fgt_i64 rk_ = r0_ + (fgt_i64)k_ * " << stride << ";\n      if (rk_ < NR) {\n";
         issue(o, "        ", "rk_", "k_");
@@ -1408,7 +1474,8 @@ struct Emitter {
         o << "      }\n      fgt_cp_commit();\n    }\n";
       }
       o << "  }\n";
-      if (stages) o << "  int stg = " << (stages > 1 ? 1 : 0) << ";\n";
+      if (res) o << "  int stg = 0;\n";
+      else if (stages) o << "  int stg = " << (stages > 1 ? 1 : 0) << ";\n";
     }
     if (!rowpf_first.empty()) {
       o << "  { const fgt_i64 r = " << CB << " * " << RPC << " + grp; const bool rv = r < NR; " << digits_o() << "\n";
@@ -1431,6 +1498,7 @@ struct Emitter {
       reg_loads(o, "      ", "rn_", true);
       o << "    }\n";
     }
+    if (res) o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
     put(o, rowdecl, "    ");
     auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind) {
       if (cached) o << ind << "  #pragma unroll\n";
@@ -1487,7 +1555,13 @@ struct Emitter {
       if (rs->uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) " << rs->name << "[c] = " << rs->name << "_n[c];\n";
       else o << "    for (int c = 0; c < " << NCH << "; ++c) for (int v = 0; v < " << (rs->packed ? std::to_string(K.vec / 2) : VEC) << "; ++v) " << rs->name << "[c][v] = " << rs->name << "_n[c][v];\n";
     }
-    if (stages) {
+    if (res) {
+      // row i is done: its stage refills with row i+S
+      o << "    { const fgt_i64 rk_ = r + (fgt_i64)" << S << " * " << stride << ";\n      if (rk_ < NR) {\n";
+      issue(o, "        ", "rk_", "stg");
+      o << "      }\n      fgt_cp_commit();\n    }\n";
+      o << "    stg = stg + 1 == " << S << " ? 0 : stg + 1;\n";
+    } else if (stages) {
       // row i+1 -> registers; its stage refills with row i+1+S
       o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
       smem_to_regs(o, "    ", "stg");

@@ -213,6 +213,10 @@ FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // 16-bit element v of a packed row piece (two values per 32-bit word, the
 // lower index in the low half)
 template <int N> FGT_DEV fgt_u16 fgt_h16(const fgt_u32 (&w)[N], int v) { return (fgt_u16)(w[v >> 1] >> ((v & 1) * 16)); }
+// Element v of a packed 16-bit array (v a compile-time constant after unrolling).
+template <int N> FGT_DEV void fgt_set_h16(fgt_u32 (&w)[N], int v, fgt_u16 h) {
+  w[v >> 1] = (v & 1) ? ((w[v >> 1] & 0xffffu) | ((fgt_u32)h << 16)) : ((w[v >> 1] & 0xffff0000u) | (fgt_u32)h);
+}
 // packed pieces are already bf16x2 words
 template <int N> FGT_DEV fgt_u32 fgt_max_bf16x2_row(fgt_u32 acc, const fgt_u32 (&w)[N]) {
 #pragma unroll

@@ -1297,6 +1297,7 @@ struct Planner {
     mix(opt.own_exp);
     mix(opt.xw_tree);
     mix(opt.smem_cols);
+    mix(opt.ring_resident);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);
     mix(opt.row_cluster);

@@ -145,6 +145,7 @@ struct Options {
   int smem_cols = 0;              // row kernels: column accumulators in shared memory (FGT_ROW_SMEM_COLS)
   int xw_tree = 1;                // cross-warp row reductions: tree over the warp partials (FGT_ROW_XW_SHUFFLE: butterfly)
   int own_exp = 1;                // exp in redoable row phases by fgt_exp_q, else expf (FGT_ROW_EXPF, or FGT_OWN_EXP=0)
+  int ring_resident = 0;          // row kernels: operands read from the ring in every phase (FGT_ROW_RING_RESIDENT)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
   int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)
   int row_cluster = 1;            // CTAs per row in block-per-row kernels (thread-block cluster; FGT_ROW_CLUSTER)

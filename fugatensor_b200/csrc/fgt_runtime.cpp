@@ -456,8 +456,10 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       require(options->row_cluster >= 0 && options->row_cluster <= 8 && (options->row_cluster & (options->row_cluster - 1)) == 0,
               "row_cluster must be 0 or a power of two up to 8");
       if (options->row_cluster > 0) opt.row_cluster = options->row_cluster;
-      require((options->row_flags & ~(FGT_ROW_OCCUPANCY_STEP | FGT_ROW_EXPF | FGT_ROW_SMEM_COLS | FGT_ROW_XW_SHUFFLE)) == 0,
+      require((options->row_flags & ~(FGT_ROW_OCCUPANCY_STEP | FGT_ROW_EXPF | FGT_ROW_SMEM_COLS | FGT_ROW_XW_SHUFFLE |
+                                      FGT_ROW_RING_RESIDENT)) == 0,
               "unknown row_flags bits");
+      opt.ring_resident = (options->row_flags & FGT_ROW_RING_RESIDENT) != 0;
       if (options->row_flags & FGT_ROW_XW_SHUFFLE) opt.xw_tree = 0;
       opt.occupancy_step = (options->row_flags & FGT_ROW_OCCUPANCY_STEP) != 0;
       opt.smem_cols = (options->row_flags & FGT_ROW_SMEM_COLS) != 0;

@@ -160,7 +160,12 @@ typedef enum fgt_row_flag {
   FGT_ROW_SMEM_COLS = 4,
   /* cross-warp row reductions by a shuffle butterfly over the warp partials,
    * instead of every thread folding them from shared memory */
-  FGT_ROW_XW_SHUFFLE = 8
+  FGT_ROW_XW_SHUFFLE = 8,
+  /* row operands stay in the shared-memory ring while their row is computed
+   * (each phase reads the thread's own pieces again), and per-thread column
+   * operands of 16-bit types stay packed two per register: fewer registers
+   * per thread, so more CTAs per SM, for rows with several phases */
+  FGT_ROW_RING_RESIDENT = 16
 } fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
