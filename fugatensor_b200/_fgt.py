@@ -39,6 +39,10 @@ class CUDAError(FgtError):
     pass
 
 
+class NCCLError(FgtError):
+    """A collective or communicator failed or passed its deadline (FGT_COMM_TIMEOUT_MS)."""
+
+
 if not LIB_PATH.exists():
     raise ImportError(f"native backend {LIB_PATH} is not built; run `python -m fugatensor_b200.build`")
 
@@ -74,17 +78,24 @@ lib.fgt_comm_create.argtypes = [ctypes.POINTER(ctypes.c_uint8), ctypes.c_int32, 
 lib.fgt_comm_destroy.argtypes = [_vp]
 lib.fgt_comm_destroy.restype = None
 lib.fgt_spec_launch_sharded.argtypes = [_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, ctypes.c_size_t, _vp]
+lib.fgt_program_create.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(_vp)]
+lib.fgt_program_run.argtypes = [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, ctypes.c_size_t, _vp]
+lib.fgt_program_kernel_count.argtypes = [_vp]
+lib.fgt_program_kernel_count.restype = ctypes.c_int32
+lib.fgt_program_destroy.argtypes = [_vp]
+lib.fgt_program_destroy.restype = None
 
 EXPORTED = ("fgt_last_error", "fgt_abi_version", "fgt_spec_create", "fgt_spec_destroy", "fgt_spec_get_info",
             "fgt_spec_port", "fgt_spec_plan_json", "fgt_spec_kernel_source", "fgt_spec_launch",
             "fgt_comm_unique_id", "fgt_comm_create", "fgt_comm_destroy", "fgt_spec_launch_sharded",
+            "fgt_program_create", "fgt_program_run", "fgt_program_kernel_count", "fgt_program_destroy",
             "fgt_reduce_f32_noalloc")
 
 
 def check(status):
     if status != FGT_OK:
         msg = lib.fgt_last_error().decode(errors="replace")
-        cls = CompileError if status == 3 else CUDAError if status == 4 else FgtError
+        cls = CompileError if status == 3 else CUDAError if status == 4 else NCCLError if status == 5 else FgtError
         raise cls(status, msg)
 
 
@@ -158,6 +169,28 @@ class Spec:
             self._h = None
 
 
+class Program:
+    """A spec prepared for repeated runs (fgt_program, through the _native extension).
+
+    graph=True: the first run on a CUDA context instantiates the spec's
+    kernels as one CUDA graph, and every later run replays it with that run's
+    buffers (the reference prepares its programs the same way,
+    src/fugatensor/engine.py:416-423). graph=False launches kernel by kernel.
+    """
+
+    def __init__(self, spec: Spec, graph: bool = True):
+        from . import _native
+        self.spec = spec  # the program borrows the spec: keep it alive
+        self._p = _native.prepare_program(spec._h.value, bool(graph))
+        self.graph = bool(graph)
+        self.kernel_count = self._p.kernel_count
+
+    def launch(self, inputs, outputs, workspace=0, workspace_bytes=0, stream=0):
+        """Run with raw device addresses (ints) on a raw stream handle."""
+        check(self._p.run([int(p) for p in inputs], [int(p) for p in outputs], int(workspace), int(workspace_bytes),
+                          int(stream)))
+
+
 class Comm:
     """One rank of an NCCL communicator owned by libfgt."""
 
@@ -192,8 +225,9 @@ def torch_dtype(name):
             "f16": torch.float16, "bf16": torch.bfloat16}[name]
 
 
-def run(spec: Spec, *inputs, outputs=None, workspace=None, stream=None, comm=None):
-    """Launch ``spec`` on torch CUDA tensors; allocates outputs/workspace if not given."""
+def run(spec: Spec, *inputs, outputs=None, workspace=None, stream=None, comm=None, program=None):
+    """Launch ``spec`` on torch CUDA tensors; allocates outputs/workspace if not given.
+    With ``program`` (a Program of this spec) the run goes through it."""
     import torch
     if len(inputs) != spec.num_inputs:
         raise ValueError(f"partition takes {spec.num_inputs} inputs, got {len(inputs)}")
@@ -210,7 +244,12 @@ def run(spec: Spec, *inputs, outputs=None, workspace=None, stream=None, comm=Non
         workspace = torch.empty(spec.workspace_bytes, dtype=torch.uint8, device=device)
     if stream is None:
         stream = torch.cuda.current_stream(device)
-    spec.launch([t.data_ptr() for t in inputs], [t.data_ptr() for t in outputs],
-                workspace.data_ptr() if workspace is not None else 0, spec.workspace_bytes,
-                stream.cuda_stream, comm=comm)
+    ins, outs = [t.data_ptr() for t in inputs], [t.data_ptr() for t in outputs]
+    ws = workspace.data_ptr() if workspace is not None else 0
+    if program is not None:
+        if program.spec is not spec:
+            raise ValueError("program was prepared for another spec")
+        program.launch(ins, outs, ws, spec.workspace_bytes, stream.cuda_stream)
+    else:
+        spec.launch(ins, outs, ws, spec.workspace_bytes, stream.cuda_stream, comm=comm)
     return outputs

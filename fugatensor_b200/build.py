@@ -5,6 +5,8 @@
 Produces, next to this file:
   libfgt.so   the C-ABI backend (include/fgt.h): planner, kernel generator,
               NVRTC compilation for sm_100a, driver-API launches, NCCL (dlopen).
+  _native     the Python extension (pybind11) over libfgt's prepared programs:
+              the engine's cache-hit dispatch (CUDA graph replay).
 The device template library (csrc/fgt_device.cuh) is embedded into libfgt.so
 as text for NVRTC, and is also compiled once by nvcc for sm_100a here so
 that a template error is caught at build time rather than at first use.
@@ -94,16 +96,31 @@ def build(verbose: bool = False) -> Path:
     for src in CU_SOURCES:
         src = CSRC / src
         obj = BUILD / (src.stem + ".o")
-        if _stale(obj, [src, CSRC / "fgt_device.cuh", ROOT / "include" / "fgt.h"]):
+        if _stale(obj, [src, CSRC / "fgt_device.cuh", CSRC / "fgt_driver.h", ROOT / "include" / "fgt.h"]):
             _run([str(CUDA / "bin" / "nvcc"), *GENCODE, "-lineinfo", "-O3", "-fmad=false", "-std=c++17",
                   "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)])
         objs.append(obj)
     if _stale(LIB, objs + deps):
         _run(["g++", "-shared", "-o", str(LIB), *map(str, objs), f"-L{CUDA / 'lib64'}", "-lnvrtc", "-lcudart_static",
               "-lrt", "-ldl", "-lpthread", f"-Wl,-rpath,{CUDA / 'lib64'}", "-Wl,--no-undefined"])
+    native = _build_native()
     if verbose:
         print(f"built {LIB}")
+        print(f"built {native}")
     return LIB
+
+
+def _build_native() -> Path:
+    """The pybind11 extension _native, linked to libfgt.so beside it."""
+    import sysconfig
+    import pybind11
+    out = PKG / ("_native" + sysconfig.get_config_var("EXT_SUFFIX"))
+    src = CSRC / "fgt_native.cpp"
+    if _stale(out, [src, LIB, ROOT / "include" / "fgt.h"]):
+        _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", f"-I{pybind11.get_include()}",
+              f"-I{sysconfig.get_paths()['include']}", f"-I{ROOT / 'include'}", str(src), "-o", str(out),
+              f"-L{PKG}", "-lfgt", "-Wl,-rpath,$ORIGIN"])
+    return out
 
 
 if __name__ == "__main__":

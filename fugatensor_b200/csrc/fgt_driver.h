@@ -34,6 +34,15 @@ struct Driver {
                            void**, void**) = nullptr;
   // optional (CUDA 12.0+ drivers): a context's process-unique id
   CUresult (*CtxGetId)(CUcontext, unsigned long long*) = nullptr;
+  // optional: CUDA graphs of prepared programs (kernel-node parameters v2)
+  bool graphs = false;
+  CUresult (*GraphCreate)(CUgraph*, unsigned int) = nullptr;
+  CUresult (*GraphAddKernelNode)(CUgraphNode*, CUgraph, const CUgraphNode*, size_t, const CUDA_KERNEL_NODE_PARAMS_v2*) = nullptr;
+  CUresult (*GraphInstantiate)(CUgraphExec*, CUgraph, unsigned long long) = nullptr;
+  CUresult (*GraphExecKernelNodeSetParams)(CUgraphExec, CUgraphNode, const CUDA_KERNEL_NODE_PARAMS_v2*) = nullptr;
+  CUresult (*GraphLaunch)(CUgraphExec, CUstream) = nullptr;
+  CUresult (*GraphExecDestroy)(CUgraphExec) = nullptr;
+  CUresult (*GraphDestroy)(CUgraph) = nullptr;
 };
 
 inline Driver& drv() {
@@ -68,6 +77,18 @@ inline Driver& drv() {
     d.ok = all;
     if (!all) d.err = "libcuda.so.1 lacks a required driver entry point";
     d.CtxGetId = reinterpret_cast<decltype(d.CtxGetId)>(dlsym(h, "cuCtxGetId"));
+    auto opt = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      return fn != nullptr;
+    };
+    bool g = opt(d.GraphCreate, "cuGraphCreate");
+    g = opt(d.GraphAddKernelNode, "cuGraphAddKernelNode_v2") && g;
+    g = opt(d.GraphInstantiate, "cuGraphInstantiateWithFlags") && g;
+    g = opt(d.GraphExecKernelNodeSetParams, "cuGraphExecKernelNodeSetParams_v2") && g;
+    g = opt(d.GraphLaunch, "cuGraphLaunch") && g;
+    g = opt(d.GraphExecDestroy, "cuGraphExecDestroy") && g;
+    g = opt(d.GraphDestroy, "cuGraphDestroy") && g;
+    d.graphs = g;
   });
   return d;
 }

@@ -19,6 +19,9 @@
 #include <fstream>
 #include <memory>
 #include <mutex>
+#include <climits>
+#include <thread>
+#include <chrono>
 #include <sstream>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -160,20 +163,40 @@ Compiled compile_cubin(const std::string& name, const std::string& src, const st
 // host framework already loaded (torch bundles its own).
 typedef int nccl_result;
 typedef void* nccl_comm;
+constexpr nccl_result kNcclInProgress = 7;  // ncclInProgress
+
+// The communicator configuration in the layout of NCCL 2.17 (every later
+// NCCL reads a configuration by its declared size and version); only
+// `blocking` is set, the rest keep NCCL's defaults (the "undefined" values).
+struct CommConfig217 {
+  size_t size = sizeof(CommConfig217);
+  unsigned int magic = 0xcafebeef;
+  unsigned int version = 21700;  // NCCL_VERSION(2, 17, 0)
+  int blocking = 0;
+  int cgaClusterSize = INT_MIN;
+  int minCTAs = INT_MIN;
+  int maxCTAs = INT_MIN;
+  const char* netName = nullptr;
+  int splitShare = INT_MIN;
+};
+
 struct NcclApi {
   bool ok = false;
   std::string err;
   nccl_result (*GetUniqueId)(void*) = nullptr;
-  nccl_result (*CommInitRank)(nccl_comm*, int, const void* /*ncclUniqueId by value*/, int) = nullptr;
+  nccl_result (*CommInitRankConfig)(nccl_comm*, int, const void* /*ncclUniqueId by value*/, int, CommConfig217*) = nullptr;
   nccl_result (*CommDestroy)(nccl_comm) = nullptr;
+  nccl_result (*CommAbort)(nccl_comm) = nullptr;
+  nccl_result (*CommGetAsyncError)(nccl_comm, nccl_result*) = nullptr;
   nccl_result (*AllGather)(const void*, void*, size_t, int, nccl_comm, void*) = nullptr;
+  nccl_result (*AllReduce)(const void*, void*, size_t, int, int, nccl_comm, void*) = nullptr;
   const char* (*GetErrorString)(nccl_result) = nullptr;
 };
 
 struct UniqueId {
   char internal[128];
 };
-typedef nccl_result (*InitRankFn)(nccl_comm*, int, UniqueId, int);
+typedef nccl_result (*InitRankConfigFn)(nccl_comm*, int, UniqueId, int, CommConfig217*);
 
 NcclApi& nccl() {
   static NcclApi api;
@@ -185,18 +208,58 @@ NcclApi& nccl() {
       return;
     }
     api.GetUniqueId = (nccl_result(*)(void*))dlsym(h, "ncclGetUniqueId");
-    api.CommInitRank = (nccl_result(*)(nccl_comm*, int, const void*, int))dlsym(h, "ncclCommInitRank");
+    api.CommInitRankConfig =
+        (nccl_result(*)(nccl_comm*, int, const void*, int, CommConfig217*))dlsym(h, "ncclCommInitRankConfig");
     api.CommDestroy = (nccl_result(*)(nccl_comm))dlsym(h, "ncclCommDestroy");
+    api.CommAbort = (nccl_result(*)(nccl_comm))dlsym(h, "ncclCommAbort");
+    api.CommGetAsyncError = (nccl_result(*)(nccl_comm, nccl_result*))dlsym(h, "ncclCommGetAsyncError");
     api.AllGather = (nccl_result(*)(const void*, void*, size_t, int, nccl_comm, void*))dlsym(h, "ncclAllGather");
+    api.AllReduce = (nccl_result(*)(const void*, void*, size_t, int, int, nccl_comm, void*))dlsym(h, "ncclAllReduce");
     api.GetErrorString = (const char* (*)(nccl_result))dlsym(h, "ncclGetErrorString");
-    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.GetErrorString;
-    if (!api.ok) api.err = "libnccl.so.2 lacks a required symbol";
+    api.ok = api.GetUniqueId && api.CommInitRankConfig && api.CommDestroy && api.CommAbort && api.CommGetAsyncError &&
+             api.AllGather && api.AllReduce && api.GetErrorString;
+    if (!api.ok) api.err = "libnccl.so.2 lacks a required symbol (NCCL >= 2.17 is needed)";
   });
   return api;
 }
 
 void nccl_check(nccl_result r, const char* what) {
-  if (r != 0) fail(FGT_ERR_NCCL, std::string(what) + ": " + nccl().GetErrorString(r));
+  if (r != 0 && r != kNcclInProgress) fail(FGT_ERR_NCCL, std::string(what) + ": " + nccl().GetErrorString(r));
+}
+
+// Deadline of a communicator's host-side waits (initialisation, and each
+// collective's enqueue on the non-blocking communicator): FGT_COMM_TIMEOUT_MS,
+// default 300 s.
+int64_t comm_timeout_ms() {
+  if (const char* t = std::getenv("FGT_COMM_TIMEOUT_MS")) {
+    const long long v = std::atoll(t);
+    if (v > 0) return v;
+  }
+  return 300000;
+}
+
+// Wait until a non-blocking communicator leaves ncclInProgress. On an error
+// or when the deadline passes the communicator is aborted (it is unusable
+// afterwards) and FGT_ERR_NCCL is raised.
+void nccl_wait(nccl_comm& comm, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  const int64_t limit = comm_timeout_ms();
+  for (;;) {
+    nccl_result state = 0;
+    const nccl_result r = nccl().CommGetAsyncError(comm, &state);
+    if (r != 0) state = r;
+    if (state == 0) return;
+    const int64_t waited =
+        std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (state != kNcclInProgress || waited >= limit) {
+      nccl().CommAbort(comm);
+      comm = nullptr;
+      if (state != kNcclInProgress) fail(FGT_ERR_NCCL, std::string(what) + ": " + nccl().GetErrorString(state));
+      fail(FGT_ERR_NCCL, std::string(what) + ": timed out after " + std::to_string(waited) +
+                             " ms (FGT_COMM_TIMEOUT_MS); communicator aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
 }
 
 }  // namespace
@@ -222,6 +285,26 @@ struct fgt_spec {
 struct fgt_comm {
   fgt::nccl_comm comm = nullptr;
   int world = 1, rank = 0;
+};
+
+// A prepared program: per CUDA context, the spec's kernels as one
+// instantiated CUDA graph (a chain of kernel nodes in launch order).
+struct fgt_program {
+  fgt_spec* spec = nullptr;
+  bool use_graph = true;
+  std::mutex mu;
+  struct Instance {
+    CUgraph graph = nullptr;
+    CUgraphExec exec = nullptr;
+    std::vector<CUgraphNode> nodes;
+  };
+  std::map<CUcontext, Instance> instances;
+  ~fgt_program() {
+    for (auto& kv : instances) {
+      if (kv.second.exec) fgt::drv().GraphExecDestroy(kv.second.exec);
+      if (kv.second.graph) fgt::drv().GraphDestroy(kv.second.graph);
+    }
+  }
 };
 
 namespace fgt {
@@ -350,9 +433,31 @@ void check_ptr(const void* p, int64_t bytes, const std::string& what) {
   require(((uintptr_t)p % 16) == 0, what + " must be 16-byte aligned");
 }
 
-void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* const* outputs, void* ws, size_t ws_bytes,
-                void* stream) {
-  const Plan& p = s->plan;
+// One kernel launch of a spec: the kernel, its grid, and the partial count
+// of the kernel whose partials it combines (0 if none).
+struct Step {
+  size_t idx;
+  unsigned grid, gy;
+  long long nparts;
+};
+
+std::vector<Step> plan_steps(const Plan& p, const LoadedModule& lm) {
+  std::vector<Step> steps;
+  std::vector<int64_t> parts(p.kernels.size(), 0);
+  for (size_t i = 0; i < p.kernels.size(); ++i) {
+    const KernelDef& k = p.kernels[i];
+    long long nparts = 0;
+    if (k.producer >= 0) nparts = parts[k.producer];
+    if (empty_kernel(k)) continue;
+    int64_t grid = grid_for(k, lm, i);
+    parts[i] = k.kind == KKind::ROW ? grid / k.cluster * k.rows_per_cta : grid;
+    const unsigned gy = k.kind == KKind::ROW ? (unsigned)std::max<int64_t>(1, k.col_tiles) : 1u;
+    steps.push_back(Step{i, (unsigned)grid, gy, nparts});
+  }
+  return steps;
+}
+
+void validate_buffers(const Plan& p, const void* const* inputs, void* const* outputs, void* ws, size_t ws_bytes) {
   require((int64_t)ws_bytes >= p.workspace_bytes, "workspace of " + std::to_string(ws_bytes) + " bytes is smaller than the " +
                                                       std::to_string(p.workspace_bytes) + " bytes the partition needs",
           FGT_ERR_WORKSPACE);
@@ -365,24 +470,29 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
     const Node& n = p.g.nodes[p.g.outputs[i]];
     check_ptr(outputs ? outputs[i] : nullptr, n.n() * dtype_size(n.dt), "output " + std::to_string(i));
   }
+}
+
+void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* const* outputs, void* ws, size_t ws_bytes,
+                void* stream) {
+  const Plan& p = s->plan;
+  validate_buffers(p, inputs, outputs, ws, ws_bytes);
   if (!p.collectives.empty()) {
     require(comm != nullptr, "this spec reduces over the sharded dimension: launch it with fgt_spec_launch_sharded");
     require(comm->world == p.opt.world && comm->rank == p.opt.rank, "communicator rank/world differ from the spec's shard options");
+    // a communicator that failed or timed out earlier launches nothing
+    require(comm->comm != nullptr, "the communicator failed earlier and was aborted", FGT_ERR_NCCL);
+    nccl_result state = 0;
+    nccl_check(nccl().CommGetAsyncError(comm->comm, &state), "ncclCommGetAsyncError");
+    require(state == 0, std::string("communicator error before launch: ") + nccl().GetErrorString(state), FGT_ERR_NCCL);
   }
   LoadedModule& lm = module_for(s);
   CUstream st = (CUstream)stream;
-  std::vector<int64_t> parts(p.kernels.size(), 0);
-  for (size_t i = 0; i < p.kernels.size(); ++i) {
+  for (const Step& sp : plan_steps(p, lm)) {
+    const size_t i = sp.idx;
     const KernelDef& k = p.kernels[i];
-    long long nparts = 0;
-    if (k.producer >= 0) nparts = parts[k.producer];
-    if (empty_kernel(k)) continue;
-    int64_t grid = grid_for(k, lm, i);
-    parts[i] = k.kind == KKind::ROW ? grid / k.cluster * k.rows_per_cta : grid;
-    ArgBlock a = make_args(p, inputs, outputs, ws, nparts);
+    ArgBlock a = make_args(p, inputs, outputs, ws, sp.nparts);
     void* params[] = {a.bytes.data()};
-    const unsigned gy = k.kind == KKind::ROW ? (unsigned)std::max<int64_t>(1, k.col_tiles) : 1u;
-    cu_check(drv().LaunchKernel(lm.fn[i], (unsigned)grid, gy, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
+    cu_check(drv().LaunchKernel(lm.fn[i], sp.grid, sp.gy, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
                                 nullptr),
              "cuLaunchKernel");
     for (int c : p.collectives) {
@@ -391,6 +501,7 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
       nccl_check(nccl().AllGather(base + k.send_offset, base + k.recv_offset, (size_t)k.record_bytes, /*ncclChar*/ 0,
                                   comm->comm, stream),
                  "ncclAllGather");
+      nccl_wait(comm->comm, "ncclAllGather");
     }
   }
 }
@@ -619,6 +730,90 @@ fgt_status fgt_spec_launch(const fgt_spec* spec, const void* const* inputs, void
   return guarded([&] { launch_all(const_cast<fgt_spec*>(spec), nullptr, inputs, outputs, workspace, workspace_bytes, stream); });
 }
 
+fgt_status fgt_program_create(const fgt_spec* spec, int32_t use_graph, fgt_program** out) {
+  if (!out) return set_error(FGT_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  if (!spec) return set_error(FGT_ERR_INVALID, "spec is NULL");
+  return guarded([&] {
+    require(spec->plan.collectives.empty(),
+            "this spec reduces over the sharded dimension: launch it with fgt_spec_launch_sharded", FGT_ERR_UNSUPPORTED);
+    auto p = std::make_unique<fgt_program>();
+    p->spec = const_cast<fgt_spec*>(spec);
+    p->use_graph = use_graph != 0;
+    *out = p.release();
+  });
+}
+
+fgt_status fgt_program_run(fgt_program* program, const void* const* inputs, void* const* outputs, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!program) return set_error(FGT_ERR_INVALID, "program is NULL");
+  return guarded([&] {
+    fgt_spec* s = program->spec;
+    const Plan& p = s->plan;
+    if (!program->use_graph || !drv().graphs) {
+      launch_all(s, nullptr, inputs, outputs, workspace, workspace_bytes, stream);
+      return;
+    }
+    validate_buffers(p, inputs, outputs, workspace, workspace_bytes);
+    LoadedModule& lm = module_for(s);
+    CUcontext ctx = nullptr;
+    cu_check(drv().CtxGetCurrent(&ctx), "cuCtxGetCurrent");
+    const std::vector<Step> steps = plan_steps(p, lm);
+    std::lock_guard<std::mutex> lock(program->mu);
+    fgt_program::Instance& in = program->instances[ctx];
+    // kernel-node parameters of this run: the run's buffers in each kernel's
+    // argument block (copied by the driver when set)
+    std::vector<ArgBlock> args;
+    std::vector<void*> kp(steps.size());
+    std::vector<CUDA_KERNEL_NODE_PARAMS_v2> np(steps.size());
+    args.reserve(steps.size());
+    for (size_t j = 0; j < steps.size(); ++j) {
+      const Step& sp = steps[j];
+      const KernelDef& k = p.kernels[sp.idx];
+      args.push_back(make_args(p, inputs, outputs, workspace, sp.nparts));
+      kp[j] = args.back().bytes.data();
+      CUDA_KERNEL_NODE_PARAMS_v2 q;
+      std::memset(&q, 0, sizeof q);
+      q.func = lm.fn[sp.idx];
+      q.gridDimX = sp.grid;
+      q.gridDimY = sp.gy;
+      q.gridDimZ = 1;
+      q.blockDimX = (unsigned)k.nt;
+      q.blockDimY = q.blockDimZ = 1;
+      q.sharedMemBytes = (unsigned)k.smem_bytes;
+      q.kernelParams = &kp[j];
+      np[j] = q;
+    }
+    if (steps.empty()) return;
+    if (!in.exec) {
+      cu_check(drv().GraphCreate(&in.graph, 0), "cuGraphCreate");
+      CUgraphNode prev = nullptr;
+      for (size_t j = 0; j < steps.size(); ++j) {
+        CUgraphNode node = nullptr;
+        cu_check(drv().GraphAddKernelNode(&node, in.graph, prev ? &prev : nullptr, prev ? 1 : 0, &np[j]),
+                 "cuGraphAddKernelNode");
+        in.nodes.push_back(node);
+        prev = node;
+      }
+      cu_check(drv().GraphInstantiate(&in.exec, in.graph, 0), "cuGraphInstantiate");
+    } else {
+      require(in.nodes.size() == steps.size(), "internal: program graph changed shape", FGT_ERR_CUDA);
+      for (size_t j = 0; j < steps.size(); ++j)
+        cu_check(drv().GraphExecKernelNodeSetParams(in.exec, in.nodes[j], &np[j]), "cuGraphExecKernelNodeSetParams");
+    }
+    cu_check(drv().GraphLaunch(in.exec, (CUstream)stream), "cuGraphLaunch");
+  });
+}
+
+int32_t fgt_program_kernel_count(const fgt_program* program) {
+  if (!program) return 0;
+  int32_t n = 0;
+  for (const KernelDef& k : program->spec->plan.kernels) n += empty_kernel(k) ? 0 : 1;
+  return n;
+}
+
+void fgt_program_destroy(fgt_program* program) { delete program; }
+
 fgt_status fgt_comm_unique_id(uint8_t id[128]) {
   return guarded([&] {
     require(id != nullptr, "id is NULL");
@@ -639,8 +834,18 @@ fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, f
     c->rank = rank;
     UniqueId uid;
     std::memcpy(uid.internal, id, 128);
-    InitRankFn init = (InitRankFn)(void*)nccl().CommInitRank;
-    nccl_check(init(&c->comm, world, uid, rank), "ncclCommInitRank");
+    // non-blocking: initialisation proceeds in the background and is polled
+    // against the deadline, so a rank that never joins ends in an error here
+    // instead of a wait without end
+    CommConfig217 cfg;
+    InitRankConfigFn init = (InitRankConfigFn)(void*)nccl().CommInitRankConfig;
+    const nccl_result r = init(&c->comm, world, uid, rank, &cfg);
+    if (r != 0 && r != kNcclInProgress) {
+      if (c->comm) nccl().CommAbort(c->comm);
+      c->comm = nullptr;
+      fail(FGT_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + nccl().GetErrorString(r));
+    }
+    nccl_wait(c->comm, "ncclCommInitRankConfig");
     *out = c.release();
   });
 }

@@ -9,9 +9,12 @@ session ``stats`` (launches, program_submissions).
 
 ``evaluate`` joins the requested pending tensors into ONE partition (as
 _lazy.materialize does, src/fugatensor/_lazy.py:200-221), keys it
-structurally, and on a cache hit goes straight to the compiled spec's
-launch (the role of materialize_cached, cpp/lazy.cpp:871-1008). There is no
-CPU path and no fallback: a device without the native library raises.
+structurally, and on a cache hit goes straight to the partition's prepared
+program (the role of materialize_cached -> ProgramPorts::runFastCore,
+cpp/lazy.cpp:871-1008, 946-948): the native extension runs it with the GIL
+released, and a plan of two or more kernels replays as one CUDA graph (the
+reference prepares every program with graph=True, engine.py:416-423). There
+is no CPU path and no fallback: a device without the native library raises.
 """
 from __future__ import annotations
 
@@ -48,9 +51,10 @@ class Engine:
         self.tune = tune
         self._lock = threading.RLock()
         self._cache = {}
+        self._programs = {}
         self._stream_cache = {}
         self._stats = {"compilations": 0, "cache_hits": 0}
-        self.stats = {"launches": 0, "program_submissions": 0}
+        self.stats = {"launches": 0, "program_submissions": 0, "graph_replays": 0}
         self.last_execution_plan = None
         self.last_report = None
         self.last_spec = None
@@ -158,6 +162,14 @@ class Engine:
             self._stats["cache_hits"] += 1
         return spec
 
+    def _program(self, key, spec):
+        """The prepared program of a cached spec (graph replay for multi-kernel plans)."""
+        from . import _fgt
+        prog = self._programs.get(key)
+        if prog is None or prog.spec is not spec:
+            prog = self._programs[key] = _fgt.Program(spec, graph=spec.kernel_count > 1)
+        return prog
+
     def evaluate(self, *tensors):
         """Compile and materialise the requested tensors together."""
         import torch
@@ -169,10 +181,11 @@ class Engine:
             if not torch.cuda.is_available():
                 raise _fgt.CUDAError(4, "no CUDA device: fugatensor_b200 has no CPU execution path")
             spec = self._spec(desc)
+            prog = self._program(desc.key(), spec)
             device = torch.device(self.device)
             inputs = [t._data if t._data.device == device else t._data.to(device) for t in leaves]
             with torch.cuda.device(device):
-                outs = _fgt.run(spec, *inputs)
+                outs = _fgt.run(spec, *inputs, program=prog)
             for r, o in zip(roots, outs):
                 r._data = o
                 r._expr = None
@@ -183,6 +196,7 @@ class Engine:
             self.last_spec = spec
             self.stats["launches"] += spec.kernel_count
             self.stats["program_submissions"] += 1
+            self.stats["graph_replays"] += 1 if prog.graph else 0
             return tensors[0] if len(tensors) == 1 else tensors
 
     def evaluate_host(self, *tensors):
@@ -233,6 +247,7 @@ class Engine:
     def clear_cache(self):
         with self._lock:
             self._cache.clear()
+            self._programs.clear()
             self._stream_cache.clear()
             self.last_execution_plan = self.last_report = self.last_spec = None
 

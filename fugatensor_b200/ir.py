@@ -408,7 +408,7 @@ class CPartition(ctypes.Structure):
                 ("outputs", ctypes.POINTER(ctypes.c_int32))]
 
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class Descriptor:

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FGT_ABI_VERSION 4
+#define FGT_ABI_VERSION 5
 #define FGT_MAX_RANK 8
 #define FGT_MAX_OPERANDS 3
 #define FGT_MAX_ATTRS 24
@@ -221,6 +221,36 @@ fgt_status fgt_spec_kernel_source(const fgt_spec* spec, int32_t index, char* buf
 fgt_status fgt_spec_launch(const fgt_spec* spec, const void* const* inputs, void* const* outputs,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- prepared programs: CUDA graph replay ------------------------------- */
+
+typedef struct fgt_program fgt_program;  /* opaque: a spec prepared for replay */
+
+/* Prepare `spec` for repeated runs. With use_graph != 0 the first run on a
+ * CUDA context instantiates the spec's kernels as one CUDA graph (a chain of
+ * kernel nodes); every later run writes its buffers into the graph's kernel
+ * nodes and replays it with one cuGraphLaunch. use_graph = 0 launches the
+ * kernels one by one, as fgt_spec_launch. Replaces
+ * PreparedCUDAProgram(..., graph=True) -> prepare_program
+ * (src/fugatensor/_ask/executable.py:120-152, cpp/ask_runtime.cpp:789-843)
+ * and its cached dispatch ProgramPorts::runFastCore
+ * (cpp/ask_runtime.cpp:412-463, called at cpp/lazy.cpp:946-948).
+ * The spec must outlive the program. Specs that reduce over a sharded
+ * dimension (collectives) are rejected with FGT_ERR_UNSUPPORTED. */
+fgt_status fgt_program_create(const fgt_spec* spec, int32_t use_graph, fgt_program** out);
+
+/* Run the program on `stream`: same buffer contract and validation as
+ * fgt_spec_launch (checked before anything is enqueued). Runs of one
+ * program from several threads are serialised on the program's lock. The
+ * first graph run on a context instantiates the graph (host and driver
+ * resources): make it outside any stream capture. */
+fgt_status fgt_program_run(fgt_program* program, const void* const* inputs, void* const* outputs, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Kernels one run launches (graph nodes). */
+int32_t fgt_program_kernel_count(const fgt_program* program);
+
+void fgt_program_destroy(fgt_program* program);
+
 /* ---- leading-dimension sharding across GPUs (one process per GPU) ------- */
 
 /* 128-byte NCCL unique id, created on one rank and shared by the caller. */
@@ -228,7 +258,12 @@ fgt_status fgt_comm_unique_id(uint8_t id[128]);
 
 /* Join a communicator of `world` ranks on the current device. No reference
  * counterpart: the reference binds one Engine to one device
- * (src/fugatensor/engine.py:145,237-239). */
+ * (src/fugatensor/engine.py:145,237-239). The communicator is non-blocking:
+ * initialisation and every later collective enqueue are polled against a
+ * deadline of FGT_COMM_TIMEOUT_MS milliseconds (environment, default 300000).
+ * A rank that never joins, or an NCCL error, ends in FGT_ERR_NCCL and the
+ * communicator is aborted; a sharded launch on an aborted or failed
+ * communicator returns FGT_ERR_NCCL before launching any kernel. */
 fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, fgt_comm** out);
 
 void fgt_comm_destroy(fgt_comm* comm);
