@@ -271,13 +271,25 @@ def run_fgt(args):
 
     clk.__exit__(None, None, None)
 
+    # ---- strong scaling: the same global problems at every N -- c4's 2^31-element
+    # reductions and c3's LayerNorm VJP with dgamma/dbeta over all 32768 rows.
+    # N = 1 runs them unsharded (the partition table's entries); N > 1 splits
+    # dim 0 over the ranks and combines the reductions over it across ranks.
+    STRONG = (("c4", "global_reductions", "f32"), ("c3", "layernorm_vjp", "bf16"))
+    strong = {}
+    if world == 1:
+        for c, v, dt in STRONG:
+            e = partitions.get(f"{c}/{v}/{dt}")
+            if e:
+                strong[f"{c}/{v}/{dt}"] = {"n_gpus": 1, "global_shape": e["shape"], "ms": e["ms"], "GB/s": e["GB/s"],
+                                           "per_gpu_frac": e["frac"], "kernels": e["kernels"], "collectives": 0}
     # ---- sharded partitions (N > 1): the global problem split along dim 0,
-    # reductions over it combined by one NCCL all-gather (strong scaling)
+    # reductions over it combined across ranks (strong scaling)
     if world > 1 and not args.skip_table:
         from fugatensor_b200 import sharded
         group = sharded.ShardGroup(world, rank)
         peak_, _ = measured_peak()
-        for c, v, dt in (("c4", "global_reductions", "f32"), ("c3", "layernorm_vjp", "bf16")):
+        for c, v, dt in STRONG:
             r, h = W.FULL[c]
             tt = device_inputs(c, r // world, h, dt, device, seed=rank)
             dts = W.input_dtypes(c, dt)
@@ -306,10 +318,11 @@ def run_fgt(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
             nb = W.algorithmic_bytes(c, v, r, h, dt)
-            partitions[f"{c}/{v}/{dt}/sharded{world}"] = {
-                "global_shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
-                "per_gpu_frac": round(nb / ms / 1e6 / world / peak_, 4), "kernels": spec.kernel_count,
-                "collectives": spec.collective_count, "scaling": "strong"}
+            entry = {"n_gpus": world, "global_shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
+                     "per_gpu_frac": round(nb / ms / 1e6 / world / peak_, 4), "kernels": spec.kernel_count,
+                     "collectives": spec.collective_count}
+            partitions[f"{c}/{v}/{dt}/sharded{world}"] = dict(entry, scaling="strong")
+            strong[f"{c}/{v}/{dt}"] = entry
             del tt, ins, outs, ws
             torch.cuda.empty_cache()
         group.close()
@@ -402,6 +415,7 @@ def run_fgt(args):
         "clocks": clocks,
         "e2e": e2e,
         "partitions": partitions,
+        "strong_scaling": strong,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)

@@ -77,6 +77,8 @@ lib.fgt_comm_unique_id.argtypes = [ctypes.POINTER(ctypes.c_uint8)]
 lib.fgt_comm_create.argtypes = [ctypes.POINTER(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(_vp)]
 lib.fgt_comm_destroy.argtypes = [_vp]
 lib.fgt_comm_destroy.restype = None
+lib.fgt_comm_peer_exchange.argtypes = [_vp]
+lib.fgt_comm_peer_exchange.restype = ctypes.c_int32
 lib.fgt_spec_launch_sharded.argtypes = [_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, ctypes.c_size_t, _vp]
 lib.fgt_program_create.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(_vp)]
 lib.fgt_program_run.argtypes = [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, ctypes.c_size_t, _vp]
@@ -87,7 +89,8 @@ lib.fgt_program_destroy.restype = None
 
 EXPORTED = ("fgt_last_error", "fgt_abi_version", "fgt_spec_create", "fgt_spec_destroy", "fgt_spec_get_info",
             "fgt_spec_port", "fgt_spec_plan_json", "fgt_spec_kernel_source", "fgt_spec_launch",
-            "fgt_comm_unique_id", "fgt_comm_create", "fgt_comm_destroy", "fgt_spec_launch_sharded",
+            "fgt_comm_unique_id", "fgt_comm_create", "fgt_comm_peer_exchange", "fgt_comm_destroy",
+            "fgt_spec_launch_sharded",
             "fgt_program_create", "fgt_program_run", "fgt_program_kernel_count", "fgt_program_destroy",
             "fgt_reduce_f32_noalloc")
 
@@ -202,6 +205,8 @@ class Comm:
         check(lib.fgt_comm_create(buf, world, rank, ctypes.byref(handle)))
         self._h = handle
         self.world, self.rank = world, rank
+        # records of reductions over the sharded dimension: peer mailboxes (NVLink) or NCCL
+        self.peer_exchange = bool(lib.fgt_comm_peer_exchange(handle))
 
     @staticmethod
     def unique_id() -> bytes:

@@ -1103,8 +1103,13 @@ struct Emitter {
   std::string args_struct() {
     const int nin = std::max<int>(1, (int)g.input_nodes.size());
     const int nout = std::max<int>(1, (int)g.outputs.size());
+    // kernels exchanging records through the peer mailboxes also get every
+    // rank's mailbox, the communicator's status word, this rank and the wait limit
+    const std::string x = K.fin_stage == 3 ? " unsigned char* xmb[" + std::to_string(kXMaxWorld) +
+                                                 "]; unsigned* xstat; long long xrank; unsigned long long xlimit;"
+                                           : "";
     return "struct FgtArgs { const void* in[" + std::to_string(nin) + "]; void* out[" + std::to_string(nout) +
-           "]; unsigned char* ws; long long nparts; long long pad_; };\n";
+           "]; unsigned char* ws; long long nparts; long long pad_;" + x + " };\n";
   }
 
   static void put(std::ostringstream& o, const std::vector<std::string>& v, const std::string& ind) {
@@ -1780,21 +1785,27 @@ struct Emitter {
 
   // Combine partials for reduction rd into `a` (+ `a`i), per element e.
   std::string fin_combine(const RedDef& rd, const RedText& t, const std::string& src_t, const std::string& a,
-                          const std::string& e, const std::string& count, int stage, int64_t rec_off) {
+                          const std::string& e, const std::string& count, int stage, int64_t rec_off, bool xchg = false) {
     std::ostringstream s;
     const std::string M = std::to_string(rd.M);
     if (stage == 2) {
-      std::string recb = "(p.ws+" + std::to_string(K.recv_offset) + "LL)";
-      std::string pv = "((const " + t.part_t + "*)(" + recb + "+(fgt_i64)w_*" + std::to_string(K.record_bytes) + "LL+" +
-                       std::to_string(rec_off) + "LL))";
-      std::string pi = "((const fgt_i64*)(" + recb + "+(fgt_i64)w_*" + std::to_string(K.record_bytes) + "LL+" +
-                       std::to_string(rec_off + rd.M * 8) + "LL))";
-      std::string lo = rd.combine_ranks ? "0" : std::to_string(P.opt.rank);
-      std::string hi = rd.combine_ranks ? std::to_string(P.opt.world) : std::to_string(P.opt.rank + 1);
+      // ranks' records: gathered by NCCL into the workspace, or (xchg) delivered
+      // by the ranks into this rank's mailbox, read past L1 (written by peers)
+      std::string recb = xchg ? "(p.xmb[p.xrank]+" + std::to_string(kXDataOff) + "LL+(fgt_i64)(xe_ & 1u)*" +
+                                    std::to_string(kXMaxWorld * kXSlot) + "LL)"
+                              : "(p.ws+" + std::to_string(K.recv_offset) + "LL)";
+      const std::string stride = std::to_string(xchg ? kXSlot : K.record_bytes);
+      std::string pv = "((const " + t.part_t + "*)(" + recb + "+(fgt_i64)w_*" + stride + "LL+" + std::to_string(rec_off) + "LL))";
+      std::string pi = "((const fgt_i64*)(" + recb + "+(fgt_i64)w_*" + stride + "LL+" + std::to_string(rec_off + rd.M * 8) +
+                       "LL))";
+      const std::string ld0 = xchg ? "__ldcg(&" : "", ld1 = xchg ? ")" : "";
+      std::string lo = rd.combine_ranks ? "0" : (xchg ? "(int)p.xrank" : std::to_string(P.opt.rank));
+      std::string hi = rd.combine_ranks ? std::to_string(P.opt.world) : (xchg ? "(int)p.xrank + 1" : std::to_string(P.opt.rank + 1));
       s << "for (int w_ = " << lo << "; w_ < " << hi << "; ++w_) { ";
-      if (t.arg) s << "{ const " << t.part_t << " ov = " << pv << "[" << e << "]; const fgt_i64 oi = " << pi << "[" << e << "]; "
-                   << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
-      else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << pv << "[" << e << "]; " << comb_stmt(t, a, "ov") << " }";
+      if (t.arg) s << "{ const " << t.part_t << " ov = " << ld0 << pv << "[" << e << "]" << ld1 << "; const fgt_i64 oi = " << ld0
+                   << pi << "[" << e << "]" << ld1 << "; " << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
+      else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << ld0 << pv << "[" << e << "]" << ld1 << "; "
+             << comb_stmt(t, a, "ov") << " }";
       s << " }";
       return s.str();
     }
@@ -1818,7 +1829,8 @@ struct Emitter {
     post.assign(1, {});
     const bool col = K.kind == KKind::COLFIN;
     const int stage = K.fin_stage;
-    std::vector<std::string> comb, rec_write;
+    const bool xchg = stage == 3;  // stages 1 and 2 with the records exchanged through the peer mailboxes
+    std::vector<std::string> comb, rec_write, comb2;
     std::vector<std::pair<RedText, std::string>> accs;
     std::vector<std::string> finals;
     int64_t rec_off = 0;
@@ -1829,10 +1841,16 @@ struct Emitter {
       std::string a = fresh("fa");
       comb.push_back(t.fin_t + " " + a + " = " + t.ident + ";");
       if (t.arg) comb.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
-      comb.push_back(fin_combine(rd, t, src_t, a, col ? "e" : "0", "p.nparts", stage, rec_off));
+      comb.push_back(fin_combine(rd, t, src_t, a, col ? "e" : "0", "p.nparts", xchg ? 1 : stage, rec_off));
       accs.push_back({t, a});
-      if (stage == 1) {
-        std::string recb = "(p.ws+" + std::to_string(K.send_offset) + "LL+" + std::to_string(rec_off) + "LL)";
+      if (xchg) {
+        comb2.push_back(t.fin_t + " " + a + " = " + t.ident + ";");
+        if (t.arg) comb2.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
+        comb2.push_back(fin_combine(rd, t, src_t, a, col ? "e" : "0", "p.nparts", 2, rec_off, true));
+      }
+      if (stage == 1 || xchg) {
+        std::string recb = xchg ? "(xrec_+" + std::to_string(rec_off) + "LL)"
+                                : "(p.ws+" + std::to_string(K.send_offset) + "LL+" + std::to_string(rec_off) + "LL)";
         rec_write.push_back("((" + t.part_t + "*)" + recb + ")[" + (col ? "e" : "0") + "] = (" + t.part_t + ")" + a + ";");
         if (t.arg)
           rec_write.push_back("((fgt_i64*)(" + recb + "+" + std::to_string(rd.M * 8) + "LL))[" + (col ? "e" : "0") + "] = " + a + "i;");
@@ -1861,6 +1879,67 @@ struct Emitter {
     o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
     o << "  const int tid = threadIdx.x; const fgt_i64 r = 0; const bool rv = true; (void)r; (void)rv;\n";
     put(o, kdecl, "  ");
+    if (xchg) {
+      // Exchange of this CTA's record through the peer mailboxes: the record is
+      // stored into every rank's data[epoch % 2][this rank] (NVLink stores for
+      // peers), each writer fences at system scope, then one thread raises
+      // flag[this rank][CTA] = epoch on every rank and waits, bounded by
+      // p.xlimit ns, until every rank's flag here has reached the epoch
+      // (a timeout marks the communicator's status word and goes on).
+      const std::string W = std::to_string(P.opt.world), MW = std::to_string(kXMaxWorld), MC = std::to_string(kXMaxCtas);
+      const std::string slot = "p.xmb[k_]+" + std::to_string(kXDataOff) + "LL+((fgt_i64)(xe_ & 1u)*" + MW +
+                               "+p.xrank)*" + std::to_string(kXSlot) + "LL";
+      auto push = [&](const std::string& ind) {
+        o << ind << "for (int k_ = 0; k_ < " << W << "; ++k_) {\n";
+        o << ind << "  unsigned char* const xrec_ = " << slot << ";\n";
+        put(o, rec_write, ind + "  ");
+        o << ind << "}\n";
+      };
+      auto flags_and_wait = [&]() {
+        o << "  if (tid == 0) {\n";
+        o << "    for (int k_ = 0; k_ < " << W << "; ++k_)\n";
+        o << "      fgt_st_release_sys((unsigned*)(p.xmb[k_]+" << kXFlagOff << "LL) + p.xrank * " << MC << " + blockIdx.x, xe_);\n";
+        o << "    const unsigned long long t0_ = fgt_globaltimer();\n";
+        o << "    for (int k_ = 0; k_ < " << W << "; ++k_)\n";
+        o << "      if (!fgt_xwait((const unsigned*)(p.xmb[p.xrank]+" << kXFlagOff << "LL) + k_ * " << MC
+          << " + blockIdx.x, xe_, t0_, p.xlimit)) { fgt_xfail(p.xstat); break; }\n";
+        o << "    ((unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] = xe_;\n";
+        o << "  }\n";
+        o << "  __syncthreads();\n  __threadfence_system();\n";
+      };
+      o << "  __shared__ unsigned xep_;\n";
+      o << "  if (tid == 0) xep_ = ((const unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] + 1u;\n";
+      o << "  __syncthreads();\n  const unsigned xe_ = xep_;\n";
+      if (col) {
+        o << "  const fgt_i64 NI = " << d.NI << "LL;\n";
+        o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
+        o << "    " << digits_i() << "\n";
+        put(o, comb, "    ");
+        push("    ");
+        o << "  }\n  __threadfence_system();\n  __syncthreads();\n";
+        flags_and_wait();
+        o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
+        o << "    " << digits_i() << "\n";
+        put(o, comb2, "    ");
+        put(o, finals, "    ");
+        put(o, lane[0], "    ");
+        o << "  }\n}\n";
+        return o.str();
+      }
+      o << "  const fgt_i64 e = 0; (void)e;\n";
+      put(o, comb, "  ");
+      put(o, red_code, "  ");
+      o << "  if (tid == 0) {\n";
+      push("    ");
+      o << "    __threadfence_system();\n  }\n";
+      flags_and_wait();
+      o << "  if (tid != 0) return;\n  {\n";
+      put(o, comb2, "    ");
+      put(o, finals, "    ");
+      put(o, lane[0], "    ");
+      o << "  }\n}\n";
+      return o.str();
+    }
     if (col) {
       o << "  const fgt_i64 NI = " << d.NI << "LL;\n";
       o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";

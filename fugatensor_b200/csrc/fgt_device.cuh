@@ -213,6 +213,35 @@ FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // 16-bit element v of a packed row piece (two values per 32-bit word, the
 // lower index in the low half)
 template <int N> FGT_DEV fgt_u16 fgt_h16(const fgt_u32 (&w)[N], int v) { return (fgt_u16)(w[v >> 1] >> ((v & 1) * 16)); }
+// ---- peer mailboxes (records exchanged between ranks over NVLink) --------
+FGT_DEV unsigned fgt_ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+FGT_DEV void fgt_st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+FGT_DEV unsigned long long fgt_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Wait until *flag has reached epoch `ep` (wrapping compare); false when
+// `limit_ns` passed since t0 first (the caller records the failure and goes on).
+FGT_DEV bool fgt_xwait(const unsigned* flag, unsigned ep, unsigned long long t0, unsigned long long limit_ns) {
+  while ((int)(fgt_ld_acquire_sys(flag) - ep) < 0) {
+    if (fgt_globaltimer() - t0 > limit_ns) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+// A failed exchange: the host-mapped status word of the communicator.
+FGT_DEV void fgt_xfail(unsigned* status) {
+  *(volatile unsigned*)status = 1u;
+  __threadfence_system();
+}
+
 // Element v of a packed 16-bit array (v a compile-time constant after unrolling).
 template <int N> FGT_DEV void fgt_set_h16(fgt_u32 (&w)[N], int v, fgt_u16 h) {
   w[v >> 1] = (v & 1) ? ((w[v >> 1] & 0xffffu) | ((fgt_u32)h << 16)) : ((w[v >> 1] & 0xffff0000u) | (fgt_u32)h);

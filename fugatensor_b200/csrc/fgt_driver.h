@@ -43,6 +43,22 @@ struct Driver {
   CUresult (*GraphLaunch)(CUgraphExec, CUstream) = nullptr;
   CUresult (*GraphExecDestroy)(CUgraphExec) = nullptr;
   CUresult (*GraphDestroy)(CUgraph) = nullptr;
+  CUresult (*StreamIsCapturing)(CUstream, CUstreamCaptureStatus*) = nullptr;
+  // optional: peer mailboxes of communicators (device memory shared between
+  // the ranks' processes through CUDA IPC, and a host-mapped status word)
+  bool ipc = false;
+  CUresult (*MemAlloc)(CUdeviceptr*, size_t) = nullptr;
+  CUresult (*MemFree)(CUdeviceptr) = nullptr;
+  CUresult (*MemsetD8)(CUdeviceptr, unsigned char, size_t) = nullptr;
+  CUresult (*MemcpyHtoD)(CUdeviceptr, const void*, size_t) = nullptr;
+  CUresult (*MemcpyDtoH)(void*, CUdeviceptr, size_t) = nullptr;
+  CUresult (*IpcGetMemHandle)(CUipcMemHandle*, CUdeviceptr) = nullptr;
+  CUresult (*IpcOpenMemHandle)(CUdeviceptr*, CUipcMemHandle, unsigned int) = nullptr;
+  CUresult (*IpcCloseMemHandle)(CUdeviceptr) = nullptr;
+  CUresult (*MemHostAlloc)(void**, size_t, unsigned int) = nullptr;
+  CUresult (*MemHostGetDevicePointer)(CUdeviceptr*, void*, unsigned int) = nullptr;
+  CUresult (*MemFreeHost)(void*) = nullptr;
+  CUresult (*CtxSynchronize)() = nullptr;
 };
 
 inline Driver& drv() {
@@ -88,7 +104,21 @@ inline Driver& drv() {
     g = opt(d.GraphLaunch, "cuGraphLaunch") && g;
     g = opt(d.GraphExecDestroy, "cuGraphExecDestroy") && g;
     g = opt(d.GraphDestroy, "cuGraphDestroy") && g;
+    g = opt(d.StreamIsCapturing, "cuStreamIsCapturing") && g;
     d.graphs = g;
+    bool ip = opt(d.MemAlloc, "cuMemAlloc_v2");
+    ip = opt(d.MemFree, "cuMemFree_v2") && ip;
+    ip = opt(d.MemsetD8, "cuMemsetD8_v2") && ip;
+    ip = opt(d.MemcpyHtoD, "cuMemcpyHtoD_v2") && ip;
+    ip = opt(d.MemcpyDtoH, "cuMemcpyDtoH_v2") && ip;
+    ip = opt(d.IpcGetMemHandle, "cuIpcGetMemHandle") && ip;
+    ip = opt(d.IpcOpenMemHandle, "cuIpcOpenMemHandle_v2") && ip;
+    ip = opt(d.IpcCloseMemHandle, "cuIpcCloseMemHandle") && ip;
+    ip = opt(d.MemHostAlloc, "cuMemHostAlloc") && ip;
+    ip = opt(d.MemHostGetDevicePointer, "cuMemHostGetDevicePointer_v2") && ip;
+    ip = opt(d.MemFreeHost, "cuMemFreeHost") && ip;
+    ip = opt(d.CtxSynchronize, "cuCtxSynchronize") && ip;
+    d.ipc = ip;
   });
   return d;
 }

@@ -1222,9 +1222,19 @@ struct Planner {
       f2.record_bytes = rec;
       f2.send_offset = f1.send_offset;
       f2.recv_offset = f1.recv_offset;
+      f1.path = f2.path = 1;
       plan.kernels.push_back(f1);
       plan.collectives.push_back((int)plan.kernels.size() - 1);
       plan.kernels.push_back(f2);
+      // the same two stages in one kernel, the records exchanged through the
+      // ranks' peer mailboxes (launched instead when the communicator has them)
+      if (rec <= kXSlot && opt.world <= kXMaxWorld) {
+        KernelDef f3 = f;
+        f3.fin_stage = 3;
+        f3.record_bytes = rec;
+        f3.path = 2;
+        plan.kernels.push_back(f3);
+      }
     } else {
       plan.kernels.push_back(f);
     }

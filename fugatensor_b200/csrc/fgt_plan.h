@@ -68,6 +68,23 @@ struct Domain {
 };
 
 enum class KKind { ELEM, ROW, COLFIN, FULLFIN };
+
+// Peer mailbox of one communicator rank: device memory the other ranks'
+// processes map through CUDA IPC, zeroed when the communicator is created.
+//   epoch[c]        (this rank's own) launches completed by CTA index c of
+//                   the exchanging FIN kernels
+//   flag[src][c]    the last epoch whose record rank src delivered here for
+//                   CTA index c
+//   data[par][src]  records rank src delivered here; par = epoch % 2, so a
+//                   rank one launch ahead never overwrites records still read
+// A record of one rank for one launch holds at most kXSlot bytes.
+constexpr int kXMaxWorld = 8;
+constexpr int kXMaxCtas = 256;
+constexpr int64_t kXSlot = 1 << 20;
+constexpr int64_t kXEpochOff = 0;
+constexpr int64_t kXFlagOff = 4096;
+constexpr int64_t kXDataOff = 65536;
+constexpr int64_t kXBytes = kXDataOff + 2 * kXMaxWorld * kXSlot;
 enum RedRole { ROLE_ROW = 0, ROLE_COL = 1, ROLE_FULL = 2 };
 
 struct RedDef {
@@ -103,7 +120,10 @@ struct KernelDef {
   std::vector<RedDef> reds;       // reductions computed (ROW/ELEM) or finalised (FIN)
   std::vector<OutStore> stores;
   int producer = -1;              // FIN kernels: index of the kernel whose partials they read
-  int fin_stage = 0;              // FIN: 0 = unsharded, 1 = CTA partials -> rank record, 2 = ranks -> outputs
+  int fin_stage = 0;              // FIN: 0 = unsharded, 1 = CTA partials -> rank record, 2 = ranks -> outputs,
+                                  // 3 = both with the records exchanged through the peer mailboxes
+  int path = 0;                   // sharded specs: 0 always launched, 1 only with NCCL (stages 1, 2),
+                                  // 2 only with peer mailboxes (stage 3)
   // geometry (chosen by the planner)
   int nt = 256, tpr = 256, vec = 1, nch = 1, unroll = 1;
   int cluster = 1;                // ROW: CTAs of a thread-block cluster sharing one row (tpr = nt * cluster)

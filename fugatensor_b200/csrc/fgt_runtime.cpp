@@ -19,6 +19,7 @@
 #include <fstream>
 #include <memory>
 #include <mutex>
+#include <algorithm>
 #include <climits>
 #include <thread>
 #include <chrono>
@@ -285,6 +286,16 @@ struct fgt_spec {
 struct fgt_comm {
   fgt::nccl_comm comm = nullptr;
   int world = 1, rank = 0;
+  // Peer mailboxes (reductions over the sharded dimension exchange their
+  // records with NVLink stores instead of an NCCL all-gather): this rank's
+  // mailbox, every rank's mailbox mapped here (own included), and a status
+  // word in host-mapped memory that a timed-out exchange sets.
+  bool p2p = false;
+  CUdeviceptr mailbox = 0;
+  CUdeviceptr peers[fgt::kXMaxWorld] = {};
+  unsigned* status_host = nullptr;
+  CUdeviceptr status_dev = 0;
+  unsigned long long wait_limit_ns = 10000000000ull;
 };
 
 // A prepared program: per CUDA context, the spec's kernels as one
@@ -380,16 +391,27 @@ struct ArgBlock {
   std::vector<unsigned char> bytes;
 };
 
-ArgBlock make_args(const Plan& p, const void* const* inputs, void* const* outputs, void* ws, long long nparts) {
+ArgBlock make_args(const Plan& p, const void* const* inputs, void* const* outputs, void* ws, long long nparts,
+                   const fgt_comm* xcomm = nullptr) {
   const int nin = std::max<int>(1, (int)p.g.input_nodes.size());
   const int nout = std::max<int>(1, (int)p.g.outputs.size());
   ArgBlock a;
-  a.bytes.assign((size_t)(nin + nout + 3) * 8, 0);
+  const size_t base = (size_t)(nin + nout + 3) * 8;
+  a.bytes.assign(base + (xcomm ? (size_t)(kXMaxWorld + 3) * 8 : 0), 0);
   unsigned char* b = a.bytes.data();
   for (size_t i = 0; i < p.g.input_nodes.size(); ++i) std::memcpy(b + 8 * i, &inputs[i], 8);
   for (size_t i = 0; i < p.g.outputs.size(); ++i) std::memcpy(b + 8 * (nin + i), &outputs[i], 8);
   std::memcpy(b + 8 * (nin + nout), &ws, 8);
   std::memcpy(b + 8 * (nin + nout + 1), &nparts, 8);
+  if (xcomm) {
+    // peer-exchange FIN kernels: xmb[kXMaxWorld], xstat, xrank, xlimit
+    unsigned char* x = b + base;
+    for (int k = 0; k < kXMaxWorld; ++k) std::memcpy(x + 8 * k, &xcomm->peers[k], 8);
+    std::memcpy(x + 8 * kXMaxWorld, &xcomm->status_dev, 8);
+    const long long rank = xcomm->rank;
+    std::memcpy(x + 8 * (kXMaxWorld + 1), &rank, 8);
+    std::memcpy(x + 8 * (kXMaxWorld + 2), &xcomm->wait_limit_ns, 8);
+  }
   return a;
 }
 
@@ -413,6 +435,9 @@ int64_t grid_for(const KernelDef& k, const LoadedModule& lm, size_t idx) {
       return g;
     }
     case KKind::COLFIN:
+      // the peer-exchange form pairs CTA c with CTA c of every rank: the same
+      // grid on every rank, all CTAs resident, at most kXMaxCtas flags
+      if (k.fin_stage == 3) return std::max<int64_t>(1, std::min<int64_t>({(k.dom.NI + k.nt - 1) / k.nt, (int64_t)lm.sms, (int64_t)kXMaxCtas}));
       return std::max<int64_t>(1, std::min<int64_t>((k.dom.NI + k.nt - 1) / k.nt, (int64_t)lm.sms * 4));
     case KKind::FULLFIN:
       return 1;
@@ -441,7 +466,9 @@ struct Step {
   long long nparts;
 };
 
-std::vector<Step> plan_steps(const Plan& p, const LoadedModule& lm) {
+// path: 1 = NCCL (FIN stages 1 and 2 around the all-gather), 2 = peer
+// mailboxes (FIN stage 3); kernels of the other path are not launched.
+std::vector<Step> plan_steps(const Plan& p, const LoadedModule& lm, int path = 1) {
   std::vector<Step> steps;
   std::vector<int64_t> parts(p.kernels.size(), 0);
   for (size_t i = 0; i < p.kernels.size(); ++i) {
@@ -449,6 +476,7 @@ std::vector<Step> plan_steps(const Plan& p, const LoadedModule& lm) {
     long long nparts = 0;
     if (k.producer >= 0) nparts = parts[k.producer];
     if (empty_kernel(k)) continue;
+    if (k.path != 0 && k.path != path) continue;
     int64_t grid = grid_for(k, lm, i);
     parts[i] = k.kind == KKind::ROW ? grid / k.cluster * k.rows_per_cta : grid;
     const unsigned gy = k.kind == KKind::ROW ? (unsigned)std::max<int64_t>(1, k.col_tiles) : 1u;
@@ -476,6 +504,7 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
                 void* stream) {
   const Plan& p = s->plan;
   validate_buffers(p, inputs, outputs, ws, ws_bytes);
+  bool xpath = false;
   if (!p.collectives.empty()) {
     require(comm != nullptr, "this spec reduces over the sharded dimension: launch it with fgt_spec_launch_sharded");
     require(comm->world == p.opt.world && comm->rank == p.opt.rank, "communicator rank/world differ from the spec's shard options");
@@ -484,19 +513,24 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
     nccl_result state = 0;
     nccl_check(nccl().CommGetAsyncError(comm->comm, &state), "ncclCommGetAsyncError");
     require(state == 0, std::string("communicator error before launch: ") + nccl().GetErrorString(state), FGT_ERR_NCCL);
+    require(!comm->status_host || *(volatile unsigned*)comm->status_host == 0,
+            "an earlier peer exchange on this communicator timed out (a rank did not arrive within "
+            "FGT_EXCHANGE_WAIT_MS); its results are invalid",
+            FGT_ERR_NCCL);
+    for (const KernelDef& k : p.kernels) xpath = xpath || (k.path == 2 && comm->p2p);
   }
   LoadedModule& lm = module_for(s);
   CUstream st = (CUstream)stream;
-  for (const Step& sp : plan_steps(p, lm)) {
+  for (const Step& sp : plan_steps(p, lm, xpath ? 2 : 1)) {
     const size_t i = sp.idx;
     const KernelDef& k = p.kernels[i];
-    ArgBlock a = make_args(p, inputs, outputs, ws, sp.nparts);
+    ArgBlock a = make_args(p, inputs, outputs, ws, sp.nparts, k.fin_stage == 3 ? comm : nullptr);
     void* params[] = {a.bytes.data()};
     cu_check(drv().LaunchKernel(lm.fn[i], sp.grid, sp.gy, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
                                 nullptr),
              "cuLaunchKernel");
     for (int c : p.collectives) {
-      if (c != (int)i) continue;
+      if (c != (int)i || xpath) continue;
       unsigned char* base = (unsigned char*)ws;
       nccl_check(nccl().AllGather(base + k.send_offset, base + k.recv_offset, (size_t)k.record_bytes, /*ncclChar*/ 0,
                                   comm->comm, stream),
@@ -750,7 +784,14 @@ fgt_status fgt_program_run(fgt_program* program, const void* const* inputs, void
   return guarded([&] {
     fgt_spec* s = program->spec;
     const Plan& p = s->plan;
-    if (!program->use_graph || !drv().graphs) {
+    // Inside a stream capture a graph launch is not allowed: the kernels are
+    // launched one by one and become nodes of the caller's captured graph.
+    CUstreamCaptureStatus cap = CU_STREAM_CAPTURE_STATUS_NONE;
+    if (program->use_graph && drv().graphs) {
+      ensure_context();
+      cu_check(drv().StreamIsCapturing((CUstream)stream, &cap), "cuStreamIsCapturing");
+    }
+    if (!program->use_graph || !drv().graphs || cap != CU_STREAM_CAPTURE_STATUS_NONE) {
       launch_all(s, nullptr, inputs, outputs, workspace, workspace_bytes, stream);
       return;
     }
@@ -822,6 +863,95 @@ fgt_status fgt_comm_unique_id(uint8_t id[128]) {
   });
 }
 
+namespace fgt {
+namespace {
+
+// All-gather `n` bytes per rank over the communicator (host buffers; for
+// set-up and teardown only: it synchronises the context).
+void allgather_host(fgt_comm* c, const void* mine, size_t n, void* all) {
+  CUdeviceptr buf = 0;
+  cu_check(drv().MemAlloc(&buf, n * (size_t)c->world), "cuMemAlloc");
+  struct Free {
+    CUdeviceptr b;
+    ~Free() { drv().MemFree(b); }
+  } guard{buf};
+  cu_check(drv().MemcpyHtoD(buf + n * (size_t)c->rank, mine, n), "cuMemcpyHtoD");
+  nccl_check(nccl().AllGather((const void*)(buf + n * (size_t)c->rank), (void*)buf, n, /*ncclChar*/ 0, c->comm, nullptr),
+             "ncclAllGather");
+  nccl_wait(c->comm, "ncclAllGather");
+  cu_check(drv().CtxSynchronize(), "cuCtxSynchronize");
+  cu_check(drv().MemcpyDtoH(all, buf, n * (size_t)c->world), "cuMemcpyDtoH");
+}
+
+void release_mailboxes(fgt_comm* c) {
+  for (int k = 0; k < kXMaxWorld; ++k)
+    if (c->peers[k] && k != c->rank) drv().IpcCloseMemHandle(c->peers[k]);
+  for (int k = 0; k < kXMaxWorld; ++k) c->peers[k] = 0;
+  if (c->mailbox) drv().MemFree(c->mailbox);
+  if (c->status_host) drv().MemFreeHost(c->status_host);
+  c->mailbox = 0;
+  c->status_host = nullptr;
+  c->status_dev = 0;
+  c->p2p = false;
+}
+
+// Peer mailboxes: every rank allocates one (zeroed) and a host-mapped status
+// word, exports the mailbox through CUDA IPC, the handles are all-gathered
+// over the communicator, and every rank maps the others'. Used only when
+// every rank succeeded at every step (decided together, so all ranks launch
+// the same path). FGT_PEER_EXCHANGE=0 keeps the NCCL all-gather path.
+void setup_mailboxes(fgt_comm* c) {
+  if (const char* e = std::getenv("FGT_PEER_EXCHANGE"))
+    if (std::atoi(e) == 0) return;
+  if (c->world > kXMaxWorld || !drv().ipc) return;  // the same on every rank of one machine
+  if (const char* w = std::getenv("FGT_EXCHANGE_WAIT_MS")) {
+    const long long v = std::atoll(w);
+    if (v > 0) c->wait_limit_ns = (unsigned long long)v * 1000000ull;
+  }
+  struct Rec {
+    CUipcMemHandle handle;
+    int32_t ok;
+    char pad[60];
+  };
+  static_assert(sizeof(Rec) == 128, "mailbox record");
+  Rec mine;
+  std::memset(&mine, 0, sizeof mine);
+  bool ok = drv().MemAlloc(&c->mailbox, (size_t)kXBytes) == CUDA_SUCCESS;
+  ok = ok && drv().MemsetD8(c->mailbox, 0, (size_t)kXBytes) == CUDA_SUCCESS;
+  ok = ok && drv().IpcGetMemHandle(&mine.handle, c->mailbox) == CUDA_SUCCESS;
+  ok = ok && drv().MemHostAlloc((void**)&c->status_host, 64, CU_MEMHOSTALLOC_DEVICEMAP | CU_MEMHOSTALLOC_PORTABLE) ==
+                 CUDA_SUCCESS;
+  ok = ok && drv().MemHostGetDevicePointer(&c->status_dev, c->status_host, 0) == CUDA_SUCCESS;
+  if (ok) *(volatile unsigned*)c->status_host = 0;
+  mine.ok = ok ? 1 : 0;
+  std::vector<Rec> all((size_t)c->world);
+  allgather_host(c, &mine, sizeof(Rec), all.data());
+  bool every = true;
+  for (const Rec& r : all) every = every && r.ok;
+  int32_t opened = every ? 1 : 0;
+  for (int k = 0; k < c->world && opened; ++k) {
+    if (k == c->rank) continue;
+    if (drv().IpcOpenMemHandle(&c->peers[k], all[(size_t)k].handle, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS) != CUDA_SUCCESS) {
+      c->peers[k] = 0;
+      opened = 0;
+    }
+  }
+  std::vector<int32_t> agreed((size_t)c->world);
+  allgather_host(c, &opened, sizeof(int32_t), agreed.data());
+  for (int32_t a : agreed) every = every && a;
+  if (!every) {
+    release_mailboxes(c);
+    return;
+  }
+  c->peers[c->rank] = c->mailbox;
+  c->p2p = true;
+}
+
+}  // namespace
+}  // namespace fgt
+
+int32_t fgt_comm_peer_exchange(const fgt_comm* comm) { return comm && comm->p2p ? 1 : 0; }
+
 fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, fgt_comm** out) {
   if (!out) return set_error(FGT_ERR_INVALID, "out is NULL");
   *out = nullptr;
@@ -846,13 +976,39 @@ fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, f
       fail(FGT_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + nccl().GetErrorString(r));
     }
     nccl_wait(c->comm, "ncclCommInitRankConfig");
+    if (world > 1) {
+      try {
+        setup_mailboxes(c.get());
+      } catch (...) {
+        release_mailboxes(c.get());
+        if (c->comm) nccl().CommAbort(c->comm);
+        c->comm = nullptr;
+        throw;
+      }
+    }
     *out = c.release();
   });
 }
 
 void fgt_comm_destroy(fgt_comm* comm) {
   if (!comm) return;
-  if (comm->comm && nccl().ok) nccl().CommDestroy(comm->comm);
+  if (comm->p2p) {
+    // No rank unmaps or frees its mailbox while a peer may still write to it:
+    // each rank finishes its own work, then all ranks meet. If they cannot
+    // meet (a rank is gone or the deadline passed), the mailbox is left
+    // mapped rather than freed under a possible writer.
+    bool met = false;
+    try {
+      fgt::cu_check(fgt::drv().CtxSynchronize(), "cuCtxSynchronize");
+      int32_t one = 1;
+      std::vector<int32_t> all((size_t)comm->world);
+      fgt::allgather_host(comm, &one, sizeof one, all.data());
+      met = true;
+    } catch (...) {
+    }
+    if (met) fgt::release_mailboxes(comm);
+  }
+  if (comm->comm && fgt::nccl().ok) fgt::nccl().CommDestroy(comm->comm);
   delete comm;
 }
 

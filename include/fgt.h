@@ -242,7 +242,8 @@ fgt_status fgt_program_create(const fgt_spec* spec, int32_t use_graph, fgt_progr
  * fgt_spec_launch (checked before anything is enqueued). Runs of one
  * program from several threads are serialised on the program's lock. The
  * first graph run on a context instantiates the graph (host and driver
- * resources): make it outside any stream capture. */
+ * resources). On a stream that is being captured the kernels are launched
+ * one by one instead, so they become nodes of the caller's graph. */
 fgt_status fgt_program_run(fgt_program* program, const void* const* inputs, void* const* outputs, void* workspace,
                            size_t workspace_bytes, void* stream);
 
@@ -263,9 +264,25 @@ fgt_status fgt_comm_unique_id(uint8_t id[128]);
  * deadline of FGT_COMM_TIMEOUT_MS milliseconds (environment, default 300000).
  * A rank that never joins, or an NCCL error, ends in FGT_ERR_NCCL and the
  * communicator is aborted; a sharded launch on an aborted or failed
- * communicator returns FGT_ERR_NCCL before launching any kernel. */
+ * communicator returns FGT_ERR_NCCL before launching any kernel.
+ * With world > 1 (up to 8 ranks on one machine) every rank also allocates a
+ * peer mailbox (16 MiB + 64 KiB of device memory) and maps every other
+ * rank's through CUDA IPC; reductions over the sharded dimension then
+ * exchange their per-rank records inside one finalising kernel with NVLink
+ * stores and flags, instead of an NCCL all-gather between two kernels. The
+ * ranks decide together; if any rank cannot map the mailboxes, or
+ * FGT_PEER_EXCHANGE=0, all use the NCCL path. A kernel waits at most
+ * FGT_EXCHANGE_WAIT_MS (default 10000) for a peer's record; on a timeout it
+ * marks the communicator and the next sharded launch returns FGT_ERR_NCCL.
+ * Launches on one communicator must not overlap on the GPU (as for NCCL). */
 fgt_status fgt_comm_create(const uint8_t id[128], int32_t world, int32_t rank, fgt_comm** out);
 
+/* 1 when the communicator exchanges records through peer mailboxes, 0 when
+ * through NCCL. */
+int32_t fgt_comm_peer_exchange(const fgt_comm* comm);
+
+/* Collective when the communicator has peer mailboxes: every rank calls it
+ * after its last launch; no rank unmaps its mailbox before all have met. */
 void fgt_comm_destroy(fgt_comm* comm);
 
 /* Sharded launch of a spec created with options.shard_world == world of comm.

@@ -70,7 +70,7 @@ def test_graph_and_eager_programs_agree_and_match_the_oracle():
 
 
 def test_program_replay_inside_stream_capture():
-    """An instantiated program replays as a child graph of a captured graph."""
+    """On a capturing stream a program adds its kernels to the captured graph."""
     g_in = torch.randn(256, 4096, device="cuda")
     eng = ft.Engine("cuda:0", tune=False)
     X = ft.Tensor(eng, "f32", (256, 4096), data=g_in)
