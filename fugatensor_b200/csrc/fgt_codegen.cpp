@@ -1811,13 +1811,62 @@ struct Emitter {
     }
     std::string pv = "((const " + src_t + "*)(p.ws+" + std::to_string(rd.part_val) + "LL))";
     std::string pi = "((const fgt_i64*)(p.ws+" + std::to_string(rd.part_idx) + "LL))";
-    s << "for (fgt_i64 q_ = " << (K.kind == KKind::FULLFIN ? "tid" : "0") << "; q_ < " << count << "; q_ += "
-      << (K.kind == KKind::FULLFIN ? std::to_string(K.nt) : "1") << ") { ";
+    // FULLFIN: the CTA's threads stride over the partials; COLFIN: each of
+    // the kColGroups warps of a CTA sums every kColGroups-th partial of its
+    // 32 columns (pg_ is the warp's group)
+    const bool full = K.kind == KKind::FULLFIN;
+    s << "for (fgt_i64 q_ = " << (full ? "tid" : "pg_") << "; q_ < " << count << "; q_ += "
+      << (full ? std::to_string(K.nt) : std::to_string(kColGroups)) << ") { ";
     if (t.arg) s << "{ const " << src_t << " ov = " << pv << "[q_*" << M << "LL+" << e << "]; const fgt_i64 oi = " << pi << "[q_*"
                  << M << "LL+" << e << "]; " << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
     else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << pv << "[q_*" << M << "LL+" << e << "]; " << comb_stmt(t, a, "ov") << " }";
     s << " }";
     return s.str();
+  }
+
+  // COLFIN layout: a CTA handles 32 consecutive columns with kColGroups warps,
+  // warp g summing partials g, g + kColGroups, ...; the group sums are then
+  // combined in group order (a fixed order: every launch gives the same bits).
+  static constexpr int kColGroups = 8;
+
+  // Column loop of a COLFIN kernel over blocks of 32 columns: the partial
+  // sums of the CTA's warps, their combination in group order by warp 0, then
+  // `tail` (per column e, warp 0 only).
+  void col_partial_loop(std::ostringstream& o, const std::vector<std::string>& comb,
+                        const std::vector<std::pair<RedText, std::string>>& accs, const std::vector<std::string>& tail) {
+    const std::string G = std::to_string(kColGroups);
+    o << "  const fgt_i64 NI = " << d.NI << "LL;\n";
+    o << "  const int cl_ = tid & 31, pg_ = tid >> 5;\n";
+    for (auto& [t, a] : accs) {
+      o << "  __shared__ " << t.fin_t << " cg_" << a << "[" << G << "][32];\n";
+      if (t.arg) o << "  __shared__ fgt_i64 cgi_" << a << "[" << G << "][32];\n";
+    }
+    o << "  for (fgt_i64 cb_ = blockIdx.x; cb_ * 32 < NI; cb_ += gridDim.x) {\n";
+    o << "    const fgt_i64 e = cb_ * 32 + cl_;\n";
+    o << "    const bool ev_ = e < NI;\n";
+    // accumulator declarations, then the partial loops under the bound check
+    std::vector<std::string> decls, loops;
+    for (const std::string& st : comb) (st.compare(0, 4, "for ") == 0 ? loops : decls).push_back(st);
+    put(o, decls, "    ");
+    o << "    if (ev_) {\n";
+    put(o, loops, "      ");
+    o << "    }\n";
+    for (auto& [t, a] : accs) {
+      o << "    cg_" << a << "[pg_][cl_] = " << a << ";\n";
+      if (t.arg) o << "    cgi_" << a << "[pg_][cl_] = " << a << "i;\n";
+    }
+    o << "    __syncthreads();\n";
+    o << "    if (pg_ == 0 && ev_) {\n";
+    o << "      " << digits_i() << "\n";
+    for (auto& [t, a] : accs) {
+      o << "      for (int g_ = 1; g_ < " << G << "; ++g_) { ";
+      if (t.arg) o << "const " << t.fin_t << " ov = cg_" << a << "[g_][cl_]; const fgt_i64 oi = cgi_" << a << "[g_][cl_]; "
+                   << arg_stmt(t, a, a + "i", "ov", "oi");
+      else o << "const " << t.fin_t << " ov = cg_" << a << "[g_][cl_]; " << comb_stmt(t, a, "ov");
+      o << " }\n";
+    }
+    put(o, tail, "      ");
+    o << "    }\n    __syncthreads();\n  }\n";
   }
 
   std::string build_fin() {
@@ -1911,12 +1960,11 @@ struct Emitter {
       o << "  if (tid == 0) xep_ = ((const unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] + 1u;\n";
       o << "  __syncthreads();\n  const unsigned xe_ = xep_;\n";
       if (col) {
-        o << "  const fgt_i64 NI = " << d.NI << "LL;\n";
-        o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
-        o << "    " << digits_i() << "\n";
-        put(o, comb, "    ");
-        push("    ");
-        o << "  }\n  __threadfence_system();\n  __syncthreads();\n";
+        std::vector<std::string> tail{"for (int k_ = 0; k_ < " + W + "; ++k_) {", "  unsigned char* const xrec_ = " + slot + ";"};
+        for (auto& w : rec_write) tail.push_back("  " + w);
+        tail.push_back("}");
+        col_partial_loop(o, comb, accs, tail);
+        o << "  __threadfence_system();\n  __syncthreads();\n";
         flags_and_wait();
         o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
         o << "    " << digits_i() << "\n";
@@ -1940,17 +1988,24 @@ struct Emitter {
       o << "  }\n}\n";
       return o.str();
     }
+    if (col && stage != 2) {
+      std::vector<std::string> tail = rec_write;
+      if (stage != 1) {
+        tail = finals;
+        tail.insert(tail.end(), lane[0].begin(), lane[0].end());
+      }
+      col_partial_loop(o, comb, accs, tail);
+      o << "}\n";
+      return o.str();
+    }
     if (col) {
+      // stage 2: this rank's combine of the ranks' gathered records, per column
       o << "  const fgt_i64 NI = " << d.NI << "LL;\n";
       o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
       o << "    " << digits_i() << "\n";
       put(o, comb, "    ");
-      if (stage == 1) {
-        put(o, rec_write, "    ");
-      } else {
-        put(o, finals, "    ");
-        put(o, lane[0], "    ");
-      }
+      put(o, finals, "    ");
+      put(o, lane[0], "    ");
       o << "  }\n}\n";
       return o.str();
     }

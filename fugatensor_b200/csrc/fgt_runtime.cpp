@@ -437,8 +437,10 @@ int64_t grid_for(const KernelDef& k, const LoadedModule& lm, size_t idx) {
     case KKind::COLFIN:
       // the peer-exchange form pairs CTA c with CTA c of every rank: the same
       // grid on every rank, all CTAs resident, at most kXMaxCtas flags
-      if (k.fin_stage == 3) return std::max<int64_t>(1, std::min<int64_t>({(k.dom.NI + k.nt - 1) / k.nt, (int64_t)lm.sms, (int64_t)kXMaxCtas}));
-      return std::max<int64_t>(1, std::min<int64_t>((k.dom.NI + k.nt - 1) / k.nt, (int64_t)lm.sms * 4));
+      // stage 2 walks columns one per thread; the others take blocks of 32 columns
+      if (k.fin_stage == 3) return std::max<int64_t>(1, std::min<int64_t>({(k.dom.NI + 31) / 32, (int64_t)lm.sms, (int64_t)kXMaxCtas}));
+      if (k.fin_stage == 2) return std::max<int64_t>(1, std::min<int64_t>((k.dom.NI + k.nt - 1) / k.nt, (int64_t)lm.sms * 4));
+      return std::max<int64_t>(1, std::min<int64_t>((k.dom.NI + 31) / 32, (int64_t)lm.sms * 4));
     case KKind::FULLFIN:
       return 1;
   }
