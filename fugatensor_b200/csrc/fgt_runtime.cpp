@@ -98,6 +98,59 @@ void parse_ptxas_report(const std::string& log, Compiled* c) {
   }
 }
 
+// SHA-256 (FIPS 180-4) of a byte string, as 64 hex digits: the content check
+// stored beside each cached cubin (its file name carries a 64-bit FNV-1a hash).
+std::string sha256_hex(const std::string& msg) {
+  static const uint32_t K[64] = {
+      0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5, 0xd807aa98, 0x12835b01,
+      0x243185be, 0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174, 0xe49b69c1, 0xefbe4786, 0x0fc19dc6, 0x240ca1cc,
+      0x2de92c6f, 0x4a7484aa, 0x5cb0a9dc, 0x76f988da, 0x983e5152, 0xa831c66d, 0xb00327c8, 0xbf597fc7, 0xc6e00bf3, 0xd5a79147,
+      0x06ca6351, 0x14292967, 0x27b70a85, 0x2e1b2138, 0x4d2c6dfc, 0x53380d13, 0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85,
+      0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3, 0xd192e819, 0xd6990624, 0xf40e3585, 0x106aa070, 0x19a4c116, 0x1e376c08,
+      0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3, 0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208,
+      0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
+  uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+  auto rotr = [](uint32_t x, int n) { return (x >> n) | (x << (32 - n)); };
+  std::string m = msg;
+  const uint64_t bits = (uint64_t)msg.size() * 8;
+  m.push_back((char)0x80);
+  while (m.size() % 64 != 56) m.push_back(0);
+  for (int i = 7; i >= 0; --i) m.push_back((char)((bits >> (8 * i)) & 0xff));
+  for (size_t off = 0; off < m.size(); off += 64) {
+    uint32_t w[64];
+    for (int i = 0; i < 16; ++i) {
+      const unsigned char* b = (const unsigned char*)m.data() + off + 4 * i;
+      w[i] = ((uint32_t)b[0] << 24) | ((uint32_t)b[1] << 16) | ((uint32_t)b[2] << 8) | b[3];
+    }
+    for (int i = 16; i < 64; ++i) {
+      const uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
+      const uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
+      w[i] = w[i - 16] + s0 + w[i - 7] + s1;
+    }
+    uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+    for (int i = 0; i < 64; ++i) {
+      const uint32_t S1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
+      const uint32_t ch = (e & f) ^ (~e & g);
+      const uint32_t t1 = hh + S1 + ch + K[i] + w[i];
+      const uint32_t S0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
+      const uint32_t mj = (a & b) ^ (a & c) ^ (b & c);
+      const uint32_t t2 = S0 + mj;
+      hh = g;
+      g = f;
+      f = e;
+      e = d + t1;
+      d = c;
+      c = b;
+      b = a;
+      a = t1 + t2;
+    }
+    h[0] += a, h[1] += b, h[2] += c, h[3] += d, h[4] += e, h[5] += f, h[6] += g, h[7] += hh;
+  }
+  char out[65];
+  for (int i = 0; i < 8; ++i) std::snprintf(out + 8 * i, 9, "%08x", h[i]);
+  return std::string(out, 64);
+}
+
 std::string read_file(const std::string& path) {
   std::ifstream f(path, std::ios::binary);
   if (!f) return std::string();
@@ -118,19 +171,27 @@ void publish(const std::string& path, const std::string& data) {
 
 // NVRTC compile of one kernel, cached on disk by a hash of the compiler
 // version, options and source. The ptxas register report is cached beside
-// the cubin (".regs": "<registers> <spill bytes>").
+// the cubin (".regs": "<registers> <spill bytes>"), and so is the SHA-256 of
+// the full key (".key"): a cached cubin is used only when that digest
+// matches, and a 64-bit name collision moves on to the next slot (-1, -2, ...).
 Compiled compile_cubin(const std::string& name, const std::string& src, const std::string& cache_dir) {
   int maj = 0, min = 0;
   nvrtcVersion(&maj, &min);
   std::string opts;
   for (const char* o : kNvrtcOptions) opts += o, opts += ' ';
   const std::string key = std::to_string(maj) + "." + std::to_string(min) + "|" + opts + "|" + src;
+  const std::string digest = sha256_hex(key) + "\n";
   char hex[32];
   std::snprintf(hex, sizeof hex, "%016llx", (unsigned long long)fnv1a(key));
-  const std::string path = cache_dir + "/" + name + "-" + hex + ".cubin";
+  std::string path;
   Compiled c;
-  c.cubin = read_file(path);
-  if (!c.cubin.empty()) {
+  for (int slot = 0; slot < 8; ++slot) {
+    path = cache_dir + "/" + name + "-" + hex + (slot ? "-" + std::to_string(slot) : std::string()) + ".cubin";
+    const std::string stored = read_file(path + ".key");
+    if (stored.empty()) break;                  // free slot (or an entry without its digest: rebuilt)
+    if (stored != digest) continue;             // another key with the same 64-bit hash
+    c.cubin = read_file(path);
+    if (c.cubin.empty()) break;
     std::string info = read_file(path + ".regs");
     if (!info.empty()) std::sscanf(info.c_str(), "%d %d", &c.regs, &c.spill_bytes);
     return c;
@@ -156,6 +217,7 @@ Compiled compile_cubin(const std::string& name, const std::string& src, const st
   mkdirs(cache_dir);
   publish(path + ".regs", std::to_string(c.regs) + " " + std::to_string(c.spill_bytes) + "\n");
   publish(path, c.cubin);
+  publish(path + ".key", digest);  // last: the entry counts only once it is complete
   return c;
 }
 

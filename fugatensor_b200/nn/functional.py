@@ -8,8 +8,6 @@ their VJPs) into one row kernel.
 """
 from __future__ import annotations
 
-import math
-
 from .. import dtypes as _dt
 from .. import ops as _ops
 from ..autograd import stop_gradient
@@ -48,35 +46,6 @@ def _apply_affine(x, normalized_shape, weight=None, bias=None):
 
 def _work(x):
     return x.astype(_dt.fp32) if x.dtype in (_dt.fp16, _dt.bf16) else x
-
-
-def relu(x):
-    return _ops.maximum(x, 0)
-
-
-def leaky_relu(x, negative_slope=0.01):
-    return _ops.where(x > 0, x, x * negative_slope)
-
-
-def sigmoid(x):
-    pos = x >= 0
-    neg_x = _ops.where(pos, -x, x)
-    z = _ops.exp(neg_x)
-    denom = z + 1
-    return _ops.where(pos, 1 / denom, z / denom)
-
-
-def silu(x):
-    return x * sigmoid(x)
-
-
-def gelu(x, *, approximate="none"):
-    if approximate == "none":
-        return 0.5 * x * (1 + _ops.erf(x * (1.0 / math.sqrt(2.0))))
-    if approximate == "tanh":
-        inner = math.sqrt(2.0 / math.pi) * (x + 0.044715 * (x * x * x))
-        return 0.5 * x * (1 + _ops.tanh(inner))
-    raise ValueError("gelu approximate must be 'none' or 'tanh'")
 
 
 def softmax(x, axis=-1):

@@ -218,14 +218,14 @@ def test_products_and_empty_reductions(backend):
 
 
 def test_nn_functional_small(backend):
-    """tests/test_stage2_ops.py:326-360 (2x4 case) vs the reference's pure-Python refs."""
+    """tests/test_stage2_ops.py:326-360 (2x4 case) vs the reference's pure-Python refs: the
+    row graphs on this path (the case's pointwise activations are not part of it)."""
     rows = [[-2.0, -0.5, 0.0, 1.5], [1.0, -3.0, 2.0, 0.5]]
     x = T(rows)
     w = T([1.0, 2.0, 0.5, 1.5])
     b = T([0.1, -0.2, 0.3, 0.0])
-    outs = run(backend, F.relu(x), F.leaky_relu(x, 0.1), F.sigmoid(x), F.silu(x), F.gelu(x),
-               F.gelu(x, approximate="tanh"), F.softmax(x, axis=1), F.log_softmax(x, axis=1),
-               F.layer_norm(x, weight=w, bias=b), F.rms_norm(x, weight=w))
+    outs = run(backend, F.softmax(x, axis=1), F.log_softmax(x, axis=1), F.layer_norm(x, weight=w, bias=b),
+               F.rms_norm(x, weight=w))
 
     def sm(r):
         m = max(r)
@@ -247,13 +247,8 @@ def test_nn_functional_small(backend):
         inv = 1 / math.sqrt(sum(v * v for v in r) / len(r) + 1e-6)
         return [v * inv * wi for v, wi in zip(r, [1, 2, 0.5, 1.5])]
 
-    gelu = lambda v: 0.5 * v * (1 + math.erf(v / math.sqrt(2)))
-    gelu_t = lambda v: 0.5 * v * (1 + math.tanh(math.sqrt(2 / math.pi) * (v + 0.044715 * v ** 3)))
-    refs = ([[max(v, 0) for v in r] for r in rows], [[v if v > 0 else 0.1 * v for v in r] for r in rows],
-            [[1 / (1 + math.exp(-v)) for v in r] for r in rows], [[v / (1 + math.exp(-v)) for v in r] for r in rows],
-            [[gelu(v) for v in r] for r in rows], [[gelu_t(v) for v in r] for r in rows],
-            [sm(r) for r in rows], [lsm(r) for r in rows], [ln(r) for r in rows], [rn(r) for r in rows])
-    tols = (1e-5,) * 8 + (1e-4, 1e-4)
+    refs = ([sm(r) for r in rows], [lsm(r) for r in rows], [ln(r) for r in rows], [rn(r) for r in rows])
+    tols = (1e-5, 1e-5, 1e-4, 1e-4)
     for got, want, tol in zip(outs, refs, tols):
         close(got, [v for r in want for v in r], tol)
 
