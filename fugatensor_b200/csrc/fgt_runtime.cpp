@@ -487,6 +487,14 @@ int64_t grid_for(const KernelDef& k, const LoadedModule& lm, size_t idx) {
       int64_t g = std::min(groups * k.cluster, std::max<int64_t>(1, resident / std::max<int64_t>(1, k.col_tiles)));
       if (k.max_ctas > 0) g = std::min(g, k.max_ctas * k.cluster);
       g = std::max<int64_t>(k.cluster, g / k.cluster * k.cluster);
+      // Balanced waves: CTA i takes row groups i, i + G, ...; when the groups are
+      // not a whole number of rounds, the last round runs with only part of the
+      // CTAs. Keep the number of rounds and shrink G so that every CTA gets the
+      // same number of groups, or one fewer (e.g. 2048 groups on 592 resident
+      // CTAs: 512 CTAs x 4 instead of 272 x 4 + 320 x 3).
+      const int64_t ctas = g / k.cluster;
+      const int64_t rounds = (groups + ctas - 1) / ctas;
+      g = std::max<int64_t>(1, (groups + rounds - 1) / rounds) * k.cluster;
       return g;
     }
     case KKind::ELEM: {

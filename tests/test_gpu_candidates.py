@@ -6,7 +6,8 @@ flags 1 = occupancy step, 2 = CUDA expf, 8 = shuffle butterfly) and keeps the
 fastest, so any candidate can end up being the benchmarked kernel. Each
 benchmark row partition runs here in every candidate geometry at a medium
 size (several rows per CTA, so the prefetch ring wraps and column partials
-span many rows), against one oracle evaluation per partition.
+span many rows), against one oracle evaluation per partition. The geometries
+kept out of the candidate list (tuning.PARITY_EXTRA) run here too.
 """
 import os
 
@@ -51,7 +52,7 @@ def test_every_candidate_geometry_matches_oracle(cfg, variant, dtype):
     ref = O.evaluate(desc, [to_host(dev_in[k], dts[k]) for k in order], O.ACCURATE, threads=THREADS)
     inputs = [dev_in[k] for k in order]
     seen, checked, failures = set(), [], []
-    for e, r, c, f in tuning.CANDIDATES:
+    for e, r, c, f in tuning.CANDIDATES + tuning.PARITY_EXTRA:
         spec = _fgt.Spec(desc, row_elems=e, ring_kb=r, row_cluster=c, row_flags=f)
         src = tuple(spec.kernel_source(i).replace(k["name"], "K")
                     for i, k in enumerate(spec.execution_plan["cuda_lowering"]["kernels"]))
