@@ -90,7 +90,8 @@ def build(verbose: bool = False) -> Path:
         obj = BUILD / (src.stem + ".o")
         if _stale(obj, [src] + [CSRC / h for h in HEADERS] + [ROOT / "include" / "fgt.h"]):
             _run(["g++", "-std=c++17", "-O2", "-fPIC", "-Wall", "-Wno-unused-function", f"-I{ROOT / 'include'}",
-                  f"-I{CSRC}", f"-I{CUDA / 'include'}", "-c", str(src), "-o", str(obj)])
+                  f"-I{CSRC}", f"-I{CUDA / 'include'}", f'-DFGT_CUDA_LIB_DIR="{CUDA / "lib64"}"', "-c", str(src),
+                  "-o", str(obj)])
         objs.append(obj)
     # statically compiled kernels (nvcc, sm_100a)
     for src in CU_SOURCES:
@@ -101,7 +102,7 @@ def build(verbose: bool = False) -> Path:
                   "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)])
         objs.append(obj)
     if _stale(LIB, objs + deps):
-        _run(["g++", "-shared", "-o", str(LIB), *map(str, objs), f"-L{CUDA / 'lib64'}", "-lnvrtc", "-lcudart_static",
+        _run(["g++", "-shared", "-o", str(LIB), *map(str, objs), f"-L{CUDA / 'lib64'}", "-lcudart_static",
               "-lrt", "-ldl", "-lpthread", f"-Wl,-rpath,{CUDA / 'lib64'}", "-Wl,--no-undefined"])
     native = _build_native()
     if verbose:

@@ -374,6 +374,8 @@ struct Emitter {
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
   std::set<int> exp_phases;                 // phases with element exps by fgt_exp_q (range noted)
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
+  std::set<int> tm_phases;                  // phases updating column accumulators held in TMEM
+  int64_t tm_alloc = 0;                     // TMEM columns allocated per CTA (0: none)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
   std::set<std::string> f32_sum_accs;       // f32 sum accumulators (arrays) whose two lanes may add as a pair
   int64_t col_smem = 0;                     // bytes of column accumulators in shared memory (before the ring)
@@ -398,6 +400,8 @@ struct Emitter {
     int64_t smem_off = 0;  // region of this operand in the ring
   };
   std::vector<RowSite> row_sites;
+  // per-thread column operands persisted in registers (name, words per chunk)
+  std::vector<std::pair<std::string, int>> persisted_arrays;
   // Ring-resident rows (FGT_ROW_RING_RESIDENT): a staged operand's current row
   // stays in its ring stage, and each phase that reads it copies the thread's
   // own pieces of the chunk into a phase-local array (the name maps to the
@@ -685,15 +689,17 @@ struct Emitter {
     } else if (persisted) {
       std::string v = val(id, m, Sc{SC_PROLANE, 0});
       std::string cname = fresh("cv");
-      if (resident() && pack16(n.dt)) {
+      if ((resident() || P.opt.pack_cols) && pack16(n.dt)) {
         // a 16-bit value is exact in its storage bits: two per register
         kdecl.push_back("fgt_u32 " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec / 2) + "];");
         prolane.push_back("fgt_set_h16(" + cname + "[c], v, " + st_conv(n.dt, v) + ");");
         r = ld_conv(n.dt, "fgt_h16(" + cname + "[c], v)");
+        persisted_arrays.push_back({cname, K.vec / 2});
       } else {
         kdecl.push_back(vt_t(n.dt) + " " + cname + "[" + std::to_string(K.nch) + "][" + std::to_string(K.vec) + "];");
         prolane.push_back(cname + "[c][v] = " + v + ";");
         r = cname + "[c][v]";
+        persisted_arrays.push_back({cname, K.vec});
       }
       memo[key] = r;
       return r;
@@ -1006,9 +1012,22 @@ struct Emitter {
           const std::string sm = "sm_" + a + tag + PB;
           std::vector<std::string> lv;
           for (int w = 0; w < NW; ++w) lv.push_back(sm + "[" + std::to_string(w) + "]");
+          // f32 sums take two nodes of a level per FADD2 (the same two
+          // operands per node, each rounded once)
+          const bool pair2 = P.opt.lane_pairs && t.acc_t == "float" && t.op == FGT_OP_REDUCE_SUM && !t.storage;
           for (int lvl = 0; lv.size() > 1; ++lvl) {
             std::vector<std::string> nx;
-            for (size_t i = 0; i + 1 < lv.size(); i += 2) {
+            size_t i = 0;
+            for (; pair2 && i + 3 < lv.size(); i += 4) {
+              const std::string ta = a + tag + "_t" + std::to_string(lvl) + "_" + std::to_string(i / 2),
+                                tb = a + tag + "_t" + std::to_string(lvl) + "_" + std::to_string(i / 2 + 1);
+              out.push_back("const float2 " + ta + "_p2 = __fadd2_rn(make_float2(" + lv[i] + ", " + lv[i + 2] + "), make_float2(" +
+                            lv[i + 1] + ", " + lv[i + 3] + ")); const float " + ta + " = " + ta + "_p2.x; const float " + tb +
+                            " = " + ta + "_p2.y;");
+              nx.push_back(ta);
+              nx.push_back(tb);
+            }
+            for (; i + 1 < lv.size(); i += 2) {
               const std::string tv = a + tag + "_t" + std::to_string(lvl) + "_" + std::to_string(i / 2);
               out.push_back(t.acc_t + " " + tv + " = " + lv[i] + "; " + comb_stmt(t, tv, lv[i + 1]));
               nx.push_back(tv);
@@ -1296,15 +1315,55 @@ struct Emitter {
     // ((c * VEC/4 + v/4) * NT + tid) * 4 + v%4 keeps a thread's four
     // consecutive elements in one 16-byte word and neighbouring threads'
     // words adjacent (no bank conflicts for 16-byte accesses)
-    std::vector<std::string> colfin;
+    std::vector<std::string> colfin, colfin_pre;
+    // or (FGT_ROW_TMEM_COLS) in tensor memory: f32 sums of a one-row-per-CTA
+    // kernel of a multiple of 128 threads whose rows are whole numbers of
+    // thread chunks (every tcgen05 access is warp-wide). Thread t of warp w
+    // owns TMEM lane 32 * (w % 4) + t and the columns
+    // (w / 4) * n * NCH * VEC + k * NCH * VEC + c * VEC + v (accumulator k of n,
+    // chunk c, element v); a phase loads chunk c's accumulators, updates
+    // them and stores them back.
+    auto tmem_ok = [&](const RedText& t) {
+      return P.opt.tmem_cols && cached && K.cluster == 1 && K.col_tiles <= 1 && K.tpr == K.nt && K.nt % 128 == 0 &&
+             (K.vec == 4 || K.vec == 8 || K.vec == 16) && d.NI > 0 && d.NI % ((int64_t)K.tpr * K.vec) == 0 && !t.arg &&
+             t.acc_t == "float";
+    };
+    int n_tm = 0;
+    for (auto* rd : cols)
+      if (tmem_ok(red_text(g, rd->node, P.opt.accumulation, CTX_COL))) ++n_tm;
+    const int64_t tm_pt = (int64_t)K.nch * K.vec;
+    const bool use_tm = n_tm > 0 && (int64_t)(K.nt / 128) * n_tm * tm_pt <= 512;
+    if (use_tm) {
+      tm_alloc = 32;
+      while (tm_alloc < (int64_t)(K.nt / 128) * n_tm * tm_pt) tm_alloc *= 2;
+      kdecl.push_back("__shared__ unsigned tm_slot_;");
+      kdecl.push_back("if ((tid >> 5) == 0) fgt_tm_alloc(&tm_slot_, " + std::to_string(tm_alloc) + "u);");
+      kdecl.push_back("fgt_tm_fence_before(); __syncthreads(); fgt_tm_fence_after();");
+      kdecl.push_back("const unsigned tm_thr_ = tm_slot_ + ((unsigned)(((tid >> 5) & 3) * 32) << 16) + (unsigned)((tid >> 7) * " +
+                      std::to_string(n_tm * tm_pt) + ");");
+    }
+    int k_tm = 0;
     for (auto* rd : cols) {
       RedText t = red_text(g, rd->node, P.opt.accumulation, CTX_COL);
       int p = cphase[rd];
       col_phases.insert(p);
       std::string a = fresh("cacc");
-      const bool in_smem = P.opt.smem_cols && K.cluster == 1 && !t.arg;
+      const bool in_tmem = use_tm && tmem_ok(t);
+      const bool in_smem = !in_tmem && P.opt.smem_cols && K.cluster == 1 && !t.arg;
       std::string el = a + "[c][v]";
-      if (in_smem) {
+      if (in_tmem) {
+        const std::string tma = "tm_" + a, ta = "ta_" + a, VS = std::to_string(K.vec), NS = std::to_string(K.nch);
+        el = ta + "[v]";
+        kdecl.push_back("const unsigned " + tma + " = tm_thr_ + " + std::to_string(k_tm * tm_pt) + "u;");
+        kdecl.push_back("{ float z_[" + VS + "]; for (int v = 0; v < " + VS + "; ++v) z_[v] = " + t.ident + "; for (int c = 0; c < " +
+                        NS + "; ++c) fgt_tm_st(" + tma + " + c * " + VS + ", z_); }");
+        const std::string ld = "float " + ta + "[" + VS + "]; fgt_tm_ld(" + ta + ", " + tma + " + c * " + VS + ");";
+        chunkpre[p].push_back(ld);
+        chunkpost[p].push_back("fgt_tm_st(" + tma + " + c * " + VS + ", " + ta + ");");
+        colfin_pre.push_back(ld);
+        tm_phases.insert(p);
+        ++k_tm;
+      } else if (in_smem) {
         const int64_t esz = t.acc_t == "double" ? 8 : 4;
         const std::string NTC = std::to_string(K.nt);
         if (K.vec % 4 == 0)
@@ -1318,9 +1377,12 @@ struct Emitter {
         kdecl.push_back(t.acc_t + " " + a + dims + ";");
         if (t.arg) kdecl.push_back("fgt_i64 " + a + "i" + dims + ";");
       }
-      std::string init = "for (int c = 0; c < " + std::to_string(K.nch) + "; ++c) for (int v = 0; v < " + std::to_string(K.vec) +
-                         "; ++v) { " + el + " = " + t.ident + ";" + (t.arg ? " " + a + "i[c][v] = " + t.identi + ";" : std::string()) + " }";
-      kdecl.push_back(init);
+      if (!in_tmem) {
+        std::string init = "for (int c = 0; c < " + std::to_string(K.nch) + "; ++c) for (int v = 0; v < " + std::to_string(K.vec) +
+                           "; ++v) { " + el + " = " + t.ident + ";" + (t.arg ? " " + a + "i[c][v] = " + t.identi + ";" : std::string()) +
+                           " }";
+        kdecl.push_back(init);
+      }
       std::string v = val(g.nodes[rd->node].args[0], rd->opmap, Sc{SC_LANE, p});
       if (t.arg) {
         std::string ix = arg_index(*rd);
@@ -1328,7 +1390,7 @@ struct Emitter {
         lane[p].push_back("{ const fgt_i64 ix = " + ix + "; " + scan_stmt(t, a + "[c][v]", a + "i[c][v]", v, "ix") + " }");
       } else {
         lane[p].push_back(comb_stmt(t, el, v));
-        if (t.acc_t == "float" && t.op == FGT_OP_REDUCE_SUM && !t.storage) f32_sum_accs.insert(a);
+        if (t.acc_t == "float" && t.op == FGT_OP_REDUCE_SUM && !t.storage) f32_sum_accs.insert(in_tmem ? "ta_" + a : a);
       }
       std::string slot = "(" + std::string(K.cluster > 1 ? "(fgt_i64)(blockIdx.x / " + std::to_string(K.cluster) + ")"
                                                           : "(fgt_i64)blockIdx.x") +
@@ -1339,6 +1401,7 @@ struct Emitter {
                          "LL + e] = " + a + "i[c][v];";
       colfin.push_back(body);
     }
+    if (use_tm) kdecl.push_back("fgt_tm_wait_st();");
     // element stores
     for (auto& [st, p] : estores) {
       std::string v = val(st->node, store_map(*st), Sc{SC_LANE, p});
@@ -1539,6 +1602,22 @@ struct Emitter {
       const std::string dx = "dgx" + std::to_string(p), dn = "dgn" + std::to_string(p), de = "dge" + std::to_string(p);
       if (track)
         o << "    float " << dx << " = 0.0f, " << dn << " = __int_as_float(0x7f800000), " << de << " = 0.0f;\n";
+      if (p > 0 && P.opt.phase_copies && cached) {
+        // the phase reads its operands through opaque copies (fgt_opaque): the
+        // compiler then cannot merge its element values with the earlier
+        // phases' and keep them live across the barriers in between
+        for (auto& rs : row_sites) {
+          if (res && rs.staged) continue;
+          if (rs.uniform) o << "    for (int c = 0; c < " << NCH << "; ++c) fgt_opaque(" << rs.name << "[c]);\n";
+          else
+            o << "    for (int c = 0; c < " << NCH << "; ++c) for (int k = 0; k < " << (rs.packed ? K.vec / 2 : K.vec)
+              << "; ++k) fgt_opaque(" << rs.name << "[c][k]);\n";
+        }
+        for (auto& [nm, w] : persisted_arrays)
+          o << "    for (int c = 0; c < " << NCH << "; ++c) for (int k = 0; k < " << w << "; ++k) fgt_opaque(" << nm << "[c][k]);\n";
+      }
+      // this phase's TMEM loads follow the earlier rows' stores of the same columns
+      if (tm_phases.count(p)) o << "    fgt_tm_wait_st();\n";
       o << "    if (rv) {\n";
       phase_loop(p,
                  track ? div_form(lane[p], "fgt_div_q", "fgt_div_note(" + dx + ", " + dn + ", ", "fgt_exp_q",
@@ -1582,12 +1661,20 @@ struct Emitter {
     // memory (the last exchange has no later barrier of its own)
     if (K.cluster > 1) o << "  fgt_cluster_sync();\n";
     if (!colfin.empty()) {
+      if (use_tm) o << "  fgt_tm_wait_st();\n";
       o << "  #pragma unroll\n  for (int c = 0; c < " << NCH << "; ++c) {\n";
       o << "    const fgt_i64 e0 = " << E0 << ";\n";
-      o << "    " << CHK << " {\n      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
+      o << "    " << CHK << " {\n";
+      put(o, colfin_pre, "      ");
+      o << "      #pragma unroll\n      for (int v = 0; v < " << VEC << "; ++v) {\n";
       o << "        const fgt_i64 e = e0 + v;\n";
       put(o, colfin, "        ");
       o << "      }\n    }\n  }\n";
+    }
+    if (use_tm) {
+      // every warp is done with tensor memory before warp 0 frees it
+      o << "  fgt_tm_fence_before();\n  __syncthreads();\n  fgt_tm_fence_after();\n";
+      o << "  if ((tid >> 5) == 0) fgt_tm_dealloc(tm_slot_, " << tm_alloc << "u);\n";
     }
     o << "}\n";
     return o.str();
@@ -2245,6 +2332,25 @@ struct Emitter {
           done = true;
         }
       }
+      // range notes of both slots in one three-input max / min (sm_100;
+      // PTX ISA 8.8): the same value as two two-input steps, NaN included
+      if (!done && P.opt.max3 && a.back() == ';') {
+        std::string args;
+        const std::string ca = a.substr(0, a.size() - 1);
+        if (call_of(ca, "fgt_div_note", &args)) {
+          auto x = split_args(args);
+          if (x.size() == 3) {
+            out.push_back("fgt_div_note2(" + x[0] + "," + x[1] + "," + x[2] + ", " + slot_b(trim(x[2])) + ");");
+            done = true;
+          }
+        } else if (call_of(ca, "fgt_exp_note", &args)) {
+          auto x = split_args(args);
+          if (x.size() == 2) {
+            out.push_back("fgt_exp_note2(" + x[0] + "," + x[1] + ", " + slot_b(trim(x[1])) + ");");
+            done = true;
+          }
+        }
+      }
       if (!done) {
         out.push_back(sa);
         out.push_back(sb);
@@ -2293,6 +2399,13 @@ void generate_sources(Plan& plan) {
     Emitter em(plan, k, &loaded);
     k.source = em.build();
     k.smem_bytes = em.col_smem + (int64_t)em.stages * em.stage_bytes;
+    if (em.tm_alloc > 0) {
+      // at most 512 / tm_alloc CTAs per SM may hold tensor memory at once: the
+      // dynamic shared memory is padded so that no more are resident (a CTA
+      // beyond them would wait in tcgen05.alloc for another to finish)
+      const int64_t cap = 512 / em.tm_alloc;
+      if (cap < 32) k.smem_bytes = std::max<int64_t>(k.smem_bytes, 233472 / (cap + 1));
+    }
     k.row_phases = em.row_phases;
   }
 }

@@ -205,6 +205,15 @@ FGT_DEV void fgt_div_note(float& mx, float& mn, float q) {
   mx = fgt_fmax(mx, fabsf(q));
   mn = fminf(mn, fabsf(q));
 }
+// Both lanes of a pair noted at once: sm_100's three-input max.NaN / min
+// (PTX ISA 8.8), the same values as two fgt_div_note / fgt_exp_note steps.
+FGT_DEV void fgt_div_note2(float& mx, float& mn, float a, float b) {
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(mx) : "f"(mx), "f"(fabsf(a)), "f"(fabsf(b)));
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(mn) : "f"(mn), "f"(fabsf(a)), "f"(fabsf(b)));
+}
+FGT_DEV void fgt_exp_note2(float& mx, float a, float b) {
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(mx) : "f"(mx), "f"(fabsf(a)), "f"(fabsf(b)));
+}
 FGT_DEV bool fgt_div_ok(float mx, float mn) { return mx <= 1.32922800e+36f && mn >= 7.52316385e-37f; }
 FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // Max / min of a packed accumulator with a register row piece of N bf16
@@ -243,6 +252,19 @@ FGT_DEV void fgt_xfail(unsigned* status) {
 }
 
 // Element v of a packed 16-bit array (v a compile-time constant after unrolling).
+// A copy of a register value that the compiler cannot see through (an empty
+// volatile asm that claims to modify it): values a later row phase derives
+// from it are not recognised as equal to the earlier phases', so each phase
+// recomputes them instead of the compiler keeping them live across the row's
+// barriers. No instruction is emitted.
+FGT_DEV void fgt_opaque(float& x) { asm volatile("" : "+f"(x)); }
+FGT_DEV void fgt_opaque(double& x) { asm volatile("" : "+d"(x)); }
+FGT_DEV void fgt_opaque(fgt_u32& x) { asm volatile("" : "+r"(x)); }
+FGT_DEV void fgt_opaque(int& x) { asm volatile("" : "+r"(x)); }
+FGT_DEV void fgt_opaque(fgt_i64& x) { asm volatile("" : "+l"(x)); }
+FGT_DEV void fgt_opaque(fgt_u64& x) { asm volatile("" : "+l"(x)); }
+FGT_DEV void fgt_opaque(fgt_u16& x) { asm volatile("" : "+h"(x)); }
+FGT_DEV void fgt_opaque(fgt_u8&) {}
 template <int N> FGT_DEV void fgt_set_h16(fgt_u32 (&w)[N], int v, fgt_u16 h) {
   w[v >> 1] = (v & 1) ? ((w[v >> 1] & 0xffffu) | ((fgt_u32)h << 16)) : ((w[v >> 1] & 0xffff0000u) | (fgt_u32)h);
 }
@@ -420,6 +442,63 @@ template <int N> FGT_DEV void fgt_vstore_bf16_rn(fgt_u16* __restrict__ dst, cons
 // thread (cp.async.wait_group) and no block barrier is involved; data in
 // flight occupies shared memory, not registers.
 FGT_DEV unsigned fgt_smem_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+// ---- tensor memory (TMEM) as per-thread storage --------------------------
+// A CTA allocates columns of the SM's tensor memory (128 lanes x 512 columns
+// of 32 bits) with one warp; a warp of a 32x32b access reaches only the 32
+// lanes of its quarter (warp id mod 4), and each thread its own lane. Row
+// kernels keep column-reduction accumulators there: thread t of warp w owns
+// lane 32 * (w % 4) + t and a private column range chosen by w / 4, and moves
+// one chunk of accumulators to registers and back per update. tcgen05.ld is
+// asynchronous: the load and its wait are one asm statement, so no use of
+// the registers can be scheduled before the data has arrived.
+FGT_DEV void fgt_tm_alloc(unsigned* slot, unsigned ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(fgt_smem_addr(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+FGT_DEV void fgt_tm_dealloc(unsigned base, unsigned ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(base), "r"(ncols) : "memory");
+}
+FGT_DEV void fgt_tm_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+FGT_DEV void fgt_tm_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+FGT_DEV void fgt_tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+FGT_DEV void fgt_tm_ld(float (&r)[4], unsigned a) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\ntcgen05.wait::ld.sync.aligned;\n"
+               : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3])
+               : "r"(a)
+               : "memory");
+}
+FGT_DEV void fgt_tm_st(unsigned a, const float (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(a), "f"(r[0]), "f"(r[1]), "f"(r[2]), "f"(r[3])
+               : "memory");
+}
+FGT_DEV void fgt_tm_ld(float (&r)[8], unsigned a) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\ntcgen05.wait::ld.sync.aligned;\n"
+               : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]), "=f"(r[7])
+               : "r"(a)
+               : "memory");
+}
+FGT_DEV void fgt_tm_st(unsigned a, const float (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(a), "f"(r[0]), "f"(r[1]),
+               "f"(r[2]), "f"(r[3]), "f"(r[4]), "f"(r[5]), "f"(r[6]), "f"(r[7])
+               : "memory");
+}
+FGT_DEV void fgt_tm_ld(float (&r)[16], unsigned a) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]), "=f"(r[7]), "=f"(r[8]), "=f"(r[9]),
+        "=f"(r[10]), "=f"(r[11]), "=f"(r[12]), "=f"(r[13]), "=f"(r[14]), "=f"(r[15])
+      : "r"(a)
+      : "memory");
+}
+FGT_DEV void fgt_tm_st(unsigned a, const float (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(a),
+      "f"(r[0]), "f"(r[1]), "f"(r[2]), "f"(r[3]), "f"(r[4]), "f"(r[5]), "f"(r[6]), "f"(r[7]), "f"(r[8]), "f"(r[9]), "f"(r[10]),
+      "f"(r[11]), "f"(r[12]), "f"(r[13]), "f"(r[14]), "f"(r[15])
+      : "memory");
+}
 template <int BYTES> FGT_DEV void fgt_cp_async(unsigned dst, const void* src) {
   if (BYTES == 16) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
   else asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(dst), "l"(src), "n"(BYTES) : "memory");

@@ -1308,6 +1308,10 @@ struct Planner {
     mix(opt.xw_tree);
     mix(opt.smem_cols);
     mix(opt.ring_resident);
+    mix(opt.phase_copies);
+    mix(opt.pack_cols);
+    mix(opt.tmem_cols);
+    mix(opt.max3);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);
     mix(opt.row_cluster);

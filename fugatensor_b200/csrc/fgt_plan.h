@@ -166,6 +166,10 @@ struct Options {
   int xw_tree = 1;                // cross-warp row reductions: tree over the warp partials (FGT_ROW_XW_SHUFFLE: butterfly)
   int own_exp = 1;                // exp in redoable row phases by fgt_exp_q, else expf (FGT_ROW_EXPF, or FGT_OWN_EXP=0)
   int ring_resident = 0;          // row kernels: operands read from the ring in every phase (FGT_ROW_RING_RESIDENT)
+  int phase_copies = 0;           // row kernels: later phases read the row operands through opaque copies (FGT_ROW_PHASE_COPIES)
+  int pack_cols = 0;              // row kernels: 16-bit per-thread column operands two per register (FGT_ROW_PACK_COLS)
+  int tmem_cols = 0;              // row kernels: column accumulators in tensor memory (FGT_ROW_TMEM_COLS)
+  int max3 = 0;                   // three-input max/min for paired range notes (NVRTC >= 12.9; FGT_MAX3=0: off)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
   int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)
   int row_cluster = 1;            // CTAs per row in block-per-row kernels (thread-block cluster; FGT_ROW_CLUSTER)

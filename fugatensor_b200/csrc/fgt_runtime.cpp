@@ -24,6 +24,7 @@
 #include <thread>
 #include <chrono>
 #include <sstream>
+#include <dlfcn.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -174,9 +175,62 @@ void publish(const std::string& path, const std::string& data) {
 // the cubin (".regs": "<registers> <spill bytes>"), and so is the SHA-256 of
 // the full key (".key"): a cached cubin is used only when that digest
 // matches, and a 64-bit name collision moves on to the next slot (-1, -2, ...).
+// NVRTC, opened at run time. The toolkit's library (the CUDA the library was
+// built with, FGT_CUDA_LIB_DIR) comes first, by its full path: a process that
+// imported PyTorch already holds PyTorch's own, older libnvrtc.so.12, and a
+// plain soname lookup would bind that one. FGT_NVRTC names another library.
+struct NvrtcApi {
+  nvrtcResult (*Version)(int*, int*) = nullptr;
+  nvrtcResult (*CreateProgram)(nvrtcProgram*, const char*, const char*, int, const char* const*, const char* const*) = nullptr;
+  nvrtcResult (*CompileProgram)(nvrtcProgram, int, const char* const*) = nullptr;
+  nvrtcResult (*GetProgramLogSize)(nvrtcProgram, size_t*) = nullptr;
+  nvrtcResult (*GetProgramLog)(nvrtcProgram, char*) = nullptr;
+  nvrtcResult (*GetCUBINSize)(nvrtcProgram, size_t*) = nullptr;
+  nvrtcResult (*GetCUBIN)(nvrtcProgram, char*) = nullptr;
+  nvrtcResult (*DestroyProgram)(nvrtcProgram*) = nullptr;
+  std::string path;
+};
+
+#ifndef FGT_CUDA_LIB_DIR
+#define FGT_CUDA_LIB_DIR "/usr/local/cuda/lib64"
+#endif
+
+const NvrtcApi& nvrtc() {
+  static NvrtcApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    std::vector<std::string> names;
+    if (const char* e = std::getenv("FGT_NVRTC")) names.push_back(e);
+    names.push_back(std::string(FGT_CUDA_LIB_DIR) + "/libnvrtc.so.12");
+    names.push_back("libnvrtc.so.12");
+    for (const std::string& n : names) {
+      void* h = dlopen(n.c_str(), RTLD_NOW | RTLD_LOCAL);
+      if (!h) continue;
+      auto sym = [&](const char* s) { return dlsym(h, s); };
+      api.Version = (decltype(api.Version))sym("nvrtcVersion");
+      api.CreateProgram = (decltype(api.CreateProgram))sym("nvrtcCreateProgram");
+      api.CompileProgram = (decltype(api.CompileProgram))sym("nvrtcCompileProgram");
+      api.GetProgramLogSize = (decltype(api.GetProgramLogSize))sym("nvrtcGetProgramLogSize");
+      api.GetProgramLog = (decltype(api.GetProgramLog))sym("nvrtcGetProgramLog");
+      api.GetCUBINSize = (decltype(api.GetCUBINSize))sym("nvrtcGetCUBINSize");
+      api.GetCUBIN = (decltype(api.GetCUBIN))sym("nvrtcGetCUBIN");
+      api.DestroyProgram = (decltype(api.DestroyProgram))sym("nvrtcDestroyProgram");
+      if (api.Version && api.CreateProgram && api.CompileProgram && api.GetProgramLogSize && api.GetProgramLog &&
+          api.GetCUBINSize && api.GetCUBIN && api.DestroyProgram) {
+        api.path = n;
+        return;
+      }
+      api = NvrtcApi();
+    }
+  });
+  if (!api.Version) fail(FGT_ERR_COMPILE, "NVRTC (libnvrtc.so.12) could not be loaded; set FGT_NVRTC to its path");
+  return api;
+}
+
 Compiled compile_cubin(const std::string& name, const std::string& src, const std::string& cache_dir) {
   int maj = 0, min = 0;
-  nvrtcVersion(&maj, &min);
+  const NvrtcApi& nv = nvrtc();
+  nv.Version(&maj, &min);
   std::string opts;
   for (const char* o : kNvrtcOptions) opts += o, opts += ' ';
   const std::string key = std::to_string(maj) + "." + std::to_string(min) + "|" + opts + "|" + src;
@@ -197,22 +251,22 @@ Compiled compile_cubin(const std::string& name, const std::string& src, const st
     return c;
   }
   nvrtcProgram prog;
-  if (nvrtcCreateProgram(&prog, src.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) != NVRTC_SUCCESS)
+  if (nv.CreateProgram(&prog, src.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) != NVRTC_SUCCESS)
     fail(FGT_ERR_COMPILE, "nvrtcCreateProgram failed for " + name);
-  nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof kNvrtcOptions / sizeof kNvrtcOptions[0]), kNvrtcOptions);
+  nvrtcResult r = nv.CompileProgram(prog, (int)(sizeof kNvrtcOptions / sizeof kNvrtcOptions[0]), kNvrtcOptions);
   size_t log_size = 0;
-  nvrtcGetProgramLogSize(prog, &log_size);
+  nv.GetProgramLogSize(prog, &log_size);
   std::string log(log_size, '\0');
-  if (log_size) nvrtcGetProgramLog(prog, &log[0]);
+  if (log_size) nv.GetProgramLog(prog, &log[0]);
   if (r != NVRTC_SUCCESS) {
-    nvrtcDestroyProgram(&prog);
+    nv.DestroyProgram(&prog);
     fail(FGT_ERR_COMPILE, "kernel " + name + " failed to compile: " + log);
   }
   size_t n = 0;
-  nvrtcGetCUBINSize(prog, &n);
+  nv.GetCUBINSize(prog, &n);
   c.cubin.assign(n, '\0');
-  nvrtcGetCUBIN(prog, &c.cubin[0]);
-  nvrtcDestroyProgram(&prog);
+  nv.GetCUBIN(prog, &c.cubin[0]);
+  nv.DestroyProgram(&prog);
   parse_ptxas_report(log, &c);
   mkdirs(cache_dir);
   publish(path + ".regs", std::to_string(c.regs) + " " + std::to_string(c.spill_bytes) + "\n");
@@ -674,8 +728,12 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
               "row_cluster must be 0 or a power of two up to 8");
       if (options->row_cluster > 0) opt.row_cluster = options->row_cluster;
       require((options->row_flags & ~(FGT_ROW_OCCUPANCY_STEP | FGT_ROW_EXPF | FGT_ROW_SMEM_COLS | FGT_ROW_XW_SHUFFLE |
-                                      FGT_ROW_RING_RESIDENT)) == 0,
+                                      FGT_ROW_RING_RESIDENT | FGT_ROW_PHASE_COPIES | FGT_ROW_PACK_COLS |
+                                      FGT_ROW_TMEM_COLS)) == 0,
               "unknown row_flags bits");
+      opt.phase_copies = (options->row_flags & FGT_ROW_PHASE_COPIES) != 0;
+      opt.pack_cols = (options->row_flags & FGT_ROW_PACK_COLS) != 0;
+      opt.tmem_cols = (options->row_flags & FGT_ROW_TMEM_COLS) != 0;
       opt.ring_resident = (options->row_flags & FGT_ROW_RING_RESIDENT) != 0;
       if (options->row_flags & FGT_ROW_XW_SHUFFLE) opt.xw_tree = 0;
       opt.occupancy_step = (options->row_flags & FGT_ROW_OCCUPANCY_STEP) != 0;
@@ -685,6 +743,13 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
     // FGT_ROW_STAGING=0 keeps streamed row operands in registers
     // (double-buffered) instead of the shared-memory ring.
     if (const char* st = std::getenv("FGT_ROW_STAGING")) opt.row_staging = std::atoi(st) != 0;
+    {
+      // three-input max / min assemble from NVRTC 12.9 on (PTX ISA 8.8)
+      int maj = 0, mnr = 0;
+      nvrtc().Version(&maj, &mnr);
+      opt.max3 = (maj > 12 || (maj == 12 && mnr >= 9)) ? 1 : 0;
+      if (const char* m3 = std::getenv("FGT_MAX3")) opt.max3 = opt.max3 && std::atoi(m3) != 0;
+    }
     if (const char* lp = std::getenv("FGT_LANE_PAIRS")) opt.lane_pairs = std::atoi(lp) != 0;
     if (const char* ox = std::getenv("FGT_OWN_EXP")) opt.own_exp = std::atoi(ox) != 0;
     if (const char* xs = std::getenv("FGT_XW_SHUFFLE")) opt.xw_tree = std::atoi(xs) == 0;

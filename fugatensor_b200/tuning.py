@@ -43,13 +43,21 @@ from . import _fgt, ir
 # Flag 4 (column accumulators in shared memory) measured no faster on any benchmark partition (the
 # LayerNorm VJP keeps one CTA per SM at 169 registers, and two with the occupancy step spill), so it
 # is not a candidate. Candidates a flag leaves unchanged compile to the same source (kernel names
-# aside) and are timed once.
-_GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0))
-CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 8) for g in _GEOMETRIES)
+# aside) and are timed once. Four and eight elements per thread (1024 / 512 threads per 4096-wide
+# f32 row) suit short single-phase rows: the c1 chain + row sum ran at 0.84 of peak at 4 elements
+# against 0.77 at 16. Flag 32 (phase-local operand copies) with 64 (packed column operands) is
+# tried where it measured ahead: the bf16 softmax forward with expf (0.86 against 0.84) and the
+# RMSNorm VJP at 32 elements (0.92, level with the default).
+_GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0), (8, 16, 0),
+               (4, 16, 0))
+CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 8) for g in _GEOMETRIES) + ((32, 24, 0, 34), (32, 32, 0, 96))
 # Geometries outside the candidate list that stay available through the spec options and are
 # parity-checked with the candidates: ring-resident rows (row flag 16) measured slower on every
-# benchmark partition (re-reading the row from shared memory in every phase), so not candidates.
-PARITY_EXTRA = ((32, 64, 0, 16), (16, 64, 0, 16))
+# benchmark partition (re-reading the row from shared memory in every phase); column accumulators
+# in shared memory with phase-local copies (4 + 32 + 64: two CTAs per SM for the LayerNorm VJP, but
+# 0.58 of peak against 0.74) and in tensor memory (128: the driver then places one CTA per SM, and
+# each chunk's tcgen05.ld / wait / st round trip cost the RMSNorm VJP 0.92 -> 0.73) measured slower.
+PARITY_EXTRA = ((32, 64, 0, 16), (16, 64, 0, 16), (32, 32, 0, 100), (32, 32, 0, 224), (16, 32, 0, 224))
 MIN_BYTES = 64 << 20  # partitions moving less than this keep the default geometry
 RTOL = {"f32": 1e-5, "f16": 1e-2, "bf16": 1e-2}  # agreement with the default geometry
 _lock = threading.Lock()
@@ -121,7 +129,10 @@ def _time_all(specs, inputs, device, flush, rounds=9):
     times = [[] for _ in specs]
     for rnd in range(rounds + 2):
         for k, (spec, ptrs_out, ws, _) in enumerate(bound):
-            flush.zero_()
+            # the benchmark's flush: writing 256 MiB evicts L2, reading another
+            # 256 MiB then writes those dirty lines back before the timed launch
+            flush[0].add_(1)
+            flush[1].sum()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             spec.launch(ptrs_in, ptrs_out, ws.data_ptr(), spec.workspace_bytes, stream.cuda_stream)
@@ -201,7 +212,7 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     gen = torch.Generator(device=dev).manual_seed(0)
     with torch.cuda.device(dev):
         inputs = [_synthetic(dt, s, dev, gen) for dt, s in default.input_types]
-        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        flush = torch.zeros((2, 256 << 20), dtype=torch.uint8, device=dev)
         ms_all = _time_all([s for _, s in specs], inputs, dev, flush)
         timed = sorted(((ms, g, s) for ms, (g, s) in zip(ms_all, specs)), key=lambda t: t[0])
         del flush

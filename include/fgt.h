@@ -165,7 +165,22 @@ typedef enum fgt_row_flag {
    * (each phase reads the thread's own pieces again), and per-thread column
    * operands of 16-bit types stay packed two per register: fewer registers
    * per thread, so more CTAs per SM, for rows with several phases */
-  FGT_ROW_RING_RESIDENT = 16
+  FGT_ROW_RING_RESIDENT = 16,
+  /* every phase after a row's first reads the row operands (and per-thread
+   * column operands) through copies the compiler cannot see through, so each
+   * phase recomputes its element values instead of the compiler keeping the
+   * earlier phases' values live: fewer registers for rows with several
+   * phases, at the price of recomputation */
+  FGT_ROW_PHASE_COPIES = 32,
+  /* per-thread column operands of 16-bit types (gamma) held two per 32-bit
+   * register, as in FGT_ROW_RING_RESIDENT, without keeping rows in the ring */
+  FGT_ROW_PACK_COLS = 64,
+  /* column-reduction accumulators (dgamma, dbeta) in the SM's tensor memory
+   * (tcgen05.alloc / ld / st): each thread keeps its columns in its own TMEM
+   * lane and reads and writes one chunk at a time, so they hold neither
+   * registers nor shared memory; f32 sums over block-per-row kernels of a
+   * multiple of 128 threads only (others keep registers) */
+  FGT_ROW_TMEM_COLS = 128
 } fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */

@@ -2,12 +2,13 @@
 
 The engine measures the row geometry of large partitions
 (fugatensor_b200/tuning.py: elements per thread, shared-memory ring size, row
-flags 1 = occupancy step, 2 = CUDA expf, 8 = shuffle butterfly) and keeps the
-fastest, so any candidate can end up being the benchmarked kernel. Each
+flags 1 = occupancy step, 2 = CUDA expf, 8 = shuffle butterfly, 32 = phase-local
+operand copies, 64 = packed column operands) and keeps the fastest, so any candidate can end up being the benchmarked kernel. Each
 benchmark row partition runs here in every candidate geometry at a medium
 size (several rows per CTA, so the prefetch ring wraps and column partials
 span many rows), against one oracle evaluation per partition. The geometries
-kept out of the candidate list (tuning.PARITY_EXTRA) run here too.
+kept out of the candidate list (tuning.PARITY_EXTRA: ring-resident rows,
+column accumulators in shared or tensor memory) run here too.
 """
 import os
 
