@@ -286,7 +286,7 @@ def run_fgt(args):
     # ---- sharded partitions (N > 1): the global problem split along dim 0,
     # reductions over it combined across ranks (strong scaling)
     if world > 1 and not args.skip_table:
-        from fugatensor_b200 import sharded
+        from fugatensor_b200 import sharded, tuning
         group = sharded.ShardGroup(world, rank)
         peak_, _ = measured_peak()
         for c, v, dt in STRONG:
@@ -298,7 +298,15 @@ def run_fgt(args):
             desc, leaves, _ = engine.trace(*W.build(c, v, full))
             names = [next(k for k, x in full.items() if x is l) for l in leaves]
             split = [i for i, k in enumerate(names) if k in ("x", "X", "dY")]
-            spec = sharded.shard_spec(desc, world, rank, split)
+            # rank-local kernels in the geometry measured for the unsharded partition of the
+            # local shapes (measured on rank 0, the same on every rank)
+            local = {k: ft.Tensor(engine, dts[k], tuple(x.shape), data=torch.empty(0)) for k, x in tt.items()}
+            geom = [None]
+            if rank == 0:
+                desc_l, _, _ = engine.trace(*W.build(c, v, local))
+                geom = [list(tuning.select_geometry(desc_l, device=str(device))[0])]
+            dist.broadcast_object_list(geom, src=0)
+            spec = sharded.shard_spec(desc, world, rank, split, geometry=geom[0])
             ins = [tt[k] for k in names]
             outs = [torch.empty(s, dtype=__import__("fugatensor_b200")._fgt.torch_dtype(d), device=device)
                     for d, s in spec.output_types]
@@ -320,7 +328,7 @@ def run_fgt(args):
             nb = W.algorithmic_bytes(c, v, r, h, dt)
             entry = {"n_gpus": world, "global_shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
                      "per_gpu_frac": round(nb / ms / 1e6 / world / peak_, 4), "kernels": spec.kernel_count,
-                     "collectives": spec.collective_count}
+                     "collectives": spec.collective_count, "geometry": geom[0]}
             partitions[f"{c}/{v}/{dt}/sharded{world}"] = dict(entry, scaling="strong")
             strong[f"{c}/{v}/{dt}"] = entry
             del tt, ins, outs, ws

@@ -372,6 +372,7 @@ struct Emitter {
   std::map<std::string, std::string> texpr;  // temp -> its defining expression
   std::map<std::string, std::string> cse;    // (scope, type, expression) -> temp
   std::set<int> div_phases;                 // phases with element divisions by a hoisted reciprocal
+  std::map<int, std::set<std::string>> div_rcps;  // the reciprocals those divisions use, per phase
   std::set<int> exp_phases;                 // phases with element exps by fgt_exp_q (range noted)
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
   std::set<int> tm_phases;                  // phases updating column accumulators held in TMEM
@@ -408,6 +409,16 @@ struct Emitter {
   // operand's index in row_sites).
   std::map<std::string, int> resident_loc;
   bool resident() const { return P.opt.ring_resident && cached && K.cluster == 1; }
+  // Narrow division applies when every floating output of the partition is
+  // f16 / bf16: their rounding hides the product's at most one-ulp f32 error.
+  bool narrow_div() const {
+    if (!P.opt.narrow_div) return false;
+    for (int o : g.outputs) {
+      const int dt = g.nodes[o].dt;
+      if (is_float(dt) && dtype_size(dt) != 2) return false;
+    }
+    return true;
+  }
   int stages = 0;                  // shared-memory ring depth (0: register path)
   int64_t stage_bytes = 0;         // bytes of one stage (all staged operands)
   // Shared-memory address (bytes from the dynamic base) of a thread's piece.
@@ -764,6 +775,7 @@ struct Emitter {
           const Node& up = g.nodes[n.args[2]];
           const int64_t HN = n.n() / n.shape[0];
           const std::string H = std::to_string(HN) + "LL";
+          const std::string NUS = std::to_string(std::max<int64_t>(1, g.nodes[n.args[1]].n())) + "LL";
           const std::string A = csr_acc_t();
           const Idx li = to_linear(m, n.shape, d);
           const std::string lin = itext(li);
@@ -772,30 +784,34 @@ struct Emitter {
           bool ident = li.aff && li.k == 0 && (int)li.c.size() == d.nd();
           for (int j = 0; ident && j < d.nd(); ++j) ident = li.c[j] == d.iw[j];
           if (elem && D.k == SC_LANE && ident && n.n() == d.NI && HN % K.vec == 0) {
-            // a chunk's VEC elements share one row: walk its bucket once and
-            // read VEC consecutive update values per entry
+            // a chunk's VEC elements share one row: walk its list once and
+            // read VEC consecutive update values per entry, two entries per
+            // step (the second entry's loads issue before the first's values
+            // are summed); at most NU hops
             auto it = memo.find("csr_chunk");
             std::string sa;
             if (it != memo.end()) sa = it->second;
             else {
               sa = fresh("sa");
               memo["csr_chunk"] = sa;
-              const std::string V = std::to_string(K.vec);
-              chunkpre[0].push_back(A + " " + sa + "[" + V + "]; for (int v = 0; v < " + V + "; ++v) " + sa + "[v] = 0; { const fgt_i64 r_ = e0 / " +
-                                    H + ", h_ = e0 - r_ * " + H + "; const int b_ = " + csr_arr(2) + "[r_], c_ = " + csr_arr(0) +
-                                    "[r_]; for (int k_ = 0; k_ < c_; ++k_) { const fgt_i64 u_ = " + csr_arr(3) + "[b_ + k_]; " +
-                                    st_t(up.dt) + " uv_[" + V + "]; fgt_vload_keep(uv_, " + ptr_of(n.args[2]) + " + u_ * " + H +
-                                    " + h_); for (int v = 0; v < " + V + "; ++v) " + sa + "[v] += (" + A + ")(" +
-                                    ld_conv(up.dt, "uv_[v]") + "); } }");
+              const std::string V = std::to_string(K.vec), ST = st_t(up.dt), U = ptr_of(n.args[2]);
+              const std::string add_a = "for (int v = 0; v < " + V + "; ++v) " + sa + "[v] += (" + A + ")(" + ld_conv(up.dt, "ua_[v]") + ");";
+              const std::string add_b = "for (int v = 0; v < " + V + "; ++v) " + sa + "[v] += (" + A + ")(" + ld_conv(up.dt, "ub_[v]") + ");";
+              chunkpre[0].push_back(
+                  A + " " + sa + "[" + V + "]; for (int v = 0; v < " + V + "; ++v) " + sa + "[v] = 0; { const fgt_i64 r_ = e0 / " + H +
+                  ", h_ = e0 - r_ * " + H + "; int i_ = " + ll_head() + "[r_]; for (fgt_i64 n_ = 0; i_ >= 0 && n_ < " + NUS +
+                  "; n_ += 2) { " + ST + " ua_[" + V + "]; fgt_vload_keep(ua_, " + U + " + (fgt_i64)i_ * " + H + " + h_); const int j_ = " +
+                  ll_next() + "[i_]; if (j_ >= 0) { " + ST + " ub_[" + V + "]; fgt_vload_keep(ub_, " + U + " + (fgt_i64)j_ * " + H +
+                  " + h_); const int k_ = " + ll_next() + "[j_]; " + add_a + " " + add_b + " i_ = k_; } else { " + add_a +
+                  " i_ = -1; } } }");
             }
             av = sa + "[v]";
           } else {
-          av = fresh("sa");
-          add(D, A + " " + av + " = 0; { const fgt_i64 l_ = " + lin +
-                     "; const fgt_i64 r_ = l_ / " + H + ", h_ = l_ - r_ * " + H + "; const int b_ = " + csr_arr(2) +
-                     "[r_], c_ = " + csr_arr(0) + "[r_]; for (int k_ = 0; k_ < c_; ++k_) { const fgt_i64 u_ = " + csr_arr(3) +
-                     "[b_ + k_]; " + av + " += (" + A + ")(" + ld_conv(up.dt, ptr_of(n.args[2]) + "[u_ * " + H + " + h_]") +
-                     "); } }");
+            av = fresh("sa");
+            add(D, A + " " + av + " = 0; { const fgt_i64 l_ = " + lin + "; const fgt_i64 r_ = l_ / " + H + ", h_ = l_ - r_ * " + H +
+                       "; int i_ = " + ll_head() + "[r_]; for (fgt_i64 n_ = 0; i_ >= 0 && n_ < " + NUS + "; ++n_) { " + av +
+                       " += (" + A + ")(" + ld_conv(up.dt, ptr_of(n.args[2]) + "[(fgt_i64)i_ * " + H + " + h_]") + "); i_ = " +
+                       ll_next() + "[i_]; } }");
           }
         }
         std::string expr;
@@ -855,6 +871,7 @@ struct Emitter {
           add(D, "const float " + q + " = @DIVQ@(" + a[0] + "," + a[1] + "," + rcp + ");");
           add(D, "@NOTE@(" + q + ");");
           div_phases.insert(D.p);
+          div_rcps[D.p].insert(rcp);
           expr = rnd(n.dt, q);
         } else {
           expr = rnd(n.dt, "fgt_div_by(" + a[0] + "," + a[1] + "," + rcp + ")");
@@ -1600,6 +1617,14 @@ struct Emitter {
       // redo computes them with expf.
       const bool track = (div_phases.count(p) || exp_phases.count(p)) && !col_phases.count(p) && cached;
       const std::string dx = "dgx" + std::to_string(p), dn = "dgn" + std::to_string(p), de = "dge" + std::to_string(p);
+      // Narrow division (FGT_ROW_NARROW_DIV, partitions whose floating outputs
+      // are all 16-bit): x * RN(1/d) with no range notes; the phase is redone
+      // with IEEE division only when a row's divisor has no normal reciprocal
+      // (fgt_recip_for_div's NaN).
+      const bool narrow = narrow_div();
+      std::string rcp_ok;
+      if (narrow && div_rcps.count(p))
+        for (auto& rc : div_rcps[p]) rcp_ok += " && fgt_rcp_ok(" + rc + ")";
       if (track)
         o << "    float " << dx << " = 0.0f, " << dn << " = __int_as_float(0x7f800000), " << de << " = 0.0f;\n";
       if (p > 0 && P.opt.phase_copies && cached) {
@@ -1620,13 +1645,13 @@ struct Emitter {
       if (tm_phases.count(p)) o << "    fgt_tm_wait_st();\n";
       o << "    if (rv) {\n";
       phase_loop(p,
-                 track ? div_form(lane[p], "fgt_div_q", "fgt_div_note(" + dx + ", " + dn + ", ", "fgt_exp_q",
-                                  "fgt_exp_note(" + de + ", ")
-                       : div_form(lane[p], "fgt_div_by", ""),
+                 track ? div_form(lane[p], narrow ? "@MUL@" : "fgt_div_q",
+                                  narrow ? "" : "fgt_div_note(" + dx + ", " + dn + ", ", "fgt_exp_q", "fgt_exp_note(" + de + ", ")
+                       : div_form(lane[p], narrow ? "fgt_div_nby" : "fgt_div_by", ""),
                  "    ");
       o << "    }\n";
       if (track) {
-        o << "    if (rv && !(fgt_div_ok(" << dx << ", " << dn << ") && fgt_exp_ok(" << de << "))) {\n";
+        o << "    if (rv && !(fgt_div_ok(" << dx << ", " << dn << ") && fgt_exp_ok(" << de << ")" << rcp_ok << ")) {\n";
         put(o, resets[p], "      ");
         phase_loop(p, div_form(lane[p], "fgt_div_ieee", ""), "    ");
         o << "    }\n";
@@ -1689,18 +1714,13 @@ struct Emitter {
   std::string scatter_acc_ptr() const {
     return "((" + scatter_acc_t() + "*)(p.ws+" + std::to_string(K.scatter_acc) + "LL))";
   }
-  // CSR scatter: int32 arrays 0 counts, 1 fill cursors, 2 bucket offsets (R
-  // each, padded to a multiple of 4 so every array is 16-byte aligned), 3
-  // update ids (one per index)
-  std::string csr_arr(int k) const {
+  // Bucket lists of a row scatter: head[r] is the last update scattered to
+  // base row r (-1: none) and next[i] the update after update i in its row's
+  // list (ints; RA = R rounded up to 4 keeps next 16-byte aligned).
+  std::string ll_head() const { return "((int*)(p.ws+" + std::to_string(K.scatter_acc) + "LL))"; }
+  std::string ll_next() const {
     const int64_t RA = (g.nodes[K.scatter_node].shape[0] + 3) / 4 * 4;
-    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * RA * k) + "LL))";
-  }
-  // the bucket-space cursor, after the update ids
-  std::string csr_cursor() const {
-    const Node& n = g.nodes[K.scatter_node];
-    const int64_t RA = (n.shape[0] + 3) / 4 * 4, NU = std::max<int64_t>(1, g.nodes[n.args[1]].n());
-    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * (3 * RA + NU)) + "LL))";
+    return "((int*)(p.ws+" + std::to_string(K.scatter_acc + 4 * RA) + "LL))";
   }
   // bucket sums: f64 for floats (rounded once with the base), unsigned
   // (wrapping) for integers
@@ -1709,32 +1729,6 @@ struct Emitter {
     if (is_float(n.dt)) return "double";
     return n.dt == FGT_I64 ? "unsigned long long" : "unsigned int";
   }
-  // stage 13: bucket offsets. A row's bucket only has to be a contiguous
-  // slot of the id array, in any place, so each warp takes 32 rows, scans
-  // their counts with shuffles and reserves one block for them from the
-  // cursor with a single atomicAdd (one atomic per 32 rows, all CTAs at
-  // once). The loop bound is uniform per warp: every lane reaches the
-  // shuffles.
-  std::string build_scan() {
-    const int64_t R = g.nodes[K.scatter_node].shape[0];
-    std::ostringstream o;
-    o << args_struct();
-    o << "extern \"C\" __global__ void __launch_bounds__(" << K.nt << ") " << K.name << "(const FgtArgs p) {\n";
-    o << "  const int lane = threadIdx.x & 31;\n";
-    o << "  const fgt_i64 R = " << R << "LL;\n";
-    o << "  const int* cnt = " << csr_arr(0) << "; int* off = " << csr_arr(2) << "; int* cursor = " << csr_cursor() << ";\n";
-    o << "  const fgt_i64 nw = (fgt_i64)gridDim.x * (blockDim.x >> 5);\n";
-    o << "  for (fgt_i64 w0 = ((fgt_i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; w0 < R; w0 += nw * 32) {\n";
-    o << "    const fgt_i64 i = w0 + lane;\n";
-    o << "    const int c = i < R ? cnt[i] : 0;\n";
-    o << "    int x = c;\n";
-    o << "    #pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { const int y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= d) x += y; }\n";
-    o << "    int base = 0;\n    if (lane == 31) base = atomicAdd(cursor, x);\n";
-    o << "    base = __shfl_sync(0xffffffffu, base, 31);\n";
-    o << "    if (i < R) off[i] = base + x - c;\n  }\n}\n";
-    return o.str();
-  }
-
   std::string build_elem() {
     nphase = 1;
     rowsc.assign(2, {});
@@ -1745,11 +1739,10 @@ struct Emitter {
     std::vector<std::pair<RedText, std::string>> accs;
     std::vector<std::string> partial_store;
     if (K.scatter_stage == 1) lane[0].push_back(scatter_acc_ptr() + "[e] = 0;");
-    if (K.scatter_stage == 11)
-      lane[0].push_back(csr_arr(0) + "[e] = 0; " + csr_arr(1) + "[e] = 0; if (e == 0) " + csr_cursor() + "[0] = 0;");
-    if (K.scatter_stage == 12 || K.scatter_stage == 14) {
-      // over the indices: count each in-range index's update, then place its
-      // id in the row's bucket (a cursor per row; order within a bucket free)
+    if (K.scatter_stage == 11) lane[0].push_back(ll_head() + "[e] = -1;");
+    if (K.scatter_stage == 12) {
+      // over the indices: each in-range index's update becomes the head of its
+      // row's list, the previous head its next (order within a list free)
       const Node& n = g.nodes[K.scatter_node];
       Map mi;
       mi.lin = true;
@@ -1757,9 +1750,7 @@ struct Emitter {
       for (int j = 0; j < d.nd(); ++j) mi.l.c[j] = d.iw[j];
       const std::string iv = val(n.args[1], mi, Sc{SC_LANE, 0});
       const std::string R = std::to_string(n.shape[0]) + "LL";
-      const std::string body = K.scatter_stage == 12
-                                   ? "atomicAdd(" + csr_arr(0) + " + gi_, 1);"
-                                   : csr_arr(3) + "[" + csr_arr(2) + "[gi_] + atomicAdd(" + csr_arr(1) + " + gi_, 1)] = (int)e;";
+      const std::string body = ll_next() + "[e] = atomicExch(" + ll_head() + " + gi_, (int)e);";
       lane[0].push_back("{ const fgt_i64 gi_ = (fgt_i64)(" + iv + "); if (gi_ >= 0LL && gi_ < " + R + ") " + body + " }");
     }
     if (K.scatter_stage == 2) {
@@ -2132,7 +2123,20 @@ struct Emitter {
         if (!enote.empty()) out.push_back(enote + s.substr(8));
         continue;
       }
-      for (size_t at; (at = s.find("@DIVQ@")) != std::string::npos;) s.replace(at, 6, fn);
+      for (size_t at; (at = s.find("@DIVQ@")) != std::string::npos;) {
+        if (fn != "@MUL@") {
+          s.replace(at, 6, fn);
+          continue;
+        }
+        // x * y with y = RN(1/d): the argument list (x, d, y) up to its closing parenthesis
+        size_t e = at + 7;
+        for (int depth = 1; e < s.size() && depth > 0; ++e) {
+          if (s[e] == '(') ++depth;
+          else if (s[e] == ')') --depth;
+        }
+        auto xa = split_args(s.substr(at + 7, e - 1 - (at + 7)));
+        s.replace(at, e - at, "__fmul_rn(" + xa[0] + "," + xa[2] + ")");
+      }
       for (size_t at; (at = s.find("@EXPQ@")) != std::string::npos;) s.replace(at, 6, efn);
       out.push_back(s);
     }
@@ -2370,7 +2374,7 @@ struct Emitter {
   }
 
   std::string build() {
-    std::string src = row ? build_row() : elem ? (K.scatter_stage == 13 ? build_scan() : build_elem()) : build_fin();
+    std::string src = row ? build_row() : elem ? build_elem() : build_fin();
     // kernels without per-phase tracking keep the per-element guarded division
     std::istringstream in(src);
     std::ostringstream out;

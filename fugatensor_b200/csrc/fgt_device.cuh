@@ -214,6 +214,11 @@ FGT_DEV void fgt_div_note2(float& mx, float& mn, float a, float b) {
 FGT_DEV void fgt_exp_note2(float& mx, float a, float b) {
   asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(mx) : "f"(mx), "f"(fabsf(a)), "f"(fabsf(b)));
 }
+// Narrow division (x * RN(1/d), partitions with only 16-bit floating
+// outputs): usable while the row's reciprocal is a number (fgt_recip_for_div
+// returns NaN for a divisor without a normal reciprocal).
+FGT_DEV bool fgt_rcp_ok(float y) { return y == y; }
+FGT_DEV float fgt_div_nby(float x, float d, float y) { return y == y ? __fmul_rn(x, y) : __fdiv_rn(x, d); }
 FGT_DEV bool fgt_div_ok(float mx, float mn) { return mx <= 1.32922800e+36f && mn >= 7.52316385e-37f; }
 FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // Max / min of a packed accumulator with a register row piece of N bf16

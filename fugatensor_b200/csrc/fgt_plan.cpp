@@ -671,18 +671,18 @@ struct Planner {
     const Node& base = g.nodes[n.args[0]];
     const Node& up = g.nodes[n.args[2]];
     const int ax = (int)n.attrs[0], ir = g.nodes[n.args[1]].rank();
-    // Counting-sort form for row scatters whose updates are materialised
-    // (read by pointer at any update row): every update is read once and no
-    // base-sized accumulator is zeroed, updated atomically and read back.
+    // Bucket form for row scatters whose updates are materialised (read by
+    // pointer at any update row): every update is read once and no base-sized
+    // accumulator is zeroed, updated atomically and read back. Each base row
+    // heads a list of the updates scattered to it.
     const bool csr = ax == 0 && ir == 1 && base.rank() >= 1 && loc[n.args[2]].kind != Loc::NONE && base.shape[0] > 0 &&
                      base.shape[0] < (1LL << 31) && g.nodes[n.args[1]].n() < (1LL << 31);
     const int acc_bytes = is_float(n.dt) ? 8 : dtype_size(n.dt);
     const int64_t R = base.rank() >= 1 ? base.shape[0] : 1, NU = g.nodes[n.args[1]].n();
-    // CSR arrays: counts, cursors and offsets of RA = R rounded up to 4 ints
-    // each (every array 16-byte aligned), one update id per index, then the
-    // cursor that hands out bucket space
+    // bucket lists: a head per base row (RA = R rounded up to 4 ints, so the
+    // next array is 16-byte aligned) and the next update of each index
     const int64_t RA = (R + 3) / 4 * 4;
-    const int64_t acc = csr ? alloc((3 * RA + std::max<int64_t>(1, NU) + 1) * 4)
+    const int64_t acc = csr ? alloc((RA + std::max<int64_t>(1, NU)) * 4)
                             : alloc(std::max<int64_t>(1, base.n()) * acc_bytes);
     auto make = [&](const Shape& shape, int stage) {
       KernelDef k;
@@ -719,11 +719,6 @@ struct Planner {
       geometry_elem(z);
       plan.kernels.push_back(z);
       if (NU > 0) plan.kernels.push_back(indices_kernel(12));
-      KernelDef sc = make(Shape{R}, 13);
-      sc.vec = 1;
-      geometry_elem(sc);
-      plan.kernels.push_back(sc);
-      if (NU > 0) plan.kernels.push_back(indices_kernel(14));
     }
     auto identity = [&](const KernelDef& k) {
       Map m;
@@ -1312,6 +1307,7 @@ struct Planner {
     mix(opt.pack_cols);
     mix(opt.tmem_cols);
     mix(opt.max3);
+    mix(opt.narrow_div);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);
     mix(opt.row_cluster);

@@ -35,9 +35,13 @@ class ShardGroup:
         self.comm.close()
 
 
-def shard_spec(descriptor: ir.Descriptor, world: int, rank: int, shard_inputs, accumulation="wide"):
-    """Rank-local spec of a global partition; shard_inputs lists the dim-0-split input ports."""
-    return _fgt.Spec(descriptor, accumulation=accumulation, world=world, rank=rank, shard_inputs=tuple(shard_inputs))
+def shard_spec(descriptor: ir.Descriptor, world: int, rank: int, shard_inputs, accumulation="wide", geometry=None):
+    """Rank-local spec of a global partition; shard_inputs lists the dim-0-split input ports.
+    geometry: row geometry (elements, ring KB, cluster, flags) of the rank-local kernels, e.g.
+    the one tuning.select_geometry measured for the unsharded partition of the local shapes."""
+    e, r, c, f = tuple(geometry) if geometry else (0, 0, 0, 0)
+    return _fgt.Spec(descriptor, accumulation=accumulation, world=world, rank=rank, shard_inputs=tuple(shard_inputs),
+                     row_elems=e, ring_kb=r, row_cluster=c, row_flags=f)
 
 
 def local_rows(global_rows: int, world: int, rank: int):

@@ -51,6 +51,9 @@ from . import _fgt, ir
 _GEOMETRIES = ((0, 0, 0), (16, 32, 0), (16, 24, 0), (32, 96, 0), (32, 32, 0), (32, 24, 0), (32, 64, 0), (8, 16, 0),
                (4, 16, 0))
 CANDIDATES = tuple(g + (f,) for f in (0, 1, 2, 8) for g in _GEOMETRIES) + ((32, 24, 0, 34), (32, 32, 0, 96))
+# Narrow division (flag 256) changes only partitions whose floating outputs are all f16 / bf16, where
+# the outputs' rounding hides its one-ulp f32 error; the agreement check above bounds it too.
+CANDIDATES += tuple(g + (f,) for f in (256, 258) for g in ((32, 24, 0), (32, 32, 0), (16, 32, 0), (32, 64, 0)))
 # Geometries outside the candidate list that stay available through the spec options and are
 # parity-checked with the candidates: ring-resident rows (row flag 16) measured slower on every
 # benchmark partition (re-reading the row from shared memory in every phase); column accumulators
@@ -180,10 +183,17 @@ def agrees(outs, ref, types):
 
 def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     """The spec of `desc` with the fastest measured row geometry (default geometry without a GPU)."""
+    return select_geometry(desc, accumulation=accumulation, device=device, cache_dir=cache_dir)[1]
+
+
+def select_geometry(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
+    """(geometry, spec): the measured row geometry of `desc` as (elements, ring KB,
+    cluster, flags) and its spec. A sharded partition's rank-local kernels take
+    the geometry measured for the unsharded partition of the local shapes."""
     import torch
     default = _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir)
     if not torch.cuda.is_available() or not _block_rows(default) or _moved_bytes(desc) < MIN_BYTES:
-        return default
+        return (0, 0, 0, 0), default
     dev = torch.device(device)
     name = torch.cuda.get_device_name(dev)
     key = hashlib.sha256(f"{desc.key()}|{accumulation}|{name}|{_lib_tag()}".encode()).hexdigest()[:32]
@@ -192,10 +202,10 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
     if hit is not None:
         geom = tuple(hit["geometry"]) + (0,) * (4 - len(hit["geometry"]))
         if geom == (0, 0, 0, 0):
-            return default
+            return geom, default
         e, r, c, o = geom
-        return _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r, row_cluster=c,
-                         row_flags=o)
+        return geom, _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir, row_elems=e, ring_kb=r, row_cluster=c,
+                               row_flags=o)
     specs, seen = [], {}
     for e, r, c, o in CANDIDATES:
         s = default if (e, r, c, o) == (0, 0, 0, 0) else _fgt.Spec(desc, accumulation=accumulation, cache_dir=cache_dir,
@@ -208,7 +218,7 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
         specs.append(((e, r, c, o), s))
     if len(specs) == 1:
         _store(path, key, {"geometry": [0, 0, 0, 0], "ms": None})
-        return default
+        return (0, 0, 0, 0), default
     gen = torch.Generator(device=dev).manual_seed(0)
     with torch.cuda.device(dev):
         inputs = [_synthetic(dt, s, dev, gen) for dt, s in default.input_types]
@@ -226,4 +236,4 @@ def select(desc, *, accumulation="wide", device="cuda:0", cache_dir=None):
         del inputs, ref
     _store(path, key, {"geometry": list(geom), "ms": round(ms, 5), "rejected": rejected,
                        "candidates": {"x".join(map(str, g)): round(t, 5) for t, g, _ in timed}})
-    return best
+    return tuple(geom), best

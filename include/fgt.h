@@ -180,7 +180,14 @@ typedef enum fgt_row_flag {
    * lane and reads and writes one chunk at a time, so they hold neither
    * registers nor shared memory; f32 sums over block-per-row kernels of a
    * multiple of 128 threads only (others keep registers) */
-  FGT_ROW_TMEM_COLS = 128
+  FGT_ROW_TMEM_COLS = 128,
+  /* in partitions whose floating outputs are all f16 / bf16, element
+   * divisions by a row constant d are computed as x * RN(1/d) (at most one
+   * ulp of f32 from the IEEE quotient, which the 16-bit rounding of the
+   * outputs hides but for rounding ties), without the per-element range
+   * checks of the exact form; a row whose divisor has no normal reciprocal
+   * is computed with IEEE division. Other partitions are unchanged. */
+  FGT_ROW_NARROW_DIV = 256
 } fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */

@@ -234,17 +234,18 @@ def test_column_reductions_over_long_rows_plan_as_tiles():
     assert k0["threads_per_row"] == 512 and not k0["streaming"] and k0["col_tiles"] == 1
 
 
-def test_row_scatter_plans_as_counting_sort():
+def test_row_scatter_plans_as_bucket_lists():
     """scatter_add along axis 0 with 1-D indices and materialised updates takes
-    the counting-sort form (zero, count, bucket allocation, fill, bucket sums);
-    other scatters keep the atomic accumulator form."""
+    the bucket-list form (clear the list heads, link every in-range update into
+    its row's list, walk each row's list once); other scatters keep the atomic
+    accumulator form."""
     from fugatensor_b200 import _fgt
     g = ir.Graph()
     b, i, u = g.parameter("f32", (1000, 64)), g.parameter("i32", (300,)), g.parameter("f32", (300, 64))
     s = _fgt.Spec(g.descriptor([g.scatter_add(b, i, u, 0)]))
     ks = s.execution_plan["cuda_lowering"]["kernels"]
-    assert len(ks) == 5 and "atomicAdd(cursor" in s.kernel_source(2)
-    assert "atomicAdd" not in s.kernel_source(4) and "fgt_vload_keep(uv_" in s.kernel_source(4)
+    assert len(ks) == 3 and "] = -1;" in s.kernel_source(0) and "atomicExch(" in s.kernel_source(1)
+    assert "atomic" not in s.kernel_source(2) and "fgt_vload_keep(ua_" in s.kernel_source(2)
     # along axis 1: the accumulator form
     g = ir.Graph()
     b, i, u = g.parameter("f32", (64, 1000)), g.parameter("i32", (300,)), g.parameter("f32", (64, 300))

@@ -298,3 +298,58 @@ def test_shared_memory_column_accumulators_change_no_bit(dtype):
         res.append([(o.view(torch.int16) if o.dtype == torch.bfloat16 else o).cpu().numpy() for o in out])
     for k, (u, w) in enumerate(zip(*res)):
         assert np.array_equal(u.view(np.uint8), w.view(np.uint8)), f"output {k}"
+
+
+def test_narrow_division_within_one_bf16_ulp_of_exact():
+    """Row flag 256 (narrow division) computes a bf16 softmax VJP's element
+    divisions as x * RN(1/s): every output equals the exact-division kernel's
+    or is one bf16 ulp from it (a rounding tie moved by the product's f32
+    error), few outputs move at all, and both match the oracle. Rows whose
+    statistics are not finite take IEEE division in both kernels."""
+    import torch
+    import fugatensor_b200.nn.functional as F
+    from fugatensor_b200 import _fgt
+    from tests._util import assert_matches
+    rng = np.random.default_rng(17)
+    rows, cols = 96, 8192
+    x = rng.standard_normal((rows, cols)).astype(np.float32) * 3
+    dy = rng.standard_normal((rows, cols)).astype(np.float32)
+    x[1, :5] = -np.inf           # exp underflows to 0 there
+    x[2, :] = 0.5                # a flat row
+    x[3, 7] = np.inf             # the row's statistics are NaN: the IEEE form runs
+    x[4, :100] = -80.0           # a wide spread: tiny quotients
+    eng = ft.Engine("cuda:0", tune=False)
+    X = eng.tensor(O.f32_to_bf16_bits(x), dtype=ft.bf16)
+    DY = eng.tensor(O.f32_to_bf16_bits(dy), dtype=ft.bf16)
+    y = F.softmax(X, axis=-1)
+    (dx,) = ft.grad(y, [X], seed=DY)
+    desc, leaves, roots = eng.trace(dx)
+    ins = [l._data for l in leaves]
+    res = []
+    for flags in (0, 256):
+        spec = _fgt.Spec(desc, row_elems=32, ring_kb=24, row_flags=flags)
+        src = "".join(spec.kernel_source(i) for i in range(spec.kernel_count))
+        assert ("fgt_div_note" in src) == (flags == 0)
+        (out,) = _fgt.run(spec, *ins)
+        torch.cuda.synchronize()
+        res.append(out.view(torch.int16).cpu().numpy().view(np.uint16))
+    exact, narrow = res
+    host = {id(X): O.f32_to_bf16_bits(x), id(DY): O.f32_to_bf16_bits(dy)}
+    ref = O.evaluate(desc, [host[id(l)] for l in leaves], O.ACCURATE)[0]
+    rn = np.isnan(O.bf16_bits_to_f32(ref))
+    for name, got in (("exact", exact), ("narrow", narrow)):
+        bad = np.flatnonzero((np.isnan(O.bf16_bits_to_f32(got)) != rn).any(axis=1))
+        assert bad.size == 0, f"{name}: NaN positions differ from the oracle in rows {bad[:8]}"
+    assert_matches(narrow, ref, "bf16", what="narrow division")
+    assert_matches(exact, ref, "bf16", what="exact division")
+    ev = O.bf16_bits_to_f32(exact).astype(np.float64)
+    nv = O.bf16_bits_to_f32(narrow).astype(np.float64)
+    fin = np.isfinite(ev)
+    assert np.array_equal(exact[~fin], narrow[~fin])
+    assert np.array_equal(exact[3], narrow[3])   # IEEE form in both
+    # one bf16 ulp is at most 2^-7 of the larger magnitude (plus a sliver of
+    # the output's scale where the exact result cancels to zero)
+    gap = np.abs(ev - nv)[fin]
+    scale = np.abs(ev[fin]).max()
+    assert np.all(gap <= np.maximum(np.abs(ev), np.abs(nv))[fin] * 2.0 ** -7 + scale * 2.0 ** -20), gap.max()
+    assert (gap > 0).mean() < 0.01
