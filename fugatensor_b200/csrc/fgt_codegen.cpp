@@ -2044,7 +2044,12 @@ struct Emitter {
         col_partial_loop(o, comb, accs, tail);
         o << "  __threadfence_system();\n  __syncthreads();\n";
         flags_and_wait();
-        o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
+        // The flags pair this CTA with the same CTA of every rank, so the
+        // combine reads only the column blocks this CTA index wrote above
+        // (blocks blockIdx.x + k * gridDim.x of 32 columns), one per warp.
+        o << "  for (fgt_i64 cb_ = blockIdx.x + (fgt_i64)(tid >> 5) * gridDim.x; cb_ * 32 < NI; cb_ += (fgt_i64)gridDim.x * "
+          << K.nt / 32 << ") {\n";
+        o << "    const fgt_i64 e = cb_ * 32 + (tid & 31);\n    if (e >= NI) continue;\n";
         o << "    " << digits_i() << "\n";
         put(o, comb2, "    ");
         put(o, finals, "    ");
