@@ -299,12 +299,11 @@ def run_fgt(args):
             names = [next(k for k, x in full.items() if x is l) for l in leaves]
             split = [i for i, k in enumerate(names) if k in ("x", "X", "dY")]
             # rank-local kernels in the geometry measured for the unsharded partition of the
-            # local shapes (measured on rank 0, the same on every rank)
+            # local shapes: every rank measures it on its own GPU (so none waits long in the
+            # broadcast) and all take rank 0's choice
             local_t = {k: ft.Tensor(engine, dts[k], tuple(x.shape), data=torch.empty(0)) for k, x in tt.items()}
-            geom = [None]
-            if rank == 0:
-                desc_l, _, _ = engine.trace(*W.build(c, v, local_t))
-                geom = [list(tuning.select_geometry(desc_l, device=str(device))[0])]
+            desc_l, _, _ = engine.trace(*W.build(c, v, local_t))
+            geom = [list(tuning.select_geometry(desc_l, device=str(device))[0])]
             dist.broadcast_object_list(geom, src=0)
             spec = sharded.shard_spec(desc, world, rank, split, geometry=geom[0])
             ins = [tt[k] for k in names]

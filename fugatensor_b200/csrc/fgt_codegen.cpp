@@ -1893,8 +1893,21 @@ struct Emitter {
     // the kColGroups warps of a CTA sums every kColGroups-th partial of its
     // 32 columns (pg_ is the warp's group)
     const bool full = K.kind == KKind::FULLFIN;
-    s << "for (fgt_i64 q_ = " << (full ? "tid" : "pg_") << "; q_ < " << count << "; q_ += "
-      << (full ? std::to_string(K.nt) : std::to_string(kColGroups)) << ") { ";
+    const std::string Q0 = full ? "tid" : "pg_", QS = full ? std::to_string(K.nt) : std::to_string(kColGroups);
+    if (!t.arg && !full) {
+      // four partials' loads in flight per step, combined in order (the same
+      // sums as one partial at a time)
+      s << "for (int once_ = 0; once_ < 1; ++once_) { fgt_i64 q_ = " << Q0 << "; for (; q_ + 3 * " << QS << " < " << count
+        << "; q_ += 4 * " << QS << ") { ";
+      for (int k = 0; k < 4; ++k)
+        s << "const " << t.fin_t << " o" << k << "_ = (" << t.fin_t << ")" << pv << "[(q_ + " << k << " * " << QS << ")*" << M
+          << "LL+" << e << "]; ";
+      for (int k = 0; k < 4; ++k) s << comb_stmt(t, a, "o" + std::to_string(k) + "_") << " ";
+      s << "} for (; q_ < " << count << "; q_ += " << QS << ") { const " << t.fin_t << " ov = (" << t.fin_t << ")" << pv << "[q_*"
+        << M << "LL+" << e << "]; " << comb_stmt(t, a, "ov") << " } }";
+      return s.str();
+    }
+    s << "for (fgt_i64 q_ = " << Q0 << "; q_ < " << count << "; q_ += " << QS << ") { ";
     if (t.arg) s << "{ const " << src_t << " ov = " << pv << "[q_*" << M << "LL+" << e << "]; const fgt_i64 oi = " << pi << "[q_*"
                  << M << "LL+" << e << "]; " << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
     else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << pv << "[q_*" << M << "LL+" << e << "]; " << comb_stmt(t, a, "ov") << " }";
