@@ -1820,9 +1820,9 @@ struct Emitter {
     std::ostringstream o;
     const std::string NT = std::to_string(K.nt), VEC = std::to_string(K.vec), UU = std::to_string(U);
     o << args_struct();
-    // the row-scatter bucket sums wait on dependent loads (bucket offset, update
-    // id, update row): more resident warps hide more of that latency
-    const std::string LB = K.scatter_csr && K.scatter_stage == 3 ? NT + ", 5" : NT;
+    // the row-scatter bucket sums wait on dependent loads (list head, next link,
+    // update row): more resident warps hide more of that latency
+    const std::string LB = K.scatter_csr && K.scatter_stage == 3 ? NT + ", 8" : NT;
     o << "extern \"C\" __global__ void __launch_bounds__(" << LB << ") " << K.name << "(const FgtArgs p) {\n";
     o << "  const int tid = threadIdx.x; const fgt_i64 r = 0; const bool rv = true; (void)r; (void)rv;\n";
     o << "  const fgt_i64 NI = " << d.NI << "LL; const fgt_i64 NCK = NI / " << VEC << ";\n";

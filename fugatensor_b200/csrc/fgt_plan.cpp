@@ -784,6 +784,9 @@ struct Planner {
     }
     choose_vec(k3, an.vec_loads, outs);
     geometry_elem(k3);
+    // bucket sums: one vector chunk per thread per step, and more resident
+    // warps (8 CTAs of 256 per SM) to hide the dependent list loads
+    if (csr) k3.unroll = 1;
     plan.kernels.push_back(k3);
     loc[s] = L;
   }
