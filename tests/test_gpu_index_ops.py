@@ -56,7 +56,7 @@ def test_gather_rows_and_columns(rows, cols):
 @pytest.mark.parametrize("rows,cols,n", [(512, 96, 4000), (1021, 33, 3000), (70001, 8, 50000)])
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "i32", "i64"])
 def test_scatter_add_random(dtype, rows, cols, n):
-    """Row scatter_add (the counting-sort form) against the oracle: duplicate and
+    """Row scatter_add (the bucket-list form) against the oracle: duplicate and
     out-of-range indices, odd row counts, and more rows than one scan step."""
     rng = np.random.default_rng(11 + rows)
     idx = rng.integers(-5, rows + 5, n).astype(np.int32)
