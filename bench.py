@@ -302,8 +302,10 @@ def run_fgt(args):
             # local shapes: every rank measures it on its own GPU (so none waits long in the
             # broadcast) and all take rank 0's choice
             local_t = {k: ft.Tensor(engine, dts[k], tuple(x.shape), data=torch.empty(0)) for k, x in tt.items()}
-            desc_l, _, _ = engine.trace(*W.build(c, v, local_t))
-            geom = [list(tuning.select_geometry(desc_l, device=str(device))[0])]
+            desc_l, leaves_l, _ = engine.trace(*W.build(c, v, local_t))
+            ins_l = [tt[next(k for k, x in local_t.items() if x is l)] for l in leaves_l]
+            geom_l, spec_l = tuning.select_geometry(desc_l, device=str(device))
+            geom = [list(geom_l)]
             dist.broadcast_object_list(geom, src=0)
             spec = sharded.shard_spec(desc, world, rank, split, geometry=geom[0])
             ins = [tt[k] for k in names]
@@ -321,13 +323,30 @@ def run_fgt(args):
             b.record(stream)
             torch.cuda.synchronize()
             ms = a.elapsed_time(b) / args.table_iters
-            t = torch.tensor([ms], device=device)
+            # the same rank-local work without the cross-rank combine: the unsharded
+            # partition of the local shapes, timed the same way (the difference is
+            # the exchange's cost)
+            outs_l = [torch.empty(s_, dtype=__import__("fugatensor_b200")._fgt.torch_dtype(d_), device=device)
+                      for d_, s_ in spec_l.output_types]
+            ws_l = torch.empty(max(1, spec_l.workspace_bytes), dtype=torch.uint8, device=device)
+            for _ in range(3):
+                __import__("fugatensor_b200")._fgt.run(spec_l, *ins_l, outputs=outs_l, workspace=ws_l)
+            torch.cuda.synchronize()
+            a.record(stream)
+            for _ in range(args.table_iters):
+                __import__("fugatensor_b200")._fgt.run(spec_l, *ins_l, outputs=outs_l, workspace=ws_l)
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms_l = a.elapsed_time(b) / args.table_iters
+            t = torch.tensor([ms, ms_l], device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+            ms, ms_l = float(t[0].item()), float(t[1].item())
+            del outs_l, ws_l
             nb = W.algorithmic_bytes(c, v, r, h, dt)
             entry = {"n_gpus": world, "global_shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
                      "per_gpu_frac": round(nb / ms / 1e6 / world / peak_, 4), "kernels": spec.kernel_count,
-                     "collectives": spec.collective_count, "geometry": geom[0]}
+                     "collectives": spec.collective_count, "geometry": geom[0],
+                     "local_ms": round(ms_l, 5)}
             partitions[f"{c}/{v}/{dt}/sharded{world}"] = dict(entry, scaling="strong")
             strong[f"{c}/{v}/{dt}"] = entry
             del tt, ins, outs, ws
