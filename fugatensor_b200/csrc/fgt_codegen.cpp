@@ -1585,7 +1585,7 @@ struct Emitter {
     }
     if (res) o << "    fgt_cp_wait<" << stages - 1 << ">();\n";
     put(o, rowdecl, "    ");
-    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind, bool with_post = true) {
+    auto phase_loop = [&](int p, const std::vector<std::string>& body, const std::string& ind) {
       if (cached) o << ind << "  #pragma unroll\n";
       else o << ind << "  #pragma unroll 1\n";
       o << ind << "  for (int c = 0; c < " << NCH << "; ++c) {\n";
@@ -1602,7 +1602,7 @@ struct Emitter {
         put(o, body, ind + "        ");
       }
       o << ind << "      }\n";
-      if (with_post) put(o, chunkpost[p], ind + "      ");
+      put(o, chunkpost[p], ind + "      ");
       o << ind << "    }\n" << ind << "  }\n";
     };
     for (int p = 0; p < nphase; ++p) {
@@ -1643,34 +1643,6 @@ struct Emitter {
       }
       // this phase's TMEM loads follow the earlier rows' stores of the same columns
       if (tm_phases.count(p)) o << "    fgt_tm_wait_st();\n";
-      // Split tail (FGT_ROW_SPLIT_TAIL): the phase's element loop runs twice.
-      // The first computes only what its row reductions need; the reduction
-      // tail (fold, shuffles, the warp partials' stores) follows, then the
-      // second loop does the rest (column accumulators, element stores,
-      // cached values), and only then the barrier. The scheduler can then fill
-      // the shuffles' latency with the second loop's independent work.
-      std::vector<std::string> first_, second_;
-      size_t bar_at = std::string::npos;
-      if (P.opt.split_tail && cached && !track && !tm_phases.count(p) && phase_accs.count(p)) {
-        for (size_t i = 0; i < post[p].size(); ++i)
-          if (post[p][i] == "__syncthreads();") {
-            bar_at = i;
-            break;
-          }
-        if (bar_at != std::string::npos) split_phase(lane[p], phase_accs[p], &first_, &second_);
-        if (first_.empty() || second_.empty()) bar_at = std::string::npos;
-      }
-      if (bar_at != std::string::npos) {
-        o << "    if (rv) {\n";
-        phase_loop(p, div_form(first_, narrow ? "fgt_div_nby" : "fgt_div_by", ""), "    ", false);
-        o << "    }\n";
-        for (size_t i = 0; i < bar_at; ++i) o << "    " << post[p][i] << "\n";
-        o << "    if (rv) {\n";
-        phase_loop(p, div_form(second_, narrow ? "fgt_div_nby" : "fgt_div_by", ""), "    ");
-        o << "    }\n";
-        for (size_t i = bar_at; i < post[p].size(); ++i) o << "    " << post[p][i] << "\n";
-        continue;
-      }
       o << "    if (rv) {\n";
       phase_loop(p,
                  track ? div_form(lane[p], narrow ? "@MUL@" : "fgt_div_q",
@@ -2150,69 +2122,6 @@ struct Emitter {
     }
     o << "}\n";
     return o.str();
-  }
-
-  // Split a phase's element statements: `first` gets the statements that
-  // update the phase's row-reduction accumulators and the definitions they
-  // need (transitively); `second` gets every other statement and the
-  // definitions it needs. A definition both need appears in both (computed
-  // twice). Original order is kept in each.
-  static void split_phase(const std::vector<std::string>& body, const std::vector<std::pair<RedText, std::string>>& accs,
-                          std::vector<std::string>* first, std::vector<std::string>* second) {
-    std::set<std::string> red_names;
-    for (auto& [t, a] : accs)
-      for (const char* sfx : {"", "_s", "_pk", "i"}) red_names.insert(a + sfx);
-    const size_t n = body.size();
-    std::vector<std::string> defs(n);
-    std::vector<std::set<std::string>> uses(n);
-    std::map<std::string, size_t> def_at;
-    for (size_t i = 0; i < n; ++i) {
-      auto T = tokens(body[i]);
-      size_t k = 0;
-      while (k < T.size() && !T[k].ident) ++k;
-      // `const <type> NAME = ...;` defines NAME
-      if (k < T.size() && T[k].s == "const") {
-        size_t j = k + 1, last = std::string::npos;
-        for (; j < T.size(); ++j) {
-          if (T[j].s == "=") break;
-          if (T[j].ident) last = j;
-        }
-        if (j < T.size() && last != std::string::npos) {
-          defs[i] = T[last].s;
-          def_at[defs[i]] = i;
-        }
-      }
-      for (auto& t : T)
-        if (t.ident && t.s != defs[i]) uses[i].insert(t.s);
-    }
-    auto closure = [&](const std::vector<size_t>& roots) {
-      std::vector<char> keep(n, 0);
-      std::vector<size_t> st = roots;
-      while (!st.empty()) {
-        const size_t i = st.back();
-        st.pop_back();
-        if (keep[i]) continue;
-        keep[i] = 1;
-        for (auto& u : uses[i]) {
-          auto it = def_at.find(u);
-          if (it != def_at.end() && it->second < i) st.push_back(it->second);
-        }
-      }
-      return keep;
-    };
-    std::vector<size_t> r1, r2;
-    for (size_t i = 0; i < n; ++i) {
-      if (!defs[i].empty()) continue;
-      bool red = false;
-      for (auto& u : uses[i]) red = red || red_names.count(u);
-      (red ? r1 : r2).push_back(i);
-    }
-    if (r1.empty() || r2.empty()) return;
-    auto k1 = closure(r1), k2 = closure(r2);
-    for (size_t i = 0; i < n; ++i) {
-      if (k1[i]) first->push_back(body[i]);
-      if (k2[i] || (!k1[i] && !defs[i].empty())) second->push_back(body[i]);
-    }
   }
 
   // Lane statements with the division placeholders resolved: @DIVQ@ becomes

@@ -1311,7 +1311,6 @@ struct Planner {
     mix(opt.tmem_cols);
     mix(opt.max3);
     mix(opt.narrow_div);
-    mix(opt.split_tail);
     mix(opt.occupancy_step);
     mix(opt.ring_kb);
     mix(opt.row_cluster);

@@ -170,7 +170,6 @@ struct Options {
   int pack_cols = 0;              // row kernels: 16-bit per-thread column operands two per register (FGT_ROW_PACK_COLS)
   int tmem_cols = 0;              // row kernels: column accumulators in tensor memory (FGT_ROW_TMEM_COLS)
   int narrow_div = 0;             // row kernels: x * RN(1/d) for divisions of 16-bit-output partitions (FGT_ROW_NARROW_DIV)
-  int split_tail = 0;             // row kernels: reduction tails overlap the phase's other work (FGT_ROW_SPLIT_TAIL)
   int max3 = 0;                   // three-input max/min for paired range notes (NVRTC >= 12.9; FGT_MAX3=0: off)
   int row_elems = 16;             // elements per thread per row operand in block-per-row kernels (FGT_ROW_ELEMS)
   int ring_kb = 96;               // shared-memory row ring budget per CTA (FGT_RING_KB)

@@ -729,13 +729,12 @@ fgt_status fgt_spec_create(const fgt_partition_desc* desc, const fgt_spec_option
       if (options->row_cluster > 0) opt.row_cluster = options->row_cluster;
       require((options->row_flags & ~(FGT_ROW_OCCUPANCY_STEP | FGT_ROW_EXPF | FGT_ROW_SMEM_COLS | FGT_ROW_XW_SHUFFLE |
                                       FGT_ROW_RING_RESIDENT | FGT_ROW_PHASE_COPIES | FGT_ROW_PACK_COLS |
-                                      FGT_ROW_TMEM_COLS | FGT_ROW_NARROW_DIV | FGT_ROW_SPLIT_TAIL)) == 0,
+                                      FGT_ROW_TMEM_COLS | FGT_ROW_NARROW_DIV)) == 0,
               "unknown row_flags bits");
       opt.phase_copies = (options->row_flags & FGT_ROW_PHASE_COPIES) != 0;
       opt.pack_cols = (options->row_flags & FGT_ROW_PACK_COLS) != 0;
       opt.tmem_cols = (options->row_flags & FGT_ROW_TMEM_COLS) != 0;
       opt.narrow_div = (options->row_flags & FGT_ROW_NARROW_DIV) != 0;
-      opt.split_tail = (options->row_flags & FGT_ROW_SPLIT_TAIL) != 0;
       opt.ring_resident = (options->row_flags & FGT_ROW_RING_RESIDENT) != 0;
       if (options->row_flags & FGT_ROW_XW_SHUFFLE) opt.xw_tree = 0;
       opt.occupancy_step = (options->row_flags & FGT_ROW_OCCUPANCY_STEP) != 0;

@@ -187,14 +187,7 @@ typedef enum fgt_row_flag {
    * outputs hides but for rounding ties), without the per-element range
    * checks of the exact form; a row whose divisor has no normal reciprocal
    * is computed with IEEE division. Other partitions are unchanged. */
-  FGT_ROW_NARROW_DIV = 256,
-  /* a phase that ends in a row reduction and also updates column
-   * accumulators (or stores elements, or caches values for later phases)
-   * runs its element loop in two parts: the reduction's statements, then the
-   * reduction's shuffles and partial stores, then the other statements, then
-   * the barrier, so the shuffles' latency overlaps independent work;
-   * statements both parts need are computed in each */
-  FGT_ROW_SPLIT_TAIL = 512
+  FGT_ROW_NARROW_DIV = 256
 } fgt_row_flag;
 
 typedef struct fgt_spec fgt_spec;   /* opaque: planned + compiled partition       */
