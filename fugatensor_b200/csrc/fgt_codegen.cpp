@@ -2013,6 +2013,26 @@ struct Emitter {
     // FULLFIN: one CTA; strided partial combine, then a block combine.
     std::vector<std::string> red_code;
     if (!col && stage != 2) group_reduce(red_code, accs, 32, true, K.nt / 32, "_fin");
+    if (!col && stage != 2) {
+      // one strided loop over the partials for all reductions (their loads in
+      // flight together), unrolled; each accumulator still sees its partials
+      // in the same order
+      const std::string head = "for (fgt_i64 q_ = tid; q_ < p.nparts; q_ += " + std::to_string(K.nt) + ") { ";
+      std::vector<std::string> decls;
+      std::string bodies;
+      bool ok = true;
+      for (const std::string& st : comb) {
+        if (st.compare(0, head.size(), head) == 0 && st.size() > head.size() + 2 && st.compare(st.size() - 2, 2, " }") == 0)
+          bodies += st.substr(head.size(), st.size() - head.size() - 2) + " ";
+        else if (st.compare(0, 4, "for ") == 0) ok = false;
+        else decls.push_back(st);
+      }
+      if (ok && !bodies.empty()) {
+        comb = decls;
+        comb.push_back("#pragma unroll 4");
+        comb.push_back(head + bodies + "}");
+      }
+    }
     std::ostringstream o;
     const std::string NT = std::to_string(K.nt);
     o << args_struct();
