@@ -1876,10 +1876,23 @@ struct Emitter {
       std::string pv = "((const " + t.part_t + "*)(" + recb + "+(fgt_i64)w_*" + stride + "LL+" + std::to_string(rec_off) + "LL))";
       std::string pi = "((const fgt_i64*)(" + recb + "+(fgt_i64)w_*" + stride + "LL+" + std::to_string(rec_off + rd.M * 8) +
                        "LL))";
-      const std::string ld0 = xchg ? "__ldcg(&" : "", ld1 = xchg ? ")" : "";
+      const std::string ld0 = "", ld1 = "";
       std::string lo = rd.combine_ranks ? "0" : (xchg ? "(int)p.xrank" : std::to_string(P.opt.rank));
       std::string hi = rd.combine_ranks ? std::to_string(P.opt.world) : (xchg ? "(int)p.xrank + 1" : std::to_string(P.opt.rank + 1));
       s << "for (int w_ = " << lo << "; w_ < " << hi << "; ++w_) { ";
+      if (xchg) {
+        // this rank's mailbox slot of rank w_: record words, each waited for
+        const std::string slot = recb + "+(fgt_i64)w_*" + stride + "LL";
+        const std::string vv = "fgt_ll_get<" + t.part_t + ">(" + slot + ", " + std::to_string(rec_off) + "LL + (fgt_i64)(" + e +
+                               ") * 8LL, xe_, t0_, p.xlimit, p.xstat)";
+        if (t.arg)
+          s << "{ const " << t.part_t << " ov = " << vv << "; const fgt_i64 oi = fgt_ll_get<fgt_i64>(" << slot << ", "
+            << (rec_off + rd.M * 8) << "LL + (fgt_i64)(" << e << ") * 8LL, xe_, t0_, p.xlimit, p.xstat); "
+            << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
+        else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << vv << "; " << comb_stmt(t, a, "ov") << " }";
+        s << " }";
+        return s.str();
+      }
       if (t.arg) s << "{ const " << t.part_t << " ov = " << ld0 << pv << "[" << e << "]" << ld1 << "; const fgt_i64 oi = " << ld0
                    << pi << "[" << e << "]" << ld1 << "; " << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
       else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << ld0 << pv << "[" << e << "]" << ld1 << "; "
@@ -1988,9 +2001,16 @@ struct Emitter {
         if (t.arg) comb2.push_back("fgt_i64 " + a + "i = " + t.identi + ";");
         comb2.push_back(fin_combine(rd, t, src_t, a, col ? "e" : "0", "p.nparts", 2, rec_off, true));
       }
-      if (stage == 1 || xchg) {
-        std::string recb = xchg ? "(xrec_+" + std::to_string(rec_off) + "LL)"
-                                : "(p.ws+" + std::to_string(K.send_offset) + "LL+" + std::to_string(rec_off) + "LL)";
+      if (xchg) {
+        // record words (value, epoch) into rank k_'s slot for this rank
+        const std::string ei = col ? "e" : "0";
+        rec_write.push_back("fgt_ll_put<" + t.part_t + ">(xrec_, " + std::to_string(rec_off) + "LL + (fgt_i64)(" + ei +
+                            ") * 8LL, (" + t.part_t + ")" + a + ", xe_);");
+        if (t.arg)
+          rec_write.push_back("fgt_ll_put<fgt_i64>(xrec_, " + std::to_string(rec_off + rd.M * 8) + "LL + (fgt_i64)(" + ei +
+                              ") * 8LL, " + a + "i, xe_);");
+      } else if (stage == 1) {
+        std::string recb = "(p.ws+" + std::to_string(K.send_offset) + "LL+" + std::to_string(rec_off) + "LL)";
         rec_write.push_back("((" + t.part_t + "*)" + recb + ")[" + (col ? "e" : "0") + "] = (" + t.part_t + ")" + a + ";");
         if (t.arg)
           rec_write.push_back("((fgt_i64*)(" + recb + "+" + std::to_string(rd.M * 8) + "LL))[" + (col ? "e" : "0") + "] = " + a + "i;");
@@ -2041,48 +2061,30 @@ struct Emitter {
     put(o, kdecl, "  ");
     if (xchg) {
       // Exchange of this CTA's record through the peer mailboxes: the record is
-      // stored into every rank's data[epoch % 2][this rank] (NVLink stores for
-      // peers), each writer fences at system scope, then one thread raises
-      // flag[this rank][CTA] = epoch on every rank and waits, bounded by
-      // p.xlimit ns, until every rank's flag here has reached the epoch
-      // (a timeout marks the communicator's status word and goes on).
-      const std::string W = std::to_string(P.opt.world), MW = std::to_string(kXMaxWorld), MC = std::to_string(kXMaxCtas);
+      // stored as (value, epoch) words into every rank's data[epoch % 2][this
+      // rank] (NVLink stores for peers); each rank then reads the words of all
+      // ranks from its own mailbox, waiting for each to carry this launch's
+      // epoch, bounded by p.xlimit ns from the start of the reads (a timeout
+      // marks the communicator's status word and goes on). No fence or flag is
+      // needed: a word's epoch and value arrive in one 64-bit store. A rank
+      // writes a slot again only two launches later, after every rank has
+      // finished the launch that read it (each launch reads every column of
+      // every rank before it ends).
+      const std::string W = std::to_string(P.opt.world), MW = std::to_string(kXMaxWorld);
       const std::string slot = "p.xmb[k_]+" + std::to_string(kXDataOff) + "LL+((fgt_i64)(xe_ & 1u)*" + MW +
                                "+p.xrank)*" + std::to_string(kXSlot) + "LL";
-      auto push = [&](const std::string& ind) {
-        o << ind << "for (int k_ = 0; k_ < " << W << "; ++k_) {\n";
-        o << ind << "  unsigned char* const xrec_ = " << slot << ";\n";
-        put(o, rec_write, ind + "  ");
-        o << ind << "}\n";
-      };
-      auto flags_and_wait = [&]() {
-        o << "  if (tid == 0) {\n";
-        o << "    for (int k_ = 0; k_ < " << W << "; ++k_)\n";
-        o << "      fgt_st_release_sys((unsigned*)(p.xmb[k_]+" << kXFlagOff << "LL) + p.xrank * " << MC << " + blockIdx.x, xe_);\n";
-        o << "    const unsigned long long t0_ = fgt_globaltimer();\n";
-        o << "    for (int k_ = 0; k_ < " << W << "; ++k_)\n";
-        o << "      if (!fgt_xwait((const unsigned*)(p.xmb[p.xrank]+" << kXFlagOff << "LL) + k_ * " << MC
-          << " + blockIdx.x, xe_, t0_, p.xlimit)) { fgt_xfail(p.xstat); break; }\n";
-        o << "    ((unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] = xe_;\n";
-        o << "  }\n";
-        o << "  __syncthreads();\n  __threadfence_system();\n";
-      };
       o << "  __shared__ unsigned xep_;\n";
       o << "  if (tid == 0) xep_ = ((const unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] + 1u;\n";
       o << "  __syncthreads();\n  const unsigned xe_ = xep_;\n";
+      o << "  if (tid == 0) ((unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] = xe_;\n";
       if (col) {
         std::vector<std::string> tail{"for (int k_ = 0; k_ < " + W + "; ++k_) {", "  unsigned char* const xrec_ = " + slot + ";"};
         for (auto& w : rec_write) tail.push_back("  " + w);
         tail.push_back("}");
         col_partial_loop(o, comb, accs, tail);
-        o << "  __threadfence_system();\n  __syncthreads();\n";
-        flags_and_wait();
-        // The flags pair this CTA with the same CTA of every rank, so the
-        // combine reads only the column blocks this CTA index wrote above
-        // (blocks blockIdx.x + k * gridDim.x of 32 columns), one per warp.
-        o << "  for (fgt_i64 cb_ = blockIdx.x + (fgt_i64)(tid >> 5) * gridDim.x; cb_ * 32 < NI; cb_ += (fgt_i64)gridDim.x * "
-          << K.nt / 32 << ") {\n";
-        o << "    const fgt_i64 e = cb_ * 32 + (tid & 31);\n    if (e >= NI) continue;\n";
+        // every column of every rank, one column per thread
+        o << "  const unsigned long long t0_ = fgt_globaltimer();\n";
+        o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
         o << "    " << digits_i() << "\n";
         put(o, comb2, "    ");
         put(o, finals, "    ");
@@ -2093,11 +2095,12 @@ struct Emitter {
       o << "  const fgt_i64 e = 0; (void)e;\n";
       put(o, comb, "  ");
       put(o, red_code, "  ");
-      o << "  if (tid == 0) {\n";
-      push("    ");
-      o << "    __threadfence_system();\n  }\n";
-      flags_and_wait();
-      o << "  if (tid != 0) return;\n  {\n";
+      o << "  if (tid != 0) return;\n";
+      o << "  for (int k_ = 0; k_ < " << W << "; ++k_) {\n";
+      o << "    unsigned char* const xrec_ = " << slot << ";\n";
+      put(o, rec_write, "    ");
+      o << "  }\n";
+      o << "  const unsigned long long t0_ = fgt_globaltimer();\n  {\n";
       put(o, comb2, "    ");
       put(o, finals, "    ");
       put(o, lane[0], "    ");

@@ -228,32 +228,72 @@ FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // lower index in the low half)
 template <int N> FGT_DEV fgt_u16 fgt_h16(const fgt_u32 (&w)[N], int v) { return (fgt_u16)(w[v >> 1] >> ((v & 1) * 16)); }
 // ---- peer mailboxes (records exchanged between ranks over NVLink) --------
-FGT_DEV unsigned fgt_ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-FGT_DEV void fgt_st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
-}
 FGT_DEV unsigned long long fgt_globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
   return t;
 }
-// Wait until *flag has reached epoch `ep` (wrapping compare); false when
-// `limit_ns` passed since t0 first (the caller records the failure and goes on).
-FGT_DEV bool fgt_xwait(const unsigned* flag, unsigned ep, unsigned long long t0, unsigned long long limit_ns) {
-  while ((int)(fgt_ld_acquire_sys(flag) - ep) < 0) {
-    if (fgt_globaltimer() - t0 > limit_ns) return false;
-    __nanosleep(64);
-  }
-  return true;
-}
 // A failed exchange: the host-mapped status word of the communicator.
 FGT_DEV void fgt_xfail(unsigned* status) {
   *(volatile unsigned*)status = 1u;
   __threadfence_system();
+}
+
+// ---- record words of the peer exchange -------------------------------------
+// A rank's record travels as 8-byte words, each holding 4 bytes of data in its
+// low half and the launch's epoch in its high half, written and read with
+// single 64-bit accesses (naturally aligned 64-bit scalar accesses are
+// single-copy atomic). A reader that sees the epoch in a word therefore sees
+// that word's data: no fence and no separate flag are needed, as in NCCL's
+// low-latency protocol. Every record value owns 8 record bytes at an 8-byte
+// offset b, carried by the two words at bytes 2b and 2b + 8 of the slot
+// (narrower values use the first word only, zero-extended).
+FGT_DEV void fgt_ll_store(unsigned char* slot, fgt_i64 byte_off, fgt_u32 v, unsigned ep) {
+  const fgt_u64 w = ((fgt_u64)ep << 32) | v;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(slot + 2 * byte_off), "l"(w) : "memory");
+}
+// Waits, until t0 + limit ns, for the word to carry epoch `ep`; on timeout the
+// status word is set and whatever the word holds is returned.
+FGT_DEV fgt_u32 fgt_ll_load(const unsigned char* slot, fgt_i64 byte_off, unsigned ep, unsigned long long t0,
+                            unsigned long long limit, unsigned* status) {
+  fgt_u64 w;
+  for (;;) {
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(w) : "l"(slot + 2 * byte_off) : "memory");
+    if ((unsigned)(w >> 32) == ep) break;
+    if (fgt_globaltimer() - t0 > limit) {
+      fgt_xfail(status);
+      break;
+    }
+    __nanosleep(32);
+  }
+  return (fgt_u32)w;
+}
+// Bit images of the record value types (8 bytes wide, narrower ones zero-extended).
+FGT_DEV fgt_u64 fgt_bits64(float v) { return __float_as_uint(v); }
+FGT_DEV fgt_u64 fgt_bits64(double v) { return (fgt_u64)__double_as_longlong(v); }
+FGT_DEV fgt_u64 fgt_bits64(fgt_i64 v) { return (fgt_u64)v; }
+FGT_DEV fgt_u64 fgt_bits64(fgt_u64 v) { return v; }
+FGT_DEV fgt_u64 fgt_bits64(int v) { return (fgt_u32)v; }
+FGT_DEV fgt_u64 fgt_bits64(fgt_u32 v) { return v; }
+FGT_DEV fgt_u64 fgt_bits64(fgt_u16 v) { return v; }
+FGT_DEV fgt_u64 fgt_bits64(fgt_u8 v) { return v; }
+FGT_DEV fgt_u64 fgt_bits64(bool v) { return v ? 1u : 0u; }
+template <typename T> FGT_DEV void fgt_from_bits64(fgt_u64 b, T& out) { out = (T)b; }
+FGT_DEV void fgt_from_bits64(fgt_u64 b, float& out) { out = __uint_as_float((fgt_u32)b); }
+FGT_DEV void fgt_from_bits64(fgt_u64 b, double& out) { out = __longlong_as_double((long long)b); }
+template <typename T> FGT_DEV void fgt_ll_put(unsigned char* slot, fgt_i64 byte_off, T v, unsigned ep) {
+  const fgt_u64 b = fgt_bits64(v);
+  fgt_ll_store(slot, byte_off, (fgt_u32)b, ep);
+  if (sizeof(T) == 8) fgt_ll_store(slot, byte_off + 4, (fgt_u32)(b >> 32), ep);
+}
+template <typename T>
+FGT_DEV T fgt_ll_get(const unsigned char* slot, fgt_i64 byte_off, unsigned ep, unsigned long long t0, unsigned long long limit,
+                     unsigned* status) {
+  fgt_u64 b = fgt_ll_load(slot, byte_off, ep, t0, limit, status);
+  if (sizeof(T) == 8) b |= (fgt_u64)fgt_ll_load(slot, byte_off + 4, ep, t0, limit, status) << 32;
+  T r;
+  fgt_from_bits64(b, r);
+  return r;
 }
 
 // Element v of a packed 16-bit array (v a compile-time constant after unrolling).

@@ -1225,8 +1225,9 @@ struct Planner {
       plan.collectives.push_back((int)plan.kernels.size() - 1);
       plan.kernels.push_back(f2);
       // the same two stages in one kernel, the records exchanged through the
-      // ranks' peer mailboxes (launched instead when the communicator has them)
-      if (rec <= kXSlot && opt.world <= kXMaxWorld) {
+      // ranks' peer mailboxes (launched instead when the communicator has them);
+      // each 8-byte record value travels as two (value, epoch) words
+      if (2 * rec <= kXSlot && opt.world <= kXMaxWorld) {
         KernelDef f3 = f;
         f3.fin_stage = 3;
         f3.record_bytes = rec;

@@ -71,18 +71,17 @@ enum class KKind { ELEM, ROW, COLFIN, FULLFIN };
 
 // Peer mailbox of one communicator rank: device memory the other ranks'
 // processes map through CUDA IPC, zeroed when the communicator is created.
-//   epoch[c]        (this rank's own) launches completed by CTA index c of
+//   epoch[c]        (this rank's own) launches started by CTA index c of
 //                   the exchanging FIN kernels
-//   flag[src][c]    the last epoch whose record rank src delivered here for
-//                   CTA index c
-//   data[par][src]  records rank src delivered here; par = epoch % 2, so a
-//                   rank one launch ahead never overwrites records still read
-// A record of one rank for one launch holds at most kXSlot bytes.
+//   data[par][src]  record words rank src delivered here, each (value,
+//                   epoch); par = epoch % 2, so a rank one launch ahead never
+//                   overwrites words still read
+// A record of one rank for one launch holds at most kXSlot / 2 bytes (its
+// words take twice its bytes).
 constexpr int kXMaxWorld = 8;
 constexpr int kXMaxCtas = 256;
 constexpr int64_t kXSlot = 1 << 20;
 constexpr int64_t kXEpochOff = 0;
-constexpr int64_t kXFlagOff = 4096;
 constexpr int64_t kXDataOff = 65536;
 constexpr int64_t kXBytes = kXDataOff + 2 * kXMaxWorld * kXSlot;
 enum RedRole { ROLE_ROW = 0, ROLE_COL = 1, ROLE_FULL = 2 };
