@@ -2073,10 +2073,19 @@ struct Emitter {
       const std::string W = std::to_string(P.opt.world), MW = std::to_string(kXMaxWorld);
       const std::string slot = "p.xmb[k_]+" + std::to_string(kXDataOff) + "LL+((fgt_i64)(xe_ & 1u)*" + MW +
                                "+p.xrank)*" + std::to_string(kXSlot) + "LL";
+      // One epoch per launch, the same in every CTA (a word written by one CTA
+      // index is read by others): every CTA reads the communicator's epoch
+      // word, and the last CTA to have read it (counted in the word after it)
+      // advances it for the next launch.
+      const std::string EP = "((volatile unsigned*)(p.xmb[p.xrank]+" + std::to_string(kXEpochOff) + "LL))";
       o << "  __shared__ unsigned xep_;\n";
-      o << "  if (tid == 0) xep_ = ((const unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] + 1u;\n";
+      o << "  if (tid == 0) {\n";
+      o << "    xep_ = " << EP << "[0] + 1u;\n";
+      o << "    __threadfence();\n";
+      o << "    if (atomicAdd((unsigned*)" << EP << " + 1, 1u) == gridDim.x - 1) { " << EP << "[1] = 0u; " << EP
+        << "[0] = xep_; }\n";
+      o << "  }\n";
       o << "  __syncthreads();\n  const unsigned xe_ = xep_;\n";
-      o << "  if (tid == 0) ((unsigned*)(p.xmb[p.xrank]+" << kXEpochOff << "LL))[blockIdx.x] = xe_;\n";
       if (col) {
         std::vector<std::string> tail{"for (int k_ = 0; k_ < " + W + "; ++k_) {", "  unsigned char* const xrec_ = " + slot + ";"};
         for (auto& w : rec_write) tail.push_back("  " + w);

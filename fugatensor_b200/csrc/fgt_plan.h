@@ -71,8 +71,9 @@ enum class KKind { ELEM, ROW, COLFIN, FULLFIN };
 
 // Peer mailbox of one communicator rank: device memory the other ranks'
 // processes map through CUDA IPC, zeroed when the communicator is created.
-//   epoch[c]        (this rank's own) launches started by CTA index c of
-//                   the exchanging FIN kernels
+//   epoch           (this rank's own) launches of the exchanging FIN kernels,
+//                   with the count of CTAs of the current launch that have
+//                   read it in the next word
 //   data[par][src]  record words rank src delivered here, each (value,
 //                   epoch); par = epoch % 2, so a rank one launch ahead never
 //                   overwrites words still read
