@@ -318,8 +318,10 @@ def run_fgt(args):
             barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
+            h0 = time.perf_counter()
             for _ in range(args.table_iters):
                 sharded.run_sharded(spec, group, *ins, outputs=outs, workspace=ws)
+            host_ms = (time.perf_counter() - h0) * 1e3 / args.table_iters  # launch calls only (no sync)
             b.record(stream)
             torch.cuda.synchronize()
             ms = a.elapsed_time(b) / args.table_iters
@@ -338,15 +340,15 @@ def run_fgt(args):
             b.record(stream)
             torch.cuda.synchronize()
             ms_l = a.elapsed_time(b) / args.table_iters
-            t = torch.tensor([ms, ms_l], device=device)
+            t = torch.tensor([ms, ms_l, host_ms], device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms, ms_l = float(t[0].item()), float(t[1].item())
+            ms, ms_l, host_ms = float(t[0].item()), float(t[1].item()), float(t[2].item())
             del outs_l, ws_l
             nb = W.algorithmic_bytes(c, v, r, h, dt)
             entry = {"n_gpus": world, "global_shape": [r, h], "ms": round(ms, 5), "GB/s": round(nb / ms / 1e6, 1),
                      "per_gpu_frac": round(nb / ms / 1e6 / world / peak_, 4), "kernels": spec.kernel_count,
                      "collectives": spec.collective_count, "geometry": geom[0],
-                     "local_ms": round(ms_l, 5)}
+                     "local_ms": round(ms_l, 5), "host_launch_ms": round(host_ms, 5)}
             partitions[f"{c}/{v}/{dt}/sharded{world}"] = dict(entry, scaling="strong")
             strong[f"{c}/{v}/{dt}"] = entry
             del tt, ins, outs, ws
