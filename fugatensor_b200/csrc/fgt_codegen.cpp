@@ -375,6 +375,7 @@ struct Emitter {
   std::map<int, std::set<std::string>> div_rcps;  // the reciprocals those divisions use, per phase
   std::set<int> exp_phases;                 // phases with element exps by fgt_exp_q (range noted)
   std::set<int> col_phases;                 // phases updating column accumulators (not redoable)
+  std::vector<std::string> llpre;           // peer-exchange FIN: record words requested before they are combined
   std::set<int> tm_phases;                  // phases updating column accumulators held in TMEM
   int64_t tm_alloc = 0;                     // TMEM columns allocated per CTA (0: none)
   std::map<int, std::vector<std::string>> resets;  // row accumulators of a phase back to identity
@@ -1881,13 +1882,28 @@ struct Emitter {
       std::string hi = rd.combine_ranks ? std::to_string(P.opt.world) : (xchg ? "(int)p.xrank + 1" : std::to_string(P.opt.rank + 1));
       s << "for (int w_ = " << lo << "; w_ < " << hi << "; ++w_) { ";
       if (xchg) {
-        // this rank's mailbox slot of rank w_: record words, each waited for
+        // this rank's mailbox slot of rank w_: the record words are requested
+        // for every rank first (llpre, emitted before the combines), then each
+        // is taken, or waited for when it does not carry this launch's epoch yet
         const std::string slot = recb + "+(fgt_i64)w_*" + stride + "LL";
-        const std::string vv = "fgt_ll_get<" + t.part_t + ">(" + slot + ", " + std::to_string(rec_off) + "LL + (fgt_i64)(" + e +
-                               ") * 8LL, xe_, t0_, p.xlimit, p.xstat)";
+        const std::string W = std::to_string(P.opt.world);
+        const std::string off = std::to_string(rec_off) + "LL + (fgt_i64)(" + e + ") * 8LL";
+        const std::string offi = std::to_string(rec_off + rd.M * 8) + "LL + (fgt_i64)(" + e + ") * 8LL";
+        const std::string lw = "llw_" + a;
+        const bool wide = t.part_t == "double" || t.part_t == "fgt_i64" || t.part_t == "fgt_u64";
+        std::string pre = "fgt_u64 " + lw + "[" + W + "][4]; " + "\n#pragma unroll\nfor (int w_ = " + lo + "; w_ < " + hi +
+                          "; ++w_) { " + lw + "[w_ - (" + lo + ")][0] = fgt_ll_raw(" + slot + ", " + off + "); " + lw +
+                          "[w_ - (" + lo + ")][1] = " + (wide ? "fgt_ll_raw(" + slot + ", " + off + " + 4)" : std::string("0")) + ";";
         if (t.arg)
-          s << "{ const " << t.part_t << " ov = " << vv << "; const fgt_i64 oi = fgt_ll_get<fgt_i64>(" << slot << ", "
-            << (rec_off + rd.M * 8) << "LL + (fgt_i64)(" << e << ") * 8LL, xe_, t0_, p.xlimit, p.xstat); "
+          pre += " " + lw + "[w_ - (" + lo + ")][2] = fgt_ll_raw(" + slot + ", " + offi + "); " + lw + "[w_ - (" + lo +
+                 ")][3] = fgt_ll_raw(" + slot + ", " + offi + " + 4);";
+        pre += " }";
+        llpre.push_back(pre);
+        const std::string vv = "fgt_ll_value<" + t.part_t + ">(" + lw + "[w_ - (" + lo + ")][0], " + lw + "[w_ - (" + lo +
+                               ")][1], " + slot + ", " + off + ", xe_, t0_, p.xlimit, p.xstat)";
+        if (t.arg)
+          s << "{ const " << t.part_t << " ov = " << vv << "; const fgt_i64 oi = fgt_ll_value<fgt_i64>(" << lw << "[w_ - (" << lo
+            << ")][2], " << lw << "[w_ - (" << lo << ")][3], " << slot << ", " << offi << ", xe_, t0_, p.xlimit, p.xstat); "
             << arg_stmt(t, a, a + "i", "ov", "oi") << " }";
         else s << "{ const " << t.fin_t << " ov = (" << t.fin_t << ")" << vv << "; " << comb_stmt(t, a, "ov") << " }";
         s << " }";
@@ -2095,6 +2111,7 @@ struct Emitter {
         o << "  const unsigned long long t0_ = fgt_globaltimer();\n";
         o << "  for (fgt_i64 e = (fgt_i64)blockIdx.x * " << NT << " + tid; e < NI; e += (fgt_i64)gridDim.x * " << NT << ") {\n";
         o << "    " << digits_i() << "\n";
+        put(o, llpre, "    ");
         put(o, comb2, "    ");
         put(o, finals, "    ");
         put(o, lane[0], "    ");
@@ -2110,6 +2127,7 @@ struct Emitter {
       put(o, rec_write, "    ");
       o << "  }\n";
       o << "  const unsigned long long t0_ = fgt_globaltimer();\n  {\n";
+      put(o, llpre, "    ");
       put(o, comb2, "    ");
       put(o, finals, "    ");
       put(o, lane[0], "    ");

@@ -268,6 +268,19 @@ FGT_DEV fgt_u32 fgt_ll_load(const unsigned char* slot, fgt_i64 byte_off, unsigne
   }
   return (fgt_u32)w;
 }
+// A word read without waiting (all of a record's words are requested before
+// any is checked, so their latencies overlap), and its value once it carries
+// `ep`: taken as read, or waited for as fgt_ll_load does.
+FGT_DEV fgt_u64 fgt_ll_raw(const unsigned char* slot, fgt_i64 byte_off) {
+  fgt_u64 w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(w) : "l"(slot + 2 * byte_off) : "memory");
+  return w;
+}
+FGT_DEV fgt_u32 fgt_ll_take(fgt_u64 w, const unsigned char* slot, fgt_i64 byte_off, unsigned ep, unsigned long long t0,
+                            unsigned long long limit, unsigned* status) {
+  if ((unsigned)(w >> 32) == ep) return (fgt_u32)w;
+  return fgt_ll_load(slot, byte_off, ep, t0, limit, status);
+}
 // Bit images of the record value types (8 bytes wide, narrower ones zero-extended).
 FGT_DEV fgt_u64 fgt_bits64(float v) { return __float_as_uint(v); }
 FGT_DEV fgt_u64 fgt_bits64(double v) { return (fgt_u64)__double_as_longlong(v); }
@@ -285,6 +298,15 @@ template <typename T> FGT_DEV void fgt_ll_put(unsigned char* slot, fgt_i64 byte_
   const fgt_u64 b = fgt_bits64(v);
   fgt_ll_store(slot, byte_off, (fgt_u32)b, ep);
   if (sizeof(T) == 8) fgt_ll_store(slot, byte_off + 4, (fgt_u32)(b >> 32), ep);
+}
+template <typename T>
+FGT_DEV T fgt_ll_value(fgt_u64 w0, fgt_u64 w1, const unsigned char* slot, fgt_i64 byte_off, unsigned ep, unsigned long long t0,
+                       unsigned long long limit, unsigned* status) {
+  fgt_u64 b = fgt_ll_take(w0, slot, byte_off, ep, t0, limit, status);
+  if (sizeof(T) == 8) b |= (fgt_u64)fgt_ll_take(w1, slot, byte_off + 4, ep, t0, limit, status) << 32;
+  T r;
+  fgt_from_bits64(b, r);
+  return r;
 }
 template <typename T>
 FGT_DEV T fgt_ll_get(const unsigned char* slot, fgt_i64 byte_off, unsigned ep, unsigned long long t0, unsigned long long limit,
