@@ -53,11 +53,13 @@ def test_gather_rows_and_columns(rows, cols):
     _check(outs, {id(X): x, id(RI): ri, id(CI): ci})
 
 
-@pytest.mark.parametrize("rows,cols,n", [(512, 96, 4000), (1021, 33, 3000), (70001, 8, 50000)])
+@pytest.mark.parametrize("rows,cols,n", [(512, 96, 4000), (1021, 33, 3000), (70001, 8, 50000), (65536, 64, 131072)])
 @pytest.mark.parametrize("dtype", ["f32", "bf16", "i32", "i64"])
 def test_scatter_add_random(dtype, rows, cols, n):
     """Row scatter_add (the bucket-list form) against the oracle: duplicate and
-    out-of-range indices, odd row counts, and more rows than one scan step."""
+    out-of-range indices, odd row counts, more rows than one scan step, and
+    more vector chunks than the grid has threads (each thread walks several
+    rows' lists in its grid-stride loop, with the next list head read ahead)."""
     rng = np.random.default_rng(11 + rows)
     idx = rng.integers(-5, rows + 5, n).astype(np.int32)
     if dtype in ("i32", "i64"):
