@@ -3,8 +3,9 @@
 The failure is made on the host, never by faulting or hanging a GPU: rank 0
 of a two-rank communicator calls fgt_comm_create and rank 1 never does. The
 communicator is non-blocking with a deadline (FGT_COMM_TIMEOUT_MS), so rank 0
-must get FGT_ERR_NCCL within about the deadline. The attempt runs in a child process on one GPU, under its own
-timeout, with NVLS off; no kernel is launched and nothing waits on the GPU.
+must get FGT_ERR_NCCL within about the deadline. The attempt runs in a child
+process on one GPU, under its own timeout, with NVLS off; no kernel is launched
+and nothing waits on the GPU.
 """
 import os
 import subprocess
