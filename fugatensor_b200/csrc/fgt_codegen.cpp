@@ -1446,11 +1446,11 @@ struct Emitter {
     if (K.cluster > 1) {
       // one row over a cluster: the row's thread index spans the cluster's CTAs
       o << "extern \"C\" __global__ void __cluster_dims__(" << K.cluster << ", 1, 1) __launch_bounds__(" << NT << ") " << K.name
-        << "(const FgtArgs p) {\n";
+        << "(const FgtArgs p) {\n  fgt_pdl_enter();\n";
       o << "  const int tid = threadIdx.x; const unsigned crank = fgt_cluster_rank(); const int lane = (int)crank * " << NT
         << " + tid; const int grp = 0;\n";
     } else {
-      o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
+      o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n  fgt_pdl_enter();\n";
       o << "  const int tid = threadIdx.x; const int lane = tid % " << TPR << "; const int grp = tid / " << TPR << ";\n";
     }
     o << "  (void)lane; (void)grp;\n";
@@ -1824,7 +1824,7 @@ struct Emitter {
     // the row-scatter bucket sums wait on dependent loads (list head, next link,
     // update row): more resident warps hide more of that latency
     const std::string LB = K.scatter_csr && K.scatter_stage == 3 ? NT + ", 8" : NT;
-    o << "extern \"C\" __global__ void __launch_bounds__(" << LB << ") " << K.name << "(const FgtArgs p) {\n";
+    o << "extern \"C\" __global__ void __launch_bounds__(" << LB << ") " << K.name << "(const FgtArgs p) {\n  fgt_pdl_enter();\n";
     o << "  const int tid = threadIdx.x; const fgt_i64 r = 0; const bool rv = true; (void)r; (void)rv;\n";
     o << "  const fgt_i64 NI = " << d.NI << "LL; const fgt_i64 NCK = NI / " << VEC << ";\n";
     put(o, kdecl, "  ");
@@ -2072,7 +2072,7 @@ struct Emitter {
     std::ostringstream o;
     const std::string NT = std::to_string(K.nt);
     o << args_struct();
-    o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n";
+    o << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << K.name << "(const FgtArgs p) {\n  fgt_pdl_enter();\n";
     o << "  const int tid = threadIdx.x; const fgt_i64 r = 0; const bool rv = true; (void)r; (void)rv;\n";
     put(o, kdecl, "  ");
     if (xchg) {

@@ -227,6 +227,17 @@ FGT_DEV float fgt_div_ieee(float x, float d, float) { return __fdiv_rn(x, d); }
 // 16-bit element v of a packed row piece (two values per 32-bit word, the
 // lower index in the low half)
 template <int N> FGT_DEV fgt_u16 fgt_h16(const fgt_u32 (&w)[N], int v) { return (fgt_u16)(w[v >> 1] >> ((v & 1) * 16)); }
+// ---- programmatic dependent launch ----------------------------------------
+// Every kernel starts here. The next kernel on the stream, when it is launched
+// with programmatic stream serialization, may be scheduled once every CTA of
+// this grid has started (its CTAs wait in whatever room this grid leaves on
+// the SMs), and this grid waits until the grid before it has completed with its memory
+// visible before it reads anything. Without that launch attribute both
+// instructions do nothing.
+FGT_DEV void fgt_pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 // ---- peer mailboxes (records exchanged between ranks over NVLink) --------
 FGT_DEV unsigned long long fgt_globaltimer() {
   unsigned long long t;

@@ -34,6 +34,9 @@ struct Driver {
                            void**, void**) = nullptr;
   // optional (CUDA 12.0+ drivers): a context's process-unique id
   CUresult (*CtxGetId)(CUcontext, unsigned long long*) = nullptr;
+  // optional (CUDA 12.0+ drivers): launches with attributes (programmatic
+  // dependent launch of a plan's kernels)
+  CUresult (*LaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**) = nullptr;
   // optional: CUDA graphs of prepared programs (kernel-node parameters v2)
   bool graphs = false;
   CUresult (*GraphCreate)(CUgraph*, unsigned int) = nullptr;
@@ -93,6 +96,7 @@ inline Driver& drv() {
     d.ok = all;
     if (!all) d.err = "libcuda.so.1 lacks a required driver entry point";
     d.CtxGetId = reinterpret_cast<decltype(d.CtxGetId)>(dlsym(h, "cuCtxGetId"));
+    d.LaunchKernelEx = reinterpret_cast<decltype(d.LaunchKernelEx)>(dlsym(h, "cuLaunchKernelEx"));
     auto opt = [&](auto& fn, const char* name) {
       fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
       return fn != nullptr;

@@ -626,6 +626,15 @@ void validate_buffers(const Plan& p, const void* const* inputs, void* const* out
   }
 }
 
+// FGT_PDL=0: every kernel launched with plain stream order
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("FGT_PDL");
+    return !(e && std::atoi(e) == 0);
+  }();
+  return on;
+}
+
 void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* const* outputs, void* ws, size_t ws_bytes,
                 void* stream) {
   const Plan& p = s->plan;
@@ -647,14 +656,45 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
   }
   LoadedModule& lm = module_for(s);
   CUstream st = (CUstream)stream;
+  // Kernels are launched with programmatic stream serialization: each may be
+  // scheduled while the kernel before it on the stream drains, and every
+  // generated kernel waits for that predecessor to complete, with its memory
+  // visible (griddepcontrol.wait), before it reads anything, whichever kernel
+  // the predecessor is. The kernel after an NCCL collective, and every kernel
+  // while the stream is being captured into a graph, get a plain launch.
+  bool pdl = pdl_enabled() && drv().LaunchKernelEx != nullptr;
+  if (pdl && drv().StreamIsCapturing) {
+    CUstreamCaptureStatus cs = CU_STREAM_CAPTURE_STATUS_NONE;
+    pdl = drv().StreamIsCapturing(st, &cs) == CUDA_SUCCESS && cs == CU_STREAM_CAPTURE_STATUS_NONE;
+  }
+  bool after_collective = false;
   for (const Step& sp : plan_steps(p, lm, xpath ? 2 : 1)) {
     const size_t i = sp.idx;
     const KernelDef& k = p.kernels[i];
     ArgBlock a = make_args(p, inputs, outputs, ws, sp.nparts, k.fin_stage == 3 ? comm : nullptr);
     void* params[] = {a.bytes.data()};
-    cu_check(drv().LaunchKernel(lm.fn[i], sp.grid, sp.gy, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
-                                nullptr),
-             "cuLaunchKernel");
+    if (pdl && !after_collective) {
+      CUlaunchAttribute at[1] = {};
+      at[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+      at[0].value.programmaticStreamSerializationAllowed = 1;
+      CUlaunchConfig cfg = {};
+      cfg.gridDimX = sp.grid;
+      cfg.gridDimY = sp.gy;
+      cfg.gridDimZ = 1;
+      cfg.blockDimX = (unsigned)k.nt;
+      cfg.blockDimY = 1;
+      cfg.blockDimZ = 1;
+      cfg.sharedMemBytes = (unsigned)k.smem_bytes;
+      cfg.hStream = st;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      cu_check(drv().LaunchKernelEx(&cfg, lm.fn[i], params, nullptr), "cuLaunchKernelEx");
+    } else {
+      cu_check(drv().LaunchKernel(lm.fn[i], sp.grid, sp.gy, 1, (unsigned)k.nt, 1, 1, (unsigned)k.smem_bytes, st, params,
+                                  nullptr),
+               "cuLaunchKernel");
+    }
+    after_collective = false;
     for (int c : p.collectives) {
       if (c != (int)i || xpath) continue;
       unsigned char* base = (unsigned char*)ws;
@@ -662,6 +702,7 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
                                   comm->comm, stream),
                  "ncclAllGather");
       nccl_wait(comm->comm, "ncclAllGather");
+      after_collective = true;
     }
   }
 }

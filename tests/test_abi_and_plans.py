@@ -258,6 +258,26 @@ def test_row_scatter_plans_as_bucket_lists():
     assert s.kernel_count == 3
 
 
+def test_every_kernel_waits_for_its_predecessor_first():
+    """Kernels are launched with programmatic stream serialization, so each may
+    be scheduled before the kernel ahead of it on the stream has finished: the
+    first statement of every generated kernel (row, element, whole-tensor and
+    column finaliser kinds) lets its own dependents be scheduled and waits for its predecessor
+    (griddepcontrol) before anything is read."""
+    from fugatensor_b200 import _fgt
+    g = ir.Graph()
+    b, i, u = g.parameter("f32", (1000, 64)), g.parameter("i32", (300,)), g.parameter("f32", (300, 64))
+    x = g.parameter("f32", (64, 512))
+    specs = [_fgt.Spec(g.descriptor([g.scatter_add(b, i, u, 0)])),
+             _fgt.Spec(g.descriptor([g.reduce_sum(g.exp(x), (1,)), g.reduce_sum(x, (0, 1))])),
+             _fgt.Spec(g.descriptor([g.reduce_sum(g.exp(x), (1,)), g.reduce_sum(x, (0,))]))]
+    for s in specs:
+        for k in range(s.kernel_count):
+            src = s.kernel_source(k)
+            body = src[src.index("(const FgtArgs p) {") + len("(const FgtArgs p) {"):].lstrip()
+            assert body.startswith("fgt_pdl_enter();"), src[:400]
+
+
 def test_vector_width_ignores_per_row_and_guarded_loads():
     """The vector width follows the loads that can be vector loads: a row gather
     of f32 rows with i64 indices (one index per row, guarded element reads)
