@@ -660,9 +660,11 @@ void launch_all(fgt_spec* s, fgt_comm* comm, const void* const* inputs, void* co
   // scheduled while the kernel before it on the stream drains, and every
   // generated kernel waits for that predecessor to complete, with its memory
   // visible (griddepcontrol.wait), before it reads anything, whichever kernel
-  // the predecessor is. The kernel after an NCCL collective, and every kernel
-  // while the stream is being captured into a graph, get a plain launch.
-  bool pdl = pdl_enabled() && drv().LaunchKernelEx != nullptr;
+  // the predecessor is. Plain launches remain for the kernel after an NCCL
+  // collective, for every kernel while the stream is being captured into a
+  // graph, and for sharded launches (the cross-rank exchange keeps the stream
+  // order its multi-GPU runs were measured with).
+  bool pdl = pdl_enabled() && drv().LaunchKernelEx != nullptr && comm == nullptr;
   if (pdl && drv().StreamIsCapturing) {
     CUstreamCaptureStatus cs = CU_STREAM_CAPTURE_STATUS_NONE;
     pdl = drv().StreamIsCapturing(st, &cs) == CUDA_SUCCESS && cs == CU_STREAM_CAPTURE_STATUS_NONE;
